@@ -1,0 +1,252 @@
+/*
+ * fastdecode_b200.h -- C ABI of the B200 paged decode-attention engine.
+ *
+ * Every entry point takes plain pointers, sizes and strides (no torch types),
+ * is asynchronous on the caller's CUDA stream (passed as `void *stream`,
+ * i.e. a cudaStream_t; NULL means the legacy default stream) and returns an
+ * fd_status code.  The caller owns and allocates every buffer: outputs, the
+ * KV tiers and the scratch workspace.  The library never allocates device
+ * memory on its own.
+ *
+ * Block numbering (the G+C convention of the reference plugin,
+ * fastdecode/patches.py:1-7 and fastdecode/plan.py:3-4):
+ *   block id b <  tier_split  ->  tier[0], block b       (HBM tier)
+ *   block id b >= tier_split  ->  tier[1], block b - G   (host tier)
+ * A tier whose memory is pinned host memory mapped into the device address
+ * space (cudaHostAlloc / cudaHostRegister, flag Mapped) is marked
+ * host_mapped = 1 and is read over PCIe with 16-byte loads; device tiers are
+ * streamed with TMA bulk copies.
+ *
+ * Device-side checks (block id range, row length vs. block-table width, slot
+ * range, bounded waits) never trap: they write a nonzero code into the
+ * optional `error` word (int32 in device memory) and skip the access.  Read
+ * it with fd_read_error().
+ */
+#ifndef FASTDECODE_B200_H
+#define FASTDECODE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FD_API __attribute__((visibility("default")))
+#else
+#define FD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- codes */
+
+enum fd_dtype {
+  FD_DTYPE_F16 = 0,
+  FD_DTYPE_BF16 = 1,
+  FD_DTYPE_F32 = 2
+};
+
+enum fd_status {
+  FD_OK = 0,
+  FD_ERR_INVALID = 1,     /* bad shape / argument (message: fd_last_error_message) */
+  FD_ERR_UNSUPPORTED = 2, /* valid but not built (dtype, head size, group size) */
+  FD_ERR_ALIGN = 3,       /* pointer or stride not 16-byte aligned */
+  FD_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+  FD_ERR_CUDA = 5,        /* a CUDA runtime call failed */
+  FD_ERR_RANGE = 6        /* host-visible index out of range */
+};
+
+/* codes written by kernels into the device error word */
+enum fd_device_error {
+  FD_DEVERR_NONE = 0,
+  FD_DEVERR_BLOCK_ID = 1,  /* block-table entry outside both tiers */
+  FD_DEVERR_LEN = 2,       /* lens[i] needs more blocks than the table row holds */
+  FD_DEVERR_TIMEOUT = 3,   /* a bounded wait on an mbarrier gave up */
+  FD_DEVERR_SLOT = 4,      /* KV-write slot outside both tiers */
+  FD_DEVERR_SPLITS = 5     /* lens[i] exceeds the max_len the grid was sized for */
+};
+
+/* ---------------------------------------------------------------- types */
+
+/* One KV tier.  Element (block b, kv head h, token t, dim d) of K lives at
+ * k + b*blk_stride + h*head_stride + t*tok_stride + d   (in elements).
+ * Host-store layout [C, KVH, BS, D] (fastdecode/state.py:66):
+ *     blk_stride = KVH*BS*D, head_stride = BS*D, tok_stride = D.
+ * vLLM NHD layout [B, BS, KVH, 2D] split into K/V views (backend.py:265):
+ *     blk_stride = BS*KVH*2D, head_stride = 2D, tok_stride = KVH*2D. */
+typedef struct fd_kv_tier {
+  void *k;
+  void *v;
+  int64_t blk_stride;
+  int64_t head_stride;
+  int64_t tok_stride;
+  int64_t num_blocks;  /* valid ids of this tier are [0, num_blocks) */
+  int32_t host_mapped; /* 1: pinned host memory read over PCIe */
+  int32_t _pad;
+} fd_kv_tier;
+
+/* Arguments of the split-KV decode kernel.  Strides are in elements. */
+typedef struct fd_decode_args {
+  /* queries: q[row, h, d] = q + row*q_stride_n + h*q_stride_h + d, with
+   * row = q_rows ? q_rows[i] : i  (q_rows fuses the index_select of
+   * fastdecode/backend.py:287) */
+  const void *q;
+  int64_t q_stride_n;
+  int64_t q_stride_h;
+  const int64_t *q_rows;
+
+  fd_kv_tier tier[2];
+  int64_t tier_split; /* G */
+
+  /* block_table[i*bt_stride + j], j < ceil(lens[i]/block_size) <= bt_width;
+   * entries past a row's last block are never read */
+  const int32_t *block_table;
+  int64_t bt_stride;
+  int32_t bt_width;
+  const int32_t *lens; /* [n] tokens of each row (0: empty row) */
+
+  int32_t n;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_size;
+  int32_t block_size;
+  float scale;
+  int32_t dtype; /* of q, K and V */
+
+  /* output rows: out[orow, h, d], orow = out_rows ? out_rows[i] : i
+   * (out_rows fuses output.index_copy_ of backend.py:356); out_dtype is
+   * dtype or FD_DTYPE_F32 (fp32 partials for a later merge) */
+  void *out;
+  int32_t out_dtype;
+  int32_t _pad0;
+  int64_t out_stride_n;
+  int64_t out_stride_h;
+  const int64_t *out_rows;
+
+  /* lse[h*lse_stride_h + i*lse_stride_n] (natural log; -inf for empty
+   * rows); NULL to skip.  The reference layout [H, n] is
+   * lse_stride_h = n, lse_stride_n = 1. */
+  float *lse;
+  int64_t lse_stride_h;
+  int64_t lse_stride_n;
+
+  int32_t max_len;         /* upper bound on lens[] (0: bt_width*block_size) */
+  int32_t tiles_per_split; /* 0: heuristic; a tile is min(block_size,16) tokens */
+
+  void *workspace; /* scratch for split partials, fd_decode_workspace_size() bytes */
+  size_t workspace_bytes;
+  int32_t *error;  /* optional device error word */
+} fd_decode_args;
+
+/* ---------------------------------------------------------------- decode */
+
+/* Scratch bytes fd_decode_attn needs for these arguments (0 when every row
+ * fits in one split).  Pure host arithmetic. */
+FD_API size_t fd_decode_workspace_size(const fd_decode_args *a);
+
+/* Paged decode attention over a two-tier block table.
+ *   o[i,h]   = softmax(q[i,h] . K[i]^T * scale) @ V[i]
+ *   lse[h,i] = logsumexp(q[i,h] . K[i]^T * scale)
+ * Replaces, on the GPU, both halves of the reference split path:
+ *   - decode_attn, fastdecode/csrc/cpu_attn.cpp:298-411,456-489 (host tier)
+ *   - the FlashAttention paged partial, fastdecode/backend.py:293-316 (HBM tier)
+ * and the LSE merge of the two (backend.py:354-356), because one pass over
+ * the unified table covers both tiers. */
+FD_API int fd_decode_attn(const fd_decode_args *a, void *stream);
+
+/* Drop-in for the reference pybind op
+ *   decode_attn(q, k_cache, v_cache, block_table, lens, scale, out, lse)
+ * (fastdecode/csrc/cpu_attn.cpp:456-489): contiguous q [n,H,D], caches
+ * [C,KVH,BS,D] (device memory, or mapped pinned host memory), block_table
+ * [n,W] int32 with cache-relative ids, lens [n] int32, out [n,H,D] (q dtype),
+ * lse [H,n] fp32. */
+FD_API int fd_decode_attn_paged(const void *q, const void *k_cache, const void *v_cache,
+                         int32_t cache_is_host, const int32_t *block_table,
+                         const int32_t *lens, int32_t n, int32_t num_heads,
+                         int32_t num_kv_heads, int32_t head_size, int32_t block_size,
+                         int64_t num_blocks, int32_t bt_width, float scale, int32_t dtype,
+                         void *out, float *lse, void *workspace, size_t workspace_bytes,
+                         int32_t *error, void *stream);
+
+/* Workspace bytes fd_decode_attn_paged needs. */
+FD_API size_t fd_decode_attn_paged_workspace_size(int32_t n, int32_t num_heads,
+                                           int32_t num_kv_heads, int32_t head_size,
+                                           int32_t block_size, int32_t bt_width,
+                                           int32_t dtype);
+
+/* ---------------------------------------------------------------- merge */
+
+/* Two-way log-sum-exp merge, the rule of vLLM merge_attn_states as restated
+ * in fastdecode/cpu_ops.py:93-113 and called at fastdecode/backend.py:54-55,
+ * 354-356: an lse of +inf (FlashAttention's empty row) counts as -inf, and a
+ * row empty on both sides yields zeros.
+ *   o_a, o_b: [n, H, D] contiguous, dtype in_dtype (F16/BF16/F32)
+ *   lse_a, lse_b: [H, n] fp32
+ *   out: rows out_rows[i] (or i) of an [*, H, D] tensor with out_stride_n,
+ *        dtype out_dtype; out_lse [H, n] fp32 or NULL. */
+FD_API int fd_merge_attn_states(void *out, int32_t out_dtype, int64_t out_stride_n,
+                         const int64_t *out_rows, float *out_lse,
+                         const void *o_a, const float *lse_a,
+                         const void *o_b, const float *lse_b, int32_t in_dtype,
+                         int32_t n, int32_t num_heads, int32_t head_size, void *stream);
+
+/* P-way merge of fp32 partials (the same rule over P parts), used for the
+ * KV-sharded long-context path after an all-gather of per-GPU partials.
+ *   o of part p:   o_parts  + p*part_stride, layout [n, H, D]
+ *   lse of part p: lse_parts + p*part_stride, layout [H, n]
+ *   out [n, H, D] contiguous of out_dtype; out_lse [H, n] or NULL. */
+FD_API int fd_merge_partials(const float *o_parts, const float *lse_parts, int64_t part_stride,
+                      int32_t num_parts, int32_t n, int32_t num_heads, int32_t head_size,
+                      void *out, int32_t out_dtype, float *out_lse, void *stream);
+
+/* ---------------------------------------------------------------- KV write */
+
+/* Tier-aware KV write: new K/V rows go straight to their slot in whichever
+ * tier owns it.  slot s -> block s / block_size, offset s % block_size;
+ * block < tier_split -> tier[0], else tier[1] at block - tier_split.
+ * slot < 0 is skipped (reshape_and_cache_flash convention).  If any slot is
+ * outside both tiers nothing is written and the error word gets
+ * FD_DEVERR_SLOT.  Bit-exact copy.
+ * Replaces vLLM reshape_and_cache_flash (fastdecode/backend.py:269-273) plus
+ * the D2H staging and store_kv (backend.py:279-285,344-346;
+ * fastdecode/csrc/cpu_attn.cpp:413-431,492-517).
+ *   key/value: row j, head h at key + j*key_stride_n + h*key_stride_h */
+FD_API int fd_store_kv(const void *key, int64_t key_stride_n, int64_t key_stride_h,
+                const void *value, int64_t value_stride_n, int64_t value_stride_h,
+                const int64_t *slots, int32_t m, int32_t num_kv_heads, int32_t head_size,
+                int32_t block_size, int32_t dtype, const fd_kv_tier *tiers,
+                int64_t tier_split, int32_t *error, void *stream);
+
+/* ---------------------------------------------------------------- utilities */
+
+/* Message of the last FD_ERR_* returned on this thread. */
+FD_API const char *fd_last_error_message(void);
+
+/* Text for an fd_device_error code. */
+FD_API const char *fd_device_error_string(int32_t code);
+
+/* Synchronise `stream`, copy the device error word to *value and, if
+ * `clear`, reset it to 0. */
+FD_API int fd_read_error(int32_t *error, int32_t *value, int32_t clear, void *stream);
+
+/* Device address of pinned host memory (cudaHostGetDevicePointer); fails
+ * with FD_ERR_INVALID when `host` is not pinned and mapped. */
+FD_API int fd_host_device_pointer(void *host, void **device_ptr);
+
+/* Pin and map an existing host range (cudaHostRegister, Mapped|Portable),
+ * and undo it. */
+FD_API int fd_host_register(void *host, size_t bytes);
+FD_API int fd_host_unregister(void *host);
+
+/* Library version, e.g. 100 for 0.1.0. */
+FD_API int fd_version(void);
+
+/* sizeof(fd_decode_args) and sizeof(fd_kv_tier) as compiled into the
+ * library, so bindings can check their struct mirrors. */
+FD_API int fd_abi_sizes(size_t *decode_args_bytes, size_t *kv_tier_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTDECODE_B200_H */

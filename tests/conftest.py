@@ -1,0 +1,31 @@
+"""pytest configuration: the `gpu` marker and shared helpers.
+
+Tests marked `gpu` need a CUDA device and the built native library; the rest
+run on a CPU-only host (oracle vs golden vectors, host logic, gloo ranks, the
+library's exported symbols)."""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built native library")
+
+
+def pytest_collection_modifyitems(config, items):
+    import torch
+
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)

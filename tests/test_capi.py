@@ -1,0 +1,67 @@
+"""The C-ABI library loads on a CPU-only host and exports exactly the entry
+points include/*.h declares, with the struct sizes the ctypes mirrors assume.
+No kernel is launched here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+from vllm_fastdecoder_b200 import _native as nat
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols() -> set[str]:
+    names: set[str] = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = h.read_text()
+        names |= set(re.findall(r"^FD_API\s+[\w\s\*]+?\b(fd_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for must in ("fd_decode_attn", "fd_decode_attn_paged", "fd_merge_attn_states", "fd_merge_partials",
+                 "fd_store_kv", "fd_decode_workspace_size"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = nat.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(nat.SIGNATURES) == declared_symbols()
+
+
+def test_struct_mirrors_match_the_library():
+    lib = nat.load()
+    a, b = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.fd_abi_sizes(ctypes.byref(a), ctypes.byref(b)) == 0
+    assert a.value == ctypes.sizeof(nat.FdDecodeArgs)
+    assert b.value == ctypes.sizeof(nat.FdKvTier)
+
+
+def test_host_side_argument_checks_need_no_gpu():
+    """Argument validation runs before any CUDA call."""
+    lib = nat.load()
+    args = nat.FdDecodeArgs()
+    args.n = 0
+    assert lib.fd_decode_attn(ctypes.byref(args), None) == 0  # empty batch: nothing to do
+    args.n = 4
+    args.dtype = 7
+    assert lib.fd_decode_attn(ctypes.byref(args), None) == 2  # FD_ERR_UNSUPPORTED
+    assert b"dtype" in lib.fd_last_error_message()
+    assert lib.fd_merge_attn_states(None, 0, 0, None, None, None, None, None, None, 0, -1, 4, 64, None) == 1
+    assert lib.fd_device_error_string(1).startswith(b"block id")
+    assert lib.fd_version() >= 100
+
+
+def test_workspace_size_arithmetic():
+    lib = nat.load()
+    # 16 rows of 32 heads, table width 128 blocks of 16: several splits -> nonzero
+    ws = lib.fd_decode_attn_paged_workspace_size(16, 32, 32, 128, 16, 128, 0)
+    assert ws > 0 and ws % 256 == 0
+    # one tile per row: a single split, no scratch
+    assert lib.fd_decode_attn_paged_workspace_size(4, 8, 8, 64, 16, 1, 0) == 0

@@ -1,0 +1,122 @@
+"""ctypes binding of libfastdecode_b200.so (the C ABI in include/fastdecode_b200.h).
+
+Nothing here needs a GPU to import: loading the library and reading its
+symbols works on a CPU-only host; the first kernel launch needs a device.
+The library must have been built (python -m vllm_fastdecoder_b200.build); a
+missing library raises instead of falling back to anything else.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+from vllm_fastdecoder_b200.build import library_path
+
+FD_DTYPE_F16 = 0
+FD_DTYPE_BF16 = 1
+FD_DTYPE_F32 = 2
+
+FD_OK = 0
+STATUS_NAMES = {
+    1: "FD_ERR_INVALID", 2: "FD_ERR_UNSUPPORTED", 3: "FD_ERR_ALIGN",
+    4: "FD_ERR_WORKSPACE", 5: "FD_ERR_CUDA", 6: "FD_ERR_RANGE",
+}
+
+
+class FdKvTier(ctypes.Structure):
+    _fields_ = [
+        ("k", c_void_p), ("v", c_void_p),
+        ("blk_stride", c_int64), ("head_stride", c_int64), ("tok_stride", c_int64),
+        ("num_blocks", c_int64), ("host_mapped", c_int32), ("_pad", c_int32),
+    ]
+
+
+class FdDecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_stride_n", c_int64), ("q_stride_h", c_int64), ("q_rows", c_void_p),
+        ("tier", FdKvTier * 2), ("tier_split", c_int64),
+        ("block_table", c_void_p), ("bt_stride", c_int64), ("bt_width", c_int32),
+        ("lens", c_void_p),
+        ("n", c_int32), ("num_heads", c_int32), ("num_kv_heads", c_int32),
+        ("head_size", c_int32), ("block_size", c_int32), ("scale", c_float), ("dtype", c_int32),
+        ("out", c_void_p), ("out_dtype", c_int32), ("_pad0", c_int32),
+        ("out_stride_n", c_int64), ("out_stride_h", c_int64), ("out_rows", c_void_p),
+        ("lse", c_void_p), ("lse_stride_h", c_int64), ("lse_stride_n", c_int64),
+        ("max_len", c_int32), ("tiles_per_split", c_int32),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("error", c_void_p),
+    ]
+
+
+# name -> (restype, argtypes); mirrors include/fastdecode_b200.h
+SIGNATURES = {
+    "fd_decode_workspace_size": (c_size_t, [POINTER(FdDecodeArgs)]),
+    "fd_decode_attn": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
+    "fd_decode_attn_paged": (c_int32, [
+        c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+        c_int32, c_int32, c_int64, c_int32, c_float, c_int32, c_void_p, c_void_p, c_void_p,
+        c_size_t, c_void_p, c_void_p]),
+    "fd_decode_attn_paged_workspace_size": (c_size_t, [
+        c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "fd_merge_attn_states": (c_int32, [
+        c_void_p, c_int32, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_int32, c_int32, c_int32, c_int32, c_void_p]),
+    "fd_merge_partials": (c_int32, [
+        c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
+        c_void_p, c_void_p]),
+    "fd_store_kv": (c_int32, [
+        c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int32, c_int32,
+        c_int32, c_int32, c_int32, POINTER(FdKvTier), c_int64, c_void_p, c_void_p]),
+    "fd_last_error_message": (c_char_p, []),
+    "fd_device_error_string": (c_char_p, [c_int32]),
+    "fd_read_error": (c_int32, [c_void_p, POINTER(c_int32), c_int32, c_void_p]),
+    "fd_host_device_pointer": (c_int32, [c_void_p, POINTER(c_void_p)]),
+    "fd_host_register": (c_int32, [c_void_p, c_size_t]),
+    "fd_host_unregister": (c_int32, [c_void_p]),
+    "fd_version": (c_int32, []),
+    "fd_abi_sizes": (c_int32, [POINTER(c_size_t), POINTER(c_size_t)]),
+}
+
+_LIB = None
+_LOCK = threading.Lock()
+
+
+def lib_path() -> Path:
+    return library_path()
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library (once) and attach the C signatures."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        path = lib_path()
+        if not path.exists():
+            raise RuntimeError(
+                f"fastdecode_b200: native library {path} is missing; build it with "
+                "`python -m vllm_fastdecoder_b200.build` (there is no fallback path)"
+            )
+        lib = ctypes.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    """Raise RuntimeError for a nonzero fd_status, with the library's message."""
+    if status != FD_OK:
+        msg = load().fd_last_error_message()
+        text = msg.decode() if msg else ""
+        raise RuntimeError(f"{what}: {STATUS_NAMES.get(status, status)}: {text}")
+
+
+def device_error_string(code: int) -> str:
+    return load().fd_device_error_string(int(code)).decode()

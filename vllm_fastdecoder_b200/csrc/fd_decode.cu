@@ -1,0 +1,774 @@
+// Split-KV paged decode attention over a two-tier (HBM + mapped host) block
+// table, for sm_100a.
+//
+// Grid: x = split of the row's token range, y = (kv head, query-head chunk),
+// z = row.  Each CTA streams its split's K/V tiles (tile = min(block_size,16)
+// tokens of one block and one kv head) through an NST-deep shared-memory ring:
+//   * warp 4 (producer) fills a stage: device-memory tiles with TMA bulk
+//     copies (cp.async.bulk, completion counted in bytes on the stage's
+//     mbarrier), host-tier tiles (pinned, mapped) with 16-byte loads;
+//   * warps 0-3 (consumers) each own one tile per stage: q.K^T with fp32 FMAs
+//     and shuffle reductions, an fp32 online softmax in the exp2 domain, then
+//     P.V into per-lane fp32 accumulators, and release the stage.
+// The four warp-level states are merged through shared memory at the end.
+// A row that fits in one split writes o / lse directly; otherwise the split
+// writes an fp32 partial (o normalised, lse) into the workspace and
+// fd_split_merge_kernel combines them with the log-sum-exp rule.
+//
+// Numerics follow the reference CPU kernel (fastdecode/csrc/cpu_attn.cpp
+// :298-411): fp16/bf16 widened to fp32, q pre-scaled in fp32 (:338), fp32
+// accumulation, output = acc * (1/sum) cast to the output type (:401-405),
+// lse = max + log(sum) (:406), empty row -> o = 0, lse = -inf (:324-331).
+
+#include <math.h>
+
+#include <algorithm>
+
+#include "fd_common.cuh"
+#include "fd_internal.h"
+
+namespace fdk {
+
+struct DecodeParams {
+  const unsigned char* q;
+  int64_t q_sn, q_sh;  // bytes
+  const int64_t* q_rows;
+  const unsigned char* k[2];
+  const unsigned char* v[2];
+  int64_t blk_sb[2], head_sb[2], tok_sb[2];  // bytes
+  int64_t nblk[2];
+  int host[2];
+  int contig[2];
+  int64_t split;
+  const int32_t* bt;
+  int64_t bt_stride;
+  int bt_width;
+  const int32_t* lens;
+  int n, H, KVH, BS, G, gcs;
+  int TT, tiles_per_block, tiles_per_split, max_splits;
+  float qscale;  // scale * log2(e)
+  void* out;
+  int out_dtype;
+  int64_t out_sn, out_sh;  // elements
+  const int64_t* out_rows;
+  float* lse;
+  int64_t lse_sh, lse_sn;
+  float* part_o;
+  float* part_lse;
+  int32_t* err;
+};
+
+constexpr int p2div(int x, int p) { return (x % (2 * p) == 0 && 2 * p <= 32) ? p2div(x, 2 * p) : p; }
+constexpr int ceil_pow2(int x, int p) { return p >= x ? p : ceil_pow2(x, 2 * p); }
+constexpr int cmin(int a, int b) { return a < b ? a : b; }
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+template <typename T, int D, int GQ>
+struct Cfg {
+  static constexpr int kE = sizeof(T);
+  static constexpr int kRB = D * kE;  // bytes of one token row of one head
+  static constexpr int kNCH = kRB / 16;
+  static constexpr int kEPC = 16 / kE;
+  static constexpr int kNW = 4;  // consumer warps
+  static constexpr int kThreads = (kNW + 1) * 32;
+  static constexpr int kMaxTT = 16;
+  // q.K: kTPT lanes per token, each holding kCPL 16-byte chunks of q per head
+  static constexpr int kTPT = cmin(p2div(kNCH, 1), ceil_pow2(cmax(2, GQ * D / 64), 1));
+  static constexpr int kCPL = kNCH / kTPT;
+  static constexpr int kTPP = 32 / kTPT;  // tokens per pass
+  static constexpr int kNPASS = (kMaxTT + kTPP - 1) / kTPP;
+  // P.V: lane owns chunk (lane % kNCH) of token rows (lane / kNCH) + k*kRPI
+  static constexpr int kRPI = 32 / kNCH;
+  static constexpr int kPVL = kRPI * kNCH;
+  static constexpr int kTileBytes = kMaxTT * kRB;
+  static constexpr int kStageBytes = kNW * 2 * kTileBytes;
+  static constexpr int kNST = cmax(2, cmin(4, 98304 / kStageBytes));
+  static constexpr int kBarBytes = 128;
+  static constexpr int kPsBytes = ((kNW * kMaxTT * GQ * 4 + 127) / 128) * 128;
+  static constexpr int kRedBytes = (2 * kNW * GQ + kNW * kRPI * GQ * D) * 4;
+  static constexpr int kSmem = kBarBytes + kPsBytes + kNST * kStageBytes;
+  static constexpr bool kValid =
+      (kRB % 16 == 0) && kNCH <= 32 && (GQ * kCPL * kEPC <= 64 || GQ == 1) &&
+      kRedBytes <= kNST * kStageBytes && 2 * kNST * 8 <= kBarBytes && kSmem <= 227 * 1024;
+};
+
+template <typename T, int D, int GQ>
+__global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
+    fd_decode_kernel(const __grid_constant__ DecodeParams p) {
+  using C = Cfg<T, D, GQ>;
+  using DT = Dt<T>;
+  constexpr int EPC = C::kEPC;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + C::kNST;
+  float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes);
+  unsigned char* stages = smem + C::kBarBytes + C::kPsBytes;
+
+  const int split = blockIdx.x;
+  const int kh = blockIdx.y / p.gcs;
+  const int gc = blockIdx.y - kh * p.gcs;
+  const int i = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h0 = kh * p.G + gc * GQ;
+  const int len = p.lens[i];
+
+  if (len <= 0) {
+    // empty row: o = 0, lse = -inf (reference cpu_attn.cpp:324-331)
+    if (split == 0) {
+      const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+      for (int o = threadIdx.x; o < GQ * D; o += blockDim.x) {
+        const int g = o / D, d = o - g * D;
+        store_out(p.out, orow * p.out_sn + (int64_t)(h0 + g) * p.out_sh + d, p.out_dtype, 0.f);
+      }
+      if (p.lse != nullptr && threadIdx.x < GQ)
+        p.lse[(int64_t)(h0 + threadIdx.x) * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
+    }
+    return;
+  }
+  const int nblk = (len + p.BS - 1) / p.BS;
+  if (nblk > p.bt_width) {
+    if (threadIdx.x == 0 && split == 0) set_error(p.err, FD_DEVERR_LEN);
+    return;
+  }
+  const int ntiles = (len + p.TT - 1) / p.TT;
+  const int nsplits = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
+  if (nsplits > p.max_splits) {
+    if (threadIdx.x == 0 && split == 0) set_error(p.err, FD_DEVERR_SPLITS);
+    return;
+  }
+  if (split >= nsplits) return;
+  const int tbeg = split * p.tiles_per_split;
+  const int tend = min(ntiles, tbeg + p.tiles_per_split);
+  const int nstages = (tend - tbeg + C::kNW - 1) / C::kNW;
+  const uint32_t tile_bytes = (uint32_t)p.TT * C::kRB;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < C::kNST; ++s) {
+      mbar_init(&full[s], 32);
+      mbar_init(&empty[s], C::kNW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == C::kNW) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol = l2_evict_first_policy();
+    const int32_t* btrow = p.bt + (int64_t)i * p.bt_stride;
+    for (int k = 0; k < nstages; ++k) {
+      const int st = k % C::kNST;
+      const uint32_t use = (uint32_t)(k / C::kNST);
+      if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1u, p.err)) return;
+      unsigned char* sbase = stages + st * C::kStageBytes;
+      const int tile = tbeg + k * C::kNW + lane;
+      int tier = 0;
+      bool valid = false;
+      const unsigned char* ks = nullptr;
+      const unsigned char* vs = nullptr;
+      if (lane < C::kNW && tile < tend) {
+        const int b = tile / p.tiles_per_block;
+        const int r0 = (tile - b * p.tiles_per_block) * p.TT;
+        int64_t id = btrow[b];
+        if (id >= p.split) {
+          tier = 1;
+          id -= p.split;
+        }
+        if (id >= 0 && id < p.nblk[tier]) {
+          valid = true;
+          const int64_t off = id * p.blk_sb[tier] + (int64_t)kh * p.head_sb[tier] + (int64_t)r0 * p.tok_sb[tier];
+          ks = p.k[tier] + off;
+          vs = p.v[tier] + off;
+        } else {
+          set_error(p.err, FD_DEVERR_BLOCK_ID);
+        }
+      }
+      const bool bulk = valid && !p.host[tier];
+      const unsigned bulk_mask = __ballot_sync(0xffffffffu, bulk);
+      const unsigned host_mask = __ballot_sync(0xffffffffu, valid && !bulk);
+      if (lane == 0 && bulk_mask != 0u)
+        mbar_expect_tx(&full[st], (uint32_t)__popc(bulk_mask) * 2u * tile_bytes);
+      __syncwarp();
+      for (unsigned m = bulk_mask; m != 0u; m &= m - 1u) {
+        const int w = __ffs(m) - 1;
+        const unsigned char* kw = reinterpret_cast<const unsigned char*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
+        const unsigned char* vw = reinterpret_cast<const unsigned char*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
+        const int tr = __shfl_sync(0xffffffffu, tier, w);
+        unsigned char* kd = sbase + (2 * w) * tile_bytes;
+        unsigned char* vd = kd + tile_bytes;
+        if (p.contig[tr]) {
+          if (lane == 0) {
+            bulk_g2s(kd, kw, tile_bytes, &full[st], pol);
+            bulk_g2s(vd, vw, tile_bytes, &full[st], pol);
+          }
+        } else {
+          for (int r = lane; r < p.TT; r += 32) {
+            bulk_g2s(kd + r * C::kRB, kw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
+            bulk_g2s(vd + r * C::kRB, vw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
+          }
+        }
+      }
+      for (unsigned m = host_mask; m != 0u; m &= m - 1u) {
+        const int w = __ffs(m) - 1;
+        const unsigned char* kw = reinterpret_cast<const unsigned char*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
+        const unsigned char* vw = reinterpret_cast<const unsigned char*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
+        const int tr = __shfl_sync(0xffffffffu, tier, w);
+        const int64_t tsb = p.tok_sb[tr];
+        unsigned char* kd = sbase + (2 * w) * tile_bytes;
+        unsigned char* vd = kd + tile_bytes;
+        const int nch = p.TT * C::kNCH;
+        constexpr int U = 4;
+        for (int c0 = 0; c0 < nch; c0 += 32 * U) {
+          uint4 kb[U], vb[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int c = c0 + u * 32 + lane;
+            if (c < nch) {
+              const int row = c / C::kNCH;
+              const int64_t off = row * tsb + (c - row * C::kNCH) * 16;
+              kb[u] = *reinterpret_cast<const uint4*>(kw + off);
+              vb[u] = *reinterpret_cast<const uint4*>(vw + off);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int c = c0 + u * 32 + lane;
+            if (c < nch) {
+              sts128(kd + c * 16, kb[u]);
+              sts128(vd + c * 16, vb[u]);
+            }
+          }
+        }
+      }
+      // order this stage's generic smem writes before later TMA writes to it
+      if (host_mask != 0u) fence_proxy_async_smem();
+      mbar_arrive(&full[st]);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int tp = lane / C::kTPT;
+  const int sub = lane - tp * C::kTPT;
+  const int rot = tp % C::kCPL;
+
+  // q for this lane's chunks, widened and pre-scaled (reference :334-339),
+  // stored in the rotated order the K reads use (bank-conflict free).
+  float qr[GQ][C::kCPL][EPC];
+  {
+    const int64_t qrow = p.q_rows ? p.q_rows[i] : i;
+    const unsigned char* qb = p.q + qrow * p.q_sn + (int64_t)h0 * p.q_sh;
+#pragma unroll
+    for (int g = 0; g < GQ; ++g) {
+#pragma unroll
+      for (int jj = 0; jj < C::kCPL; ++jj) {
+        const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(qb + g * p.q_sh + c * 16));
+        DT::widen(v, qr[g][jj]);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) qr[g][jj][e] *= p.qscale;
+      }
+    }
+  }
+
+  float m_run[GQ], l_run[GQ], acc[GQ][EPC];
+#pragma unroll
+  for (int g = 0; g < GQ; ++g) {
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) acc[g][e] = 0.f;
+  }
+  const int cpv = lane % C::kNCH;
+  const int rg = lane / C::kNCH;
+  const bool pv_on = lane < C::kPVL;
+  float* psw = ps_all + warp * C::kMaxTT * GQ;
+  bool ok = true;
+
+  for (int k = 0; k < nstages; ++k) {
+    const int st = k % C::kNST;
+    const uint32_t use = (uint32_t)(k / C::kNST);
+    if (!mbar_wait(&full[st], use & 1u, p.err)) {
+      ok = false;
+      break;
+    }
+    const int tile = tbeg + k * C::kNW + warp;
+    if (tile < tend) {
+      const int ntok = min(p.TT, len - tile * p.TT);
+      const unsigned char* ks = stages + st * C::kStageBytes + (2 * warp) * tile_bytes;
+      const unsigned char* vs = ks + tile_bytes;
+
+      // ---- scores s = q.k (log2 domain), one token per lane group per pass
+      float s[GQ][C::kNPASS];
+#pragma unroll
+      for (int pp = 0; pp < C::kNPASS; ++pp) {
+        const int t = pp * C::kTPP + tp;
+        float dot[GQ];
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) dot[g] = 0.f;
+        if (t < ntok) {
+#pragma unroll
+          for (int jj = 0; jj < C::kCPL; ++jj) {
+            const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
+            const uint4 kv = lds128(ks + t * C::kRB + c * 16);
+            float kf[EPC];
+            DT::widen(kv, kf);
+#pragma unroll
+            for (int g = 0; g < GQ; ++g)
+#pragma unroll
+              for (int e = 0; e < EPC; ++e) dot[g] = fmaf(qr[g][jj][e], kf[e], dot[g]);
+          }
+        }
+#pragma unroll
+        for (int off = C::kTPT / 2; off >= 1; off >>= 1)
+#pragma unroll
+          for (int g = 0; g < GQ; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) s[g][pp] = (t < ntok) ? dot[g] : -INFINITY;
+      }
+
+      // ---- online softmax update for this tile
+      float alpha[GQ];
+#pragma unroll
+      for (int g = 0; g < GQ; ++g) {
+        float bm = s[g][0];
+#pragma unroll
+        for (int pp = 1; pp < C::kNPASS; ++pp) bm = fmaxf(bm, s[g][pp]);
+#pragma unroll
+        for (int off = C::kTPT; off < 32; off <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+        const float mn = fmaxf(m_run[g], bm);
+        alpha[g] = exp2f(m_run[g] - mn);
+        float sum = 0.f;
+#pragma unroll
+        for (int pp = 0; pp < C::kNPASS; ++pp) {
+          const float e = exp2f(s[g][pp] - mn);
+          s[g][pp] = e;
+          sum += e;
+        }
+#pragma unroll
+        for (int off = C::kTPT; off < 32; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        l_run[g] = l_run[g] * alpha[g] + sum;
+        m_run[g] = mn;
+      }
+      if (sub == 0) {
+#pragma unroll
+        for (int pp = 0; pp < C::kNPASS; ++pp) {
+          const int t = pp * C::kTPP + tp;
+          if (t < C::kMaxTT)
+#pragma unroll
+            for (int g = 0; g < GQ; ++g) psw[t * GQ + g] = s[g][pp];
+        }
+      }
+      __syncwarp();
+
+      // ---- acc = acc * alpha + P.V
+#pragma unroll
+      for (int g = 0; g < GQ; ++g)
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) acc[g][e] *= alpha[g];
+      if (pv_on) {
+#pragma unroll 4
+        for (int r = rg; r < ntok; r += C::kRPI) {
+          const uint4 vv = lds128(vs + r * C::kRB + cpv * 16);
+          float vf[EPC];
+          DT::widen(vv, vf);
+          float pr[GQ];
+#pragma unroll
+          for (int g = 0; g < GQ; ++g) pr[g] = psw[r * GQ + g];
+#pragma unroll
+          for (int g = 0; g < GQ; ++g)
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) acc[g][e] = fmaf(pr[g], vf[e], acc[g][e]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+
+  // -------------------------------------------------------------- combine
+  named_barrier_sync(1, C::kNW * 32);
+  float* red_m = reinterpret_cast<float*>(stages);
+  float* red_l = red_m + C::kNW * GQ;
+  float* red_acc = red_l + C::kNW * GQ;
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GQ; ++g) {
+      red_m[warp * GQ + g] = ok ? m_run[g] : -INFINITY;
+      red_l[warp * GQ + g] = ok ? l_run[g] : 0.f;
+    }
+  }
+  if (pv_on) {
+#pragma unroll
+    for (int g = 0; g < GQ; ++g)
+#pragma unroll
+      for (int e = 0; e < EPC; ++e)
+        red_acc[((warp * C::kRPI + rg) * GQ + g) * D + cpv * EPC + e] = acc[g][e];
+  }
+  named_barrier_sync(1, C::kNW * 32);
+
+  const bool single = (nsplits == 1);
+  const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+  for (int o = threadIdx.x; o < GQ * D; o += C::kNW * 32) {
+    const int g = o / D;
+    const int d = o - g * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < C::kNW; ++w) M = fmaxf(M, red_m[w * GQ + g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < C::kNW; ++w) {
+      const float sc = exp2f(red_m[w * GQ + g] - M);
+      L += red_l[w * GQ + g] * sc;
+      float a = 0.f;
+#pragma unroll
+      for (int r = 0; r < C::kRPI; ++r) a += red_acc[((w * C::kRPI + r) * GQ + g) * D + d];
+      O += a * sc;
+    }
+    const float inv = 1.f / L;
+    const float lse_nat = (M + log2f(L)) * kLn2;
+    const int h = h0 + g;
+    if (single) {
+      store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
+      if (d == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = lse_nat;
+    } else {
+      const int64_t pidx = ((int64_t)i * p.H + h) * p.max_splits + split;
+      p.part_o[pidx * D + d] = O * inv;
+      if (d == 0) p.part_lse[pidx] = lse_nat;
+    }
+  }
+}
+
+// Combine the split partials of rows that needed more than one split.
+__global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, int D) {
+  extern __shared__ float wsm[];
+  const int h = blockIdx.x;
+  const int i = blockIdx.y;
+  const int len = p.lens[i];
+  if (len <= 0) return;
+  const int nblk = (len + p.BS - 1) / p.BS;
+  if (nblk > p.bt_width) return;
+  const int ntiles = (len + p.TT - 1) / p.TT;
+  const int ns = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
+  if (ns <= 1 || ns > p.max_splits) return;
+  const int64_t base = ((int64_t)i * p.H + h) * p.max_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_lse[base + s]);
+  for (int s = threadIdx.x; s < ns; s += blockDim.x) wsm[s] = exp2f((p.part_lse[base + s] - M) * kLog2e);
+  __syncthreads();
+  float L = 0.f;
+  for (int s = 0; s < ns; ++s) L += wsm[s];
+  const float inv = 1.f / L;
+  const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float O = 0.f;
+    for (int s = 0; s < ns; ++s) O = fmaf(wsm[s], p.part_o[(base + s) * D + d], O);
+    store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
+  }
+  if (threadIdx.x == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = M + logf(L);
+}
+
+}  // namespace fdk
+
+// ============================================================== host side
+
+namespace {
+
+using fdk::Cfg;
+using fdk::DecodeParams;
+
+constexpr int kTargetCtas = 148 * 2 * 8;  // ~8 waves at 2 CTAs per SM
+
+struct Geometry {
+  int TT, tiles_per_block, tiles_per_split, max_splits, G, GQ, gcs;
+  size_t ws_bytes;
+};
+
+typedef int (*launch_fn)(const DecodeParams&, dim3, cudaStream_t);
+
+template <typename T, int D, int GQ>
+int launch_impl(const DecodeParams& p, dim3 grid, cudaStream_t s) {
+  using C = Cfg<T, D, GQ>;
+  static unsigned long long done = 0;
+  auto kern = fdk::fd_decode_kernel<T, D, GQ>;
+  int st = fdh::ensure_smem(reinterpret_cast<const void*>(kern), C::kSmem, &done);
+  if (st != FD_OK) return st;
+  kern<<<grid, C::kThreads, C::kSmem, s>>>(p);
+  return fdh::cuda_status(cudaGetLastError(), "fd_decode_kernel launch");
+}
+
+template <typename T, int D, int GQ>
+constexpr launch_fn pick() {
+  if constexpr (Cfg<T, D, GQ>::kValid) {
+    return &launch_impl<T, D, GQ>;
+  } else {
+    return nullptr;
+  }
+}
+
+template <typename T, int D>
+launch_fn pick_gq(int gq) {
+  switch (gq) {
+    case 1:
+      return pick<T, D, 1>();
+    case 2:
+      return pick<T, D, 2>();
+    case 4:
+      return pick<T, D, 4>();
+    default:
+      return nullptr;
+  }
+}
+
+template <typename T>
+launch_fn pick_d(int D, int gq) {
+  switch (D) {
+    case 64:
+      return pick_gq<T, 64>(gq);
+    case 72:
+      return pick_gq<T, 72>(gq);
+    case 96:
+      return pick_gq<T, 96>(gq);
+    case 128:
+      return pick_gq<T, 128>(gq);
+    case 256:
+      return pick_gq<T, 256>(gq);
+    default:
+      return nullptr;
+  }
+}
+
+launch_fn pick_kernel(int dtype, int D, int gq) {
+  switch (dtype) {
+    case FD_DTYPE_F16:
+      return pick_d<__half>(D, gq);
+    case FD_DTYPE_BF16:
+      return pick_d<__nv_bfloat16>(D, gq);
+    case FD_DTYPE_F32:
+      return pick_d<float>(D, gq);
+    default:
+      return nullptr;
+  }
+}
+
+// Largest query-head group per CTA (4, 2 or 1) that divides G and is built.
+int choose_gq(int dtype, int D, int G) {
+  const int opts[3] = {4, 2, 1};
+  for (int gq : opts)
+    if (G % gq == 0 && pick_kernel(dtype, D, gq) != nullptr) return gq;
+  return 0;
+}
+
+int geometry(const fd_decode_args* a, Geometry* g) {
+  const int BS = a->block_size;
+  if (BS <= 0) return fdh::fail(FD_ERR_INVALID, "block_size must be positive, got %d", BS);
+  if (BS > 16 && BS % 16 != 0)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "block_size %d: above 16 it must be a multiple of 16", BS);
+  if (a->num_kv_heads <= 0 || a->num_heads <= 0 || a->num_heads % a->num_kv_heads != 0)
+    return fdh::fail(FD_ERR_INVALID, "num_heads must be a multiple of num_kv_heads");
+  g->TT = BS <= 16 ? BS : 16;
+  g->tiles_per_block = BS / g->TT;
+  g->G = a->num_heads / a->num_kv_heads;
+  g->GQ = choose_gq(a->dtype, a->head_size, g->G);
+  if (g->GQ == 0)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "no decode kernel for dtype %d head_size %d", a->dtype,
+                     a->head_size);
+  g->gcs = g->G / g->GQ;
+  const int64_t max_len =
+      a->max_len > 0 ? (int64_t)a->max_len : (int64_t)a->bt_width * (int64_t)BS;
+  const int64_t ntiles_max = std::max<int64_t>(1, (max_len + g->TT - 1) / g->TT);
+  int64_t tps = a->tiles_per_split;
+  if (tps <= 0) {
+    const int64_t ctas_per_row = (int64_t)a->num_kv_heads * g->gcs;
+    const int64_t est = (int64_t)std::max(a->n, 1) * ctas_per_row * ntiles_max;
+    tps = std::max<int64_t>(8, (est + kTargetCtas - 1) / kTargetCtas);
+  }
+  tps = (tps + 3) / 4 * 4;  // whole stages of the 4 consumer warps
+  g->tiles_per_split = (int)std::min<int64_t>(tps, 1 << 30);
+  g->max_splits = (int)((ntiles_max + tps - 1) / tps);
+  g->ws_bytes = 0;
+  if (g->max_splits > 1) {
+    const size_t rows = (size_t)a->n * (size_t)a->num_heads * (size_t)g->max_splits;
+    const size_t o_bytes = (rows * (size_t)a->head_size * 4 + 255) / 256 * 256;
+    g->ws_bytes = o_bytes + (rows * 4 + 255) / 256 * 256;
+  }
+  return FD_OK;
+}
+
+}  // namespace
+
+extern "C" size_t fd_decode_workspace_size(const fd_decode_args* a) {
+  if (a == nullptr || a->n <= 0) return 0;
+  Geometry g;
+  if (geometry(a, &g) != FD_OK) return 0;
+  return g.ws_bytes;
+}
+
+extern "C" int fd_decode_attn(const fd_decode_args* a, void* stream) {
+  if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_decode_attn: null args");
+  if (a->n < 0) return fdh::fail(FD_ERR_INVALID, "n must be >= 0");
+  if (a->n == 0) return FD_OK;
+  const int es = fdh::elem_size(a->dtype);
+  if (es == 0) return fdh::fail(FD_ERR_UNSUPPORTED, "unsupported dtype %d", a->dtype);
+  if (a->out_dtype != a->dtype && a->out_dtype != FD_DTYPE_F32)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "out_dtype must equal dtype or be FD_DTYPE_F32");
+  if (a->q == nullptr || a->out == nullptr || a->block_table == nullptr || a->lens == nullptr)
+    return fdh::fail(FD_ERR_INVALID, "q, out, block_table and lens are required");
+  if (a->bt_width <= 0) return fdh::fail(FD_ERR_INVALID, "bt_width must be positive");
+  if (a->n > 65535) return fdh::fail(FD_ERR_UNSUPPORTED, "at most 65535 rows per call");
+  Geometry g;
+  int st = geometry(a, &g);
+  if (st != FD_OK) return st;
+  const int D = a->head_size;
+  const int64_t row_bytes = (int64_t)D * es;
+  if (row_bytes % 16 != 0) return fdh::fail(FD_ERR_ALIGN, "head_size*elem_size must be a multiple of 16");
+  if (!fdh::aligned16(a->q) || (a->q_stride_h * es) % 16 != 0 || (a->q_stride_n * es) % 16 != 0)
+    return fdh::fail(FD_ERR_ALIGN, "q pointer and strides must be 16-byte aligned");
+
+  DecodeParams p{};
+  p.q = static_cast<const unsigned char*>(a->q);
+  p.q_sn = a->q_stride_n * es;
+  p.q_sh = a->q_stride_h * es;
+  p.q_rows = a->q_rows;
+  for (int t = 0; t < 2; ++t) {
+    const fd_kv_tier& tr = a->tier[t];
+    p.k[t] = static_cast<const unsigned char*>(tr.k);
+    p.v[t] = static_cast<const unsigned char*>(tr.v);
+    p.blk_sb[t] = tr.blk_stride * es;
+    p.head_sb[t] = tr.head_stride * es;
+    p.tok_sb[t] = tr.tok_stride * es;
+    p.nblk[t] = tr.num_blocks > 0 ? tr.num_blocks : 0;
+    p.host[t] = tr.host_mapped ? 1 : 0;
+    p.contig[t] = (p.tok_sb[t] == row_bytes) ? 1 : 0;
+    if (p.nblk[t] > 0) {
+      if (tr.k == nullptr || tr.v == nullptr)
+        return fdh::fail(FD_ERR_INVALID, "tier %d has blocks but no K/V pointer", t);
+      if (!fdh::aligned16(tr.k) || !fdh::aligned16(tr.v) || p.blk_sb[t] % 16 != 0 ||
+          p.head_sb[t] % 16 != 0 || p.tok_sb[t] % 16 != 0)
+        return fdh::fail(FD_ERR_ALIGN, "tier %d K/V pointers and strides must be 16-byte aligned", t);
+    }
+  }
+  p.split = a->tier_split;
+  p.bt = a->block_table;
+  p.bt_stride = a->bt_stride;
+  p.bt_width = a->bt_width;
+  p.lens = a->lens;
+  p.n = a->n;
+  p.H = a->num_heads;
+  p.KVH = a->num_kv_heads;
+  p.BS = a->block_size;
+  p.G = g.G;
+  p.gcs = g.gcs;
+  p.TT = g.TT;
+  p.tiles_per_block = g.tiles_per_block;
+  p.tiles_per_split = g.tiles_per_split;
+  p.max_splits = g.max_splits;
+  p.qscale = a->scale * fdk::kLog2e;
+  p.out = a->out;
+  p.out_dtype = a->out_dtype;
+  p.out_sn = a->out_stride_n;
+  p.out_sh = a->out_stride_h;
+  p.out_rows = a->out_rows;
+  p.lse = a->lse;
+  p.lse_sh = a->lse_stride_h;
+  p.lse_sn = a->lse_stride_n;
+  p.err = a->error;
+  if (g.max_splits > 1) {
+    if (a->workspace == nullptr || a->workspace_bytes < g.ws_bytes)
+      return fdh::fail(FD_ERR_WORKSPACE, "workspace of %zu bytes needed, got %zu", g.ws_bytes,
+                       a->workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fdh::fail(FD_ERR_ALIGN, "workspace must be 256-byte aligned");
+    const size_t rows = (size_t)a->n * (size_t)a->num_heads * (size_t)g.max_splits;
+    const size_t o_bytes = (rows * (size_t)D * 4 + 255) / 256 * 256;
+    p.part_o = static_cast<float*>(a->workspace);
+    p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(a->workspace) + o_bytes);
+  }
+  if ((int64_t)a->num_kv_heads * g.gcs > 65535)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "too many heads for the grid");
+  launch_fn fn = pick_kernel(a->dtype, D, g.GQ);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dim3 grid(g.max_splits, a->num_kv_heads * g.gcs, a->n);
+  st = fn(p, grid, s);
+  if (st != FD_OK) return st;
+  if (g.max_splits > 1) {
+    const int threads = D <= 128 ? 128 : 256;
+    const size_t sm = (size_t)g.max_splits * sizeof(float);
+    if (sm > 48 * 1024) return fdh::fail(FD_ERR_UNSUPPORTED, "too many splits (%d)", g.max_splits);
+    fdk::fd_split_merge_kernel<<<dim3(a->num_heads, a->n), threads, sm, s>>>(p, D);
+    st = fdh::cuda_status(cudaGetLastError(), "fd_split_merge_kernel launch");
+  }
+  return st;
+}
+
+namespace {
+void paged_args(fd_decode_args* a, const void* q, const void* k_cache, const void* v_cache,
+                int32_t cache_is_host, const int32_t* block_table, const int32_t* lens, int32_t n,
+                int32_t H, int32_t KVH, int32_t D, int32_t BS, int64_t num_blocks, int32_t W,
+                float scale, int32_t dtype, void* out, float* lse, void* ws, size_t ws_bytes,
+                int32_t* error) {
+  *a = fd_decode_args{};
+  a->q = q;
+  a->q_stride_n = (int64_t)H * D;
+  a->q_stride_h = D;
+  a->tier[0].k = const_cast<void*>(k_cache);
+  a->tier[0].v = const_cast<void*>(v_cache);
+  a->tier[0].blk_stride = (int64_t)KVH * BS * D;
+  a->tier[0].head_stride = (int64_t)BS * D;
+  a->tier[0].tok_stride = D;
+  a->tier[0].num_blocks = num_blocks;
+  a->tier[0].host_mapped = cache_is_host;
+  a->tier_split = INT64_MAX;
+  a->block_table = block_table;
+  a->bt_stride = W;
+  a->bt_width = W;
+  a->lens = lens;
+  a->n = n;
+  a->num_heads = H;
+  a->num_kv_heads = KVH;
+  a->head_size = D;
+  a->block_size = BS;
+  a->scale = scale;
+  a->dtype = dtype;
+  a->out = out;
+  a->out_dtype = dtype;
+  a->out_stride_n = (int64_t)H * D;
+  a->out_stride_h = D;
+  a->lse = lse;
+  a->lse_stride_h = n;
+  a->lse_stride_n = 1;
+  a->workspace = ws;
+  a->workspace_bytes = ws_bytes;
+  a->error = error;
+}
+}  // namespace
+
+extern "C" size_t fd_decode_attn_paged_workspace_size(int32_t n, int32_t num_heads,
+                                                      int32_t num_kv_heads, int32_t head_size,
+                                                      int32_t block_size, int32_t bt_width,
+                                                      int32_t dtype) {
+  fd_decode_args a;
+  paged_args(&a, nullptr, nullptr, nullptr, 0, nullptr, nullptr, n, num_heads, num_kv_heads,
+             head_size, block_size, 0, bt_width, 1.f, dtype, nullptr, nullptr, nullptr, 0,
+             nullptr);
+  return fd_decode_workspace_size(&a);
+}
+
+extern "C" int fd_decode_attn_paged(const void* q, const void* k_cache, const void* v_cache,
+                                    int32_t cache_is_host, const int32_t* block_table,
+                                    const int32_t* lens, int32_t n, int32_t num_heads,
+                                    int32_t num_kv_heads, int32_t head_size, int32_t block_size,
+                                    int64_t num_blocks, int32_t bt_width, float scale,
+                                    int32_t dtype, void* out, float* lse, void* workspace,
+                                    size_t workspace_bytes, int32_t* error, void* stream) {
+  fd_decode_args a;
+  paged_args(&a, q, k_cache, v_cache, cache_is_host, block_table, lens, n, num_heads,
+             num_kv_heads, head_size, block_size, num_blocks, bt_width, scale, dtype, out, lse,
+             workspace, workspace_bytes, error);
+  return fd_decode_attn(&a, stream);
+}

@@ -1,0 +1,37 @@
+// Host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+
+#include "fastdecode_b200.h"
+
+namespace fdh {
+
+// Record a message for fd_last_error_message() and return `status`.
+int fail(int status, const char* fmt, ...);
+
+inline int elem_size(int32_t dtype) {
+  switch (dtype) {
+    case FD_DTYPE_F16:
+    case FD_DTYPE_BF16:
+      return 2;
+    case FD_DTYPE_F32:
+      return 4;
+    default:
+      return 0;
+  }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return FD_OK;
+  return fail(FD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Raise the dynamic shared-memory limit of `kernel` once per device.
+int ensure_smem(const void* kernel, int bytes, unsigned long long* done_mask);
+
+}  // namespace fdh

@@ -1,0 +1,396 @@
+"""Torch-level front end of the sm_100a kernels (the C ABI in include/).
+
+Mirrors the reference operator interface of fastdecode/cpu_ops.py and
+fastdecode/csrc/cpu_attn.cpp:
+  load_ext()                          -> object with decode_attn / store_kv /
+                                         set_num_threads / get_num_threads /
+                                         has_avx2, like cpu_ops.load_ext
+                                         (cpu_ops.py:21-46)
+  decode_attn(q, k_cache, v_cache, block_table, lens, scale, out, lse)
+                                      (cpu_attn.cpp:456-489), same argument
+                                      meaning and the same RuntimeError
+                                      checks (:460-477), on device tensors or
+                                      on pinned host caches read over PCIe
+  store_kv(k, v, slots, k_cache, v_cache)
+                                      (cpu_attn.cpp:492-517), range error ->
+                                      RuntimeError (:506-510)
+  merge_attn_states(out, o_a, lse_a, o_b, lse_b)
+                                      vLLM's op as called at backend.py:54-55
+plus the two-tier entry points the backend uses (decode_tiered, store_kv_tiered,
+merge_partials).  Every call is asynchronous on the current CUDA stream.
+There is no CPU path: without the native library or a CUDA device these raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from vllm_fastdecoder_b200 import _native as nat
+
+_DTYPE = {torch.float16: nat.FD_DTYPE_F16, torch.bfloat16: nat.FD_DTYPE_BF16, torch.float32: nat.FD_DTYPE_F32}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE[dt]
+    except KeyError:
+        raise RuntimeError(f"unsupported dtype {dt}") from None
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ------------------------------------------------------------- per-device state
+
+_WS: dict[int, torch.Tensor] = {}
+_ERR: dict[int, torch.Tensor] = {}
+_HOST_PTR: dict[int, int] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Grow-only scratch buffer (256-byte aligned) for split partials."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _WS.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        cap = max(nbytes, 1 << 20, 2 * (buf.numel() if buf is not None else 0))
+        buf = torch.empty(cap, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _WS[idx] = buf
+    return buf
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    """The int32 device error word the kernels on `device` report into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _ERR.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _ERR[idx] = w
+    return w
+
+
+def check_device_errors(device: torch.device | None = None) -> None:
+    """Synchronise and raise RuntimeError if a kernel on `device` flagged an
+    error since the last check (the word is cleared)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    w = error_word(dev)
+    val = ctypes.c_int32(0)
+    nat.check(nat.load().fd_read_error(w.data_ptr(), ctypes.byref(val), 1, _stream(dev)), "fd_read_error")
+    if val.value != 0:
+        raise RuntimeError(f"fastdecode_b200 device error {val.value}: {nat.device_error_string(val.value)}")
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """Device address of t.data_ptr() for a pinned, mapped host tensor (the
+    storage base is translated once and cached; views keep their offset)."""
+    _check(t.device.type == "cpu", "expected a host tensor")
+    _check(t.is_pinned(), "host KV tier must be pinned (pin_memory=True) to be read by the GPU")
+    base = t.untyped_storage().data_ptr()
+    if base not in _HOST_PTR:
+        out = ctypes.c_void_p()
+        nat.check(nat.load().fd_host_device_pointer(base, ctypes.byref(out)), "fd_host_device_pointer")
+        _HOST_PTR[base] = out.value or 0
+    return _HOST_PTR[base] + (t.data_ptr() - base)
+
+
+# ------------------------------------------------------------- KV tiers
+
+
+@dataclass
+class KVTier:
+    """One KV tier viewed as K/V tensors of logical shape [B, KVH, BS, D]
+    (any strides with a contiguous last dim).  Device tensors are streamed
+    with TMA; pinned host tensors are read over PCIe through their mapped
+    device address."""
+
+    k: torch.Tensor
+    v: torch.Tensor
+
+    def __post_init__(self) -> None:
+        _check(self.k.dim() == 4 and self.v.dim() == 4, "KV tier views must be 4-D [B, KVH, BS, D]")
+        _check(self.k.shape == self.v.shape, "K and V views must have the same shape")
+        _check(self.k.stride() == self.v.stride(), "K and V views must have the same strides")
+        _check(self.k.stride(3) == 1, "head_size must be the contiguous dimension")
+        _check(self.k.dtype == self.v.dtype, "K and V dtypes differ")
+
+    @property
+    def host(self) -> bool:
+        return self.k.device.type == "cpu"
+
+    def to_c(self) -> nat.FdKvTier:
+        t = nat.FdKvTier()
+        if self.host:
+            t.k = host_device_pointer(self.k)
+            t.v = host_device_pointer(self.v)
+        else:
+            t.k = self.k.data_ptr()
+            t.v = self.v.data_ptr()
+        s = self.k.stride()
+        t.blk_stride, t.head_stride, t.tok_stride = s[0], s[1], s[2]
+        t.num_blocks = self.k.shape[0]
+        t.host_mapped = 1 if self.host else 0
+        return t
+
+
+def _empty_tier() -> nat.FdKvTier:
+    return nat.FdKvTier()
+
+
+def _tier_device(t: KVTier | None) -> torch.device | None:
+    if t is None or t.host:
+        return None
+    return t.k.device
+
+
+# ------------------------------------------------------------- decode
+
+
+def choose_tiles_per_split(total_tokens: int, n_ctas_per_row: int, block_size: int,
+                           num_sms: int = 148) -> int:
+    """Tiles (min(block_size,16) tokens) per split so that the grid holds about
+    eight waves of two CTAs per SM, given the real token count of the batch."""
+    tt = block_size if block_size <= 16 else 16
+    tiles = max(1, math.ceil(total_tokens / tt)) * max(1, n_ctas_per_row)
+    tps = max(8, math.ceil(tiles / (num_sms * 2 * 8)))
+    return (tps + 3) // 4 * 4
+
+
+def decode_tiered(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tier_split: int,
+                  block_table: torch.Tensor, lens: torch.Tensor, scale: float, out: torch.Tensor,
+                  lse: torch.Tensor | None = None, *, q_rows: torch.Tensor | None = None,
+                  out_rows: torch.Tensor | None = None, max_len: int = 0,
+                  tiles_per_split: int = 0, n: int | None = None) -> None:
+    """Paged decode attention over a two-tier block table (fd_decode_attn).
+
+    q [T, H, D] (rows q_rows[i] or i), tiers[0]/tiers[1] the HBM and host
+    tiers (ids < tier_split and >= tier_split), block_table [n, W] int32,
+    lens [n] int32, out [*, H, D] (rows out_rows[i] or i; q dtype or fp32),
+    lse [H, n] fp32 or None."""
+    lib = nat.load()
+    dev = q.device
+    _check(dev.type == "cuda", "q must be a CUDA tensor")
+    H, D = q.shape[-2], q.shape[-1]
+    _check(q.stride(-1) == 1 and out.stride(-1) == 1, "q and out need a contiguous head dim")
+    n = block_table.shape[0] if n is None else n
+    _check(block_table.dtype == torch.int32 and lens.dtype == torch.int32, "block_table and lens must be int32")
+    _check(block_table.stride(-1) == 1, "block_table rows must be contiguous")
+    _check(block_table.device == dev and lens.device == dev, "block_table and lens must be on q's device")
+    t0, t1 = tiers
+    ref = t0 if t0 is not None else t1
+    _check(ref is not None, "at least one KV tier is required")
+    _check(ref.k.dtype == q.dtype, "q and KV cache dtypes differ")
+    KVH, BS = ref.k.shape[1], ref.k.shape[2]
+    _check(ref.k.shape[3] == D, "head size mismatch")
+    for t in tiers:
+        if t is not None:
+            _check(t.k.shape[1:] == ref.k.shape[1:], "tiers must share [KVH, BS, D]")
+            _check(t.host or t.k.device == dev, "device tier must live on q's device")
+    a = nat.FdDecodeArgs()
+    a.q = q.data_ptr()
+    a.q_stride_n = q.stride(0)
+    a.q_stride_h = q.stride(1)
+    a.q_rows = _ptr(q_rows)
+    a.tier[0] = t0.to_c() if t0 is not None else _empty_tier()
+    a.tier[1] = t1.to_c() if t1 is not None else _empty_tier()
+    a.tier_split = int(tier_split)
+    a.block_table = block_table.data_ptr()
+    a.bt_stride = block_table.stride(0)
+    a.bt_width = block_table.shape[1]
+    a.lens = lens.data_ptr()
+    a.n = n
+    a.num_heads = H
+    a.num_kv_heads = KVH
+    a.head_size = D
+    a.block_size = BS
+    a.scale = float(scale)
+    a.dtype = dtype_code(q.dtype)
+    a.out = out.data_ptr()
+    a.out_dtype = dtype_code(out.dtype)
+    a.out_stride_n = out.stride(0)
+    a.out_stride_h = out.stride(1)
+    a.out_rows = _ptr(out_rows)
+    if lse is not None:
+        _check(lse.dtype == torch.float32 and lse.device == dev, "lse must be fp32 on q's device")
+        a.lse = lse.data_ptr()
+        a.lse_stride_h = lse.stride(0)
+        a.lse_stride_n = lse.stride(1)
+    a.max_len = int(max_len)
+    a.tiles_per_split = int(tiles_per_split)
+    a.error = error_word(dev).data_ptr()
+    need = lib.fd_decode_workspace_size(ctypes.byref(a))
+    if need:
+        ws = workspace(dev, need)
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = ws.numel()
+    nat.check(lib.fd_decode_attn(ctypes.byref(a), _stream(dev)), "fd_decode_attn")
+
+
+def decode_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                block_table: torch.Tensor, lens: torch.Tensor, scale: float,
+                out: torch.Tensor, lse: torch.Tensor) -> None:
+    """Reference signature (fastdecode/csrc/cpu_attn.cpp:456-489).
+
+    q [n,H,D] on the GPU; k_cache/v_cache [C,KVH,BS,D] contiguous, either on
+    the GPU or pinned host memory (the host tier, read over PCIe);
+    block_table [n,W] int32 cache-relative ids; lens [n] int32; out [n,H,D]
+    (q dtype); lse [H,n] fp32."""
+    for t, name in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (block_table, "block_table"),
+                    (lens, "lens"), (out, "out"), (lse, "lse")):
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+    _check(q.dim() == 3 and k_cache.dim() == 4 and v_cache.shape == k_cache.shape,
+           "expected q [n,H,D] and caches [C,KVH,BS,D]")
+    _check(block_table.dtype == torch.int32 and lens.dtype == torch.int32, "block_table and lens must be int32")
+    _check(lse.dtype == torch.float32, "lse must be float32")
+    _check(q.dtype == k_cache.dtype and out.dtype == q.dtype, "q, cache and out dtypes must match")
+    n, H, D = q.shape
+    KVH, BS = k_cache.shape[1], k_cache.shape[2]
+    _check(k_cache.shape[3] == D, "head size mismatch")
+    _check(H % KVH == 0, "num_heads must be a multiple of num_kv_heads")
+    _check(block_table.dim() == 2 and block_table.shape[0] == n and lens.shape[0] == n,
+           "block_table [n, W] and lens [n] expected")
+    _check(out.shape == q.shape and lse.shape == (H, n), "out [n,H,D] and lse [H,n] expected")
+    if n == 0:
+        return
+    _check(q.is_cuda, "q must be a CUDA tensor")
+    dev = q.device
+    bt = block_table if block_table.device == dev else block_table.to(dev, non_blocking=True)
+    ln = lens if lens.device == dev else lens.to(dev, non_blocking=True)
+    decode_tiered(q, (KVTier(k_cache, v_cache), None), 1 << 62, bt, ln, scale, out, lse)
+
+
+# ------------------------------------------------------------- KV write
+
+
+def store_kv_tiered(key: torch.Tensor, value: torch.Tensor, slots: torch.Tensor,
+                    tiers: tuple[KVTier | None, KVTier | None], tier_split_blocks: int) -> None:
+    """Write new K/V rows [m, KVH, D] to slots (int64, -1 = skip) in either tier."""
+    lib = nat.load()
+    dev = key.device
+    _check(dev.type == "cuda", "key must be a CUDA tensor")
+    _check(slots.dtype == torch.int64 and slots.device == dev, "slots must be int64 on key's device")
+    _check(key.stride(-1) == 1 and value.stride(-1) == 1, "key/value need a contiguous head dim")
+    t0, t1 = tiers
+    ref = t0 if t0 is not None else t1
+    _check(ref is not None and key.dtype == ref.k.dtype and value.dtype == key.dtype, "dtype mismatch")
+    m = slots.shape[0]
+    KVH, BS, D = ref.k.shape[1], ref.k.shape[2], ref.k.shape[3]
+    _check(key.shape[1] == KVH and key.shape[2] == D and value.shape[1:] == key.shape[1:],
+           "key/value must be [m, KVH, D]")
+    arr = (nat.FdKvTier * 2)()
+    arr[0] = t0.to_c() if t0 is not None else _empty_tier()
+    arr[1] = t1.to_c() if t1 is not None else _empty_tier()
+    nat.check(lib.fd_store_kv(key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(),
+                              value.stride(0), value.stride(1), slots.data_ptr(), m, KVH, D, BS,
+                              dtype_code(key.dtype), arr, int(tier_split_blocks),
+                              error_word(dev).data_ptr(), _stream(dev)), "fd_store_kv")
+
+
+def store_kv(k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor, k_cache: torch.Tensor,
+             v_cache: torch.Tensor) -> None:
+    """Reference signature (fastdecode/csrc/cpu_attn.cpp:492-517): k, v [m,KVH,D]
+    on the GPU; slots [m] int64 cache-relative; caches [C,KVH,BS,D] on the GPU
+    or pinned host memory.  An out-of-range slot raises RuntimeError and
+    nothing is written."""
+    for t, name in ((k, "k"), (v, "v"), (slots, "slots"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+    _check(slots.dtype == torch.int64, "slots must be int64")
+    _check(k.dtype == k_cache.dtype and v.dtype == k.dtype, "dtype mismatch")
+    m = k.shape[0]
+    if m == 0:
+        return
+    C, KVH, BS, D = k_cache.shape
+    _check(k.shape[1] == KVH and k.shape[2] == D and v.shape == k.shape, "k/v must be [m, KVH, D]")
+    cap = C * BS
+    if slots.device.type == "cpu":
+        bad = (slots < 0) | (slots >= cap)
+        if bool(bad.any()):
+            raise RuntimeError(f"CPU slot out of range: {int(slots[bad][0])}")
+        slots = slots.to(k.device, non_blocking=True)
+    dev = k.device
+    store_kv_tiered(k, v, slots, (KVTier(k_cache, v_cache), None), 1 << 62)
+    if not torch.cuda.is_current_stream_capturing():
+        try:
+            check_device_errors(dev)
+        except RuntimeError as e:
+            raise RuntimeError(f"CPU slot out of range ({e})") from None
+
+
+# ------------------------------------------------------------- merge
+
+
+def merge_attn_states(out: torch.Tensor, o_a: torch.Tensor, lse_a: torch.Tensor, o_b: torch.Tensor,
+                      lse_b: torch.Tensor, out_lse: torch.Tensor | None = None,
+                      out_rows: torch.Tensor | None = None) -> None:
+    """vLLM merge_attn_states(output, prefix_output, prefix_lse, suffix_output,
+    suffix_lse) with the reference's rule (fastdecode/cpu_ops.py:93-113).
+    o_a/o_b [n,H,D] contiguous, lse [H,n] fp32; out rows out_rows[i] or i."""
+    _check(o_a.shape == o_b.shape and o_a.dtype == o_b.dtype, "o_a and o_b must match")
+    _check(o_a.is_contiguous() and o_b.is_contiguous(), "partials must be contiguous")
+    n, H, D = o_a.shape
+    _check(lse_a.shape == (H, n) and lse_b.shape == (H, n), "lse must be [H, n]")
+    _check(lse_a.dtype == torch.float32 and lse_b.dtype == torch.float32, "lse must be float32")
+    _check(lse_a.is_contiguous() and lse_b.is_contiguous(), "lse must be contiguous")
+    _check(out.stride(-1) == 1 and out.stride(1) == D, "out rows must be [H, D] contiguous")
+    dev = o_a.device
+    nat.check(nat.load().fd_merge_attn_states(
+        out.data_ptr(), dtype_code(out.dtype), out.stride(0), _ptr(out_rows), _ptr(out_lse),
+        o_a.data_ptr(), lse_a.data_ptr(), o_b.data_ptr(), lse_b.data_ptr(), dtype_code(o_a.dtype),
+        n, H, D, _stream(dev)), "fd_merge_attn_states")
+
+
+def merge_partials(parts: torch.Tensor, num_parts: int, n: int, H: int, D: int, out: torch.Tensor,
+                   out_lse: torch.Tensor | None = None) -> None:
+    """P-way merge of packed fp32 partials: part p occupies parts[p] =
+    [o (n*H*D) | lse (H*n)]."""
+    _check(parts.dtype == torch.float32 and parts.is_contiguous(), "parts must be contiguous fp32")
+    stride = n * H * D + H * n
+    _check(parts.numel() >= num_parts * stride, "parts buffer too small")
+    _check(out.is_contiguous() and out.shape == (n, H, D), "out must be [n, H, D] contiguous")
+    base = parts.data_ptr()
+    nat.check(nat.load().fd_merge_partials(
+        base, base + 4 * n * H * D, stride, num_parts, n, H, D, out.data_ptr(), dtype_code(out.dtype),
+        _ptr(out_lse), _stream(parts.device)), "fd_merge_partials")
+
+
+# ------------------------------------------------------------- load_ext shim
+
+
+class _Ext:
+    """Object returned by load_ext(), shaped like the reference's pybind
+    module (fastdecode/csrc/cpu_attn.cpp:531-537)."""
+
+    decode_attn = staticmethod(decode_attn)
+    store_kv = staticmethod(store_kv)
+    merge_attn_states = staticmethod(merge_attn_states)
+
+    @staticmethod
+    def set_num_threads(n: int) -> None:  # the GPU path has no host thread pool
+        del n
+
+    @staticmethod
+    def get_num_threads() -> int:
+        return 1
+
+    @staticmethod
+    def has_avx2() -> bool:  # no host SIMD kernel exists in this engine
+        return False
+
+
+def load_ext(verbose: bool = False) -> _Ext:
+    """Load the native library; raises if it is missing (no fallback)."""
+    del verbose
+    nat.load()
+    return _Ext()
