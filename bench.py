@@ -1,0 +1,511 @@
+"""Benchmark of the paged decode-attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c0|c2|c3]
+
+Under torchrun (N > 1) there is one process per GPU.
+
+A step is one decode-attention pass over one synthetic batch (see
+vllm_fastdecoder_b200/workloads.py):
+  c1 (default)  GPU/host split: 64 rows of U[256,4096] tokens, 32/32 heads,
+                fp16, HBM tier of 2048 blocks, the rest in pinned host memory;
+                N > 1 runs N independent replicas (weak scaling)
+  c0            16 rows, one 4096-block HBM pool (the reference's CPU case)
+  c2            GQA 32/8 bf16, 256 rows, lognormal lengths, all HBM
+  c3            8 rows x 131072 tokens, GQA bf16, KV sharded over the N GPUs,
+                partials all-gathered over NCCL and LSE-merged (strong scaling)
+
+Reported: `value` = rows/s with inputs resident (device-timed, CUDA events,
+max over ranks); `e2e` = the same through the public API with the step's q /
+block table / lengths copied in from pinned host memory and o / lse copied
+back every step; `roofline` = algorithmic bytes of the decode kernel per
+launch / its event-timed duration, against the measured HBM copy peak (and,
+for the host tier, the pinned host->device copy rate measured in the same
+run); `cpu_baseline` = the reference's own AVX2 kernel (compiled from its
+source into oracle/_ref) on this host's cores.
+`--impl reference` times only that reference CPU kernel on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "decode-attn seqs/s"
+UNIT = "seqs/s"
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _traffic(kernel: str, workload: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(f"{kernel}/{workload}")
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        pr = torch.cuda.get_device_properties(device)
+        self.bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.bus, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- helpers
+
+
+def pcie_h2d_gbs(device: torch.device, nbytes: int = 1 << 30) -> float:
+    """Pinned host -> device copy rate (the PCIe roofline of the host tier)."""
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize(device)
+    best = 0.0
+    for _ in range(3):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        d.copy_(h, non_blocking=True)
+        e.record()
+        e.synchronize()
+        best = max(best, nbytes / (s.elapsed_time(e) * 1e-3) / 1e9)
+    del h, d
+    return best
+
+
+def host_part(batch):
+    """The reference's CPU leg of a step: host-tier rows of the batch with
+    host-relative, compacted block ids (what its planner feeds decode_attn,
+    fastdecode/plan.py:157-160)."""
+    n, BS, G = batch.n, batch.BS, batch.G
+    rows, lens = [], []
+    for i in range(n):
+        L = int(batch.lens[i])
+        nb = (L + BS - 1) // BS
+        ids, toks = [], 0
+        for j in range(nb):
+            b = int(batch.block_table[i, j])
+            if b >= G:
+                ids.append(b - G)
+                toks += BS if j < nb - 1 else L - (nb - 1) * BS
+        rows.append(ids)
+        lens.append(toks)
+    W = max(1, max(len(r) for r in rows))
+    bt = torch.zeros(n, W, dtype=torch.int32)
+    for i, r in enumerate(rows):
+        if r:
+            bt[i, :len(r)] = torch.tensor(r, dtype=torch.int32)
+    return bt, torch.tensor(lens, dtype=torch.int32)
+
+
+def reference_inputs(batch, resident=None, rows: int | None = None):
+    """CPU tensors in the reference layout for its decode_attn: q [n,H,D],
+    caches [C,KVH,BS,D], table, lens.  For c1 the cache is the pinned host
+    tier itself and the table covers its host blocks only."""
+    n = batch.n if rows is None else rows
+    if batch.num_host_blocks > 0:
+        assert resident is not None
+        hk, hv = resident.tiers[1].k, resident.tiers[1].v
+        bt, lens = host_part(batch)
+        q = resident.q[:n].cpu()
+        return q, hk, hv, bt[:n].contiguous(), lens[:n].contiguous()
+    g = torch.Generator().manual_seed(batch.seed + 7)
+    bt = batch.block_table[:n].contiguous()
+    lens = batch.lens[:n].contiguous()
+    used = sorted({int(x) for i in range(n) for x in bt[i, :(int(lens[i]) + batch.BS - 1) // batch.BS]})
+    remap = {b: k for k, b in enumerate(used)}
+    bt2 = torch.zeros_like(bt)
+    for i in range(n):
+        nb = (int(lens[i]) + batch.BS - 1) // batch.BS
+        bt2[i, :nb] = torch.tensor([remap[int(x)] for x in bt[i, :nb]], dtype=torch.int32)
+    shape = (len(used), batch.KVH, batch.BS, batch.D)
+    kc = torch.empty(shape, dtype=batch.dtype)
+    vc = torch.empty(shape, dtype=batch.dtype)
+    kc.normal_(generator=g)
+    vc.normal_(generator=g)
+    q = torch.randn(n, batch.H, batch.D, generator=g).to(batch.dtype)
+    return q, kc, vc, bt2, lens
+
+
+def time_reference(batch, resident, steps: int, warmup: int, rows: int | None = None,
+                   budget_s: float | None = None):
+    """Median seconds per call of the reference AVX2 decode_attn with all host
+    threads.  Returns (seconds, threads, rows, kind)."""
+    from oracle import oracle as O
+
+    ext = O.load_reference_ext()
+    kind = "reference"
+    q, kc, vc, bt, lens = reference_inputs(batch, resident, rows)
+    H, n = q.shape[1], q.shape[0]
+    out = torch.empty_like(q)
+    lse = torch.empty(H, n, dtype=torch.float32)
+    threads = os.cpu_count() or 1
+    if ext is not None:
+        ext.set_num_threads(threads)
+        fn = lambda: ext.decode_attn(q, kc, vc, bt, lens, batch.scale, out, lse)  # noqa: E731
+    else:  # the C restatement, single-threaded
+        kind, threads = "port", 1
+        fn = lambda: O.decode_attn(q, kc, vc, bt, lens, batch.scale, out, lse)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    times = []
+    t_end = time.perf_counter() + (budget_s if budget_s else 1e9)
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 3:
+            break
+    return statistics.median(times), threads, n, kind
+
+
+# ---------------------------------------------------------------- our arm
+
+
+def run_ours(args, ws, rank, device):
+    from vllm_fastdecoder_b200 import gpu_ops, workloads
+
+    dist = ws > 1
+    if args.workload == "c3":
+        batch = workloads.config3(world=ws, rank=rank)
+    else:
+        batch = workloads.CONFIGS[args.workload]()
+    res = workloads.materialize(batch, device)
+    n, H, D = batch.n, batch.H, batch.D
+    sharded = args.workload == "c3" and ws > 1
+    gather = None
+    if sharded:
+        from vllm_fastdecoder_b200 import sharded as sh
+
+        gather = sh.PartialExchange(n, H, D, ws, device)
+        final = torch.empty(n, H, D, dtype=batch.dtype, device=device)
+        out, lse = gather.o_view, gather.lse_view
+    else:
+        out = torch.empty(n, H, D, dtype=batch.dtype, device=device)
+        lse = torch.empty(H, n, dtype=torch.float32, device=device)
+    tps = gpu_ops.choose_tiles_per_split(int(batch.lens.sum()), batch.KVH, batch.BS)
+    max_len = int(batch.lens.max())
+    a = gpu_ops.decode_args(res.q, res.tiers, batch.G, res.block_table, res.lens, batch.scale, out, lse,
+                            max_len=max_len, tiles_per_split=tps)
+    has_combine = a.workspace_bytes > 0
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record()
+        gpu_ops.launch_decode(a, device, "partials")
+        if ev is not None:
+            ev[1].record()
+        if has_combine:
+            gpu_ops.launch_decode(a, device, "combine")
+        if gather is not None:
+            gather.exchange_and_merge(out, lse, final)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    gpu_ops.check_device_errors(device)
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(device)
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    clocks.start()
+    time.sleep(0.25)  # let nvidia-smi take its first sample before the region
+    t_start.record()
+    for k in range(args.steps):
+        step(evs[k])
+    t_end.record()
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    if dist:
+        torch.distributed.barrier()
+    gpu_ops.check_device_errors(device)
+    elapsed = t_start.elapsed_time(t_end) * 1e-3
+    kern = sorted(e0.elapsed_time(e1) * 1e-3 for e0, e1 in evs)
+    kern_t = sum(kern) / len(kern)
+    if dist:
+        t = torch.tensor([elapsed, kern_t], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed, kern_t = float(t[0]), float(t[1])
+
+    rows_per_step = n if args.workload == "c3" else n * ws
+    value = rows_per_step * args.steps / elapsed
+
+    # ---- end to end through the public API: inputs from pinned host memory
+    h_q = res.q.cpu().pin_memory()
+    h_bt = batch.block_table.pin_memory()
+    h_lens = batch.lens.pin_memory()
+    h_out = torch.empty(out.shape, dtype=batch.dtype, pin_memory=True)
+    h_lse = torch.empty(H, n, dtype=torch.float32, pin_memory=True)
+    d_q = torch.empty_like(res.q)
+    d_bt = torch.empty_like(res.block_table)
+    d_lens = torch.empty_like(res.lens)
+    e_out = out if not sharded else final
+
+    def e2e_step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_bt.copy_(h_bt, non_blocking=True)
+        d_lens.copy_(h_lens, non_blocking=True)
+        gpu_ops.decode_tiered(d_q, res.tiers, batch.G, d_bt, d_lens, batch.scale, out, lse,
+                              max_len=max_len, tiles_per_split=tps)
+        if gather is not None:
+            gather.exchange_and_merge(out, lse, final)
+        h_out.copy_(e_out, non_blocking=True)
+        h_lse.copy_(lse if gather is None else gather.lse_out, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    if dist:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_t = e0.elapsed_time(e1) * 1e-3
+    if dist:
+        t = torch.tensor([e2e_t], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_t = float(t[0])
+    gpu_ops.check_device_errors(device)
+    h2d = h_q.numel() * h_q.element_size() + h_bt.numel() * 4 + h_lens.numel() * 4
+    d2h = h_out.numel() * h_out.element_size() + h_lse.numel() * 4
+
+    # ---- roofline of the decode kernel (per launch, this rank's batch)
+    peaks = _peaks()
+    hbm_b, host_b = batch.kv_bytes()
+    step_b = batch.step_bytes()
+    achieved = step_b / kern_t / 1e9
+    roof = {"unit": "GB/s", "achieved": round(achieved, 1), "traffic": _traffic("fd_decode_kernel", args.workload),
+            "kernel": "fd_decode_kernel", "algorithmic_bytes_per_launch": step_b,
+            "kernel_ms": round(kern_t * 1e3, 4)}
+    if host_b > 0:
+        pcie = pcie_h2d_gbs(device)
+        t_ideal = (step_b - host_b) / (peaks["hbm_gbs"] * 1e9) + host_b / (pcie * 1e9)
+        roof.update({"bound": "hbm+pcie", "peak": round(step_b / t_ideal / 1e9, 1),
+                     "frac": round(t_ideal / kern_t, 4),
+                     "peak_note": f"bytes at their tier's rate: HBM {peaks['hbm_gbs']} GB/s "
+                                  f"({peaks['source']}), host tier {pcie:.1f} GB/s (pinned H2D copy "
+                                  "measured in this run)",
+                     "hbm_bytes": step_b - host_b, "host_bytes": host_b})
+    else:
+        roof.update({"bound": "hbm", "peak": peaks["hbm_gbs"], "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_note": f"HBM copy bandwidth, {peaks['source']} (burst figure)"})
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "strong" if args.workload == "c3" else "weak", "vs_baseline": None, "dtype": _dtype_name(batch.dtype),
+        "data": "synthetic (seeded N(0,1) q/K/V, configuration shapes)",
+        "config": _config(batch, args, ws, tps, has_combine),
+        "kv_gbs": round((hbm_b + host_b) * (1 if args.workload == "c3" else ws) * args.steps / elapsed / 1e9, 1),
+        "e2e": {"value": round(rows_per_step * args.steps / e2e_t, 2), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "vllm_fastdecoder_b200.gpu_ops.decode_tiered (C ABI fd_decode_attn)"},
+        "roofline": roof,
+        "clocks": clk,
+        "gpu_launches": args.steps * (1 + int(has_combine) + (1 if gather is not None else 0)),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        rows = None if args.workload != "c3" else 1
+        t, th, r, kind = time_reference(batch, res, steps=30, warmup=3, rows=rows, budget_s=20.0)
+        line["cpu_baseline"] = {
+            "value": round(r / t, 2), "unit": UNIT, "cores": th, "kind": kind,
+            "sample": _sample_text(batch, r),
+            "cpu": _cpu_model(),
+        }
+    return line
+
+
+def _dtype_name(dt) -> str:
+    return {torch.float16: "fp16", torch.bfloat16: "bf16", torch.float32: "fp32"}[dt]
+
+
+def _cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _sample_text(batch, rows) -> str:
+    if batch.num_host_blocks > 0:
+        _, host_b = batch.kv_bytes()
+        return (f"the reference's CPU leg of one {batch.name} step: decode_attn over the host-tier blocks of "
+                f"all {batch.n} rows ({host_b / 1e9:.3f} GB of host KV), median of up to 30 calls")
+    return f"decode_attn over {rows} of the {batch.n} rows of one {batch.name} step, median of up to 30 calls"
+
+
+def _config(batch, args, ws, tps, has_combine) -> dict:
+    hbm_b, host_b = batch.kv_bytes()
+    return {
+        "workload": {
+            "c1": "GPU/host split with LSE merge (config 1): 64 rows, ctx U[256,4096], 32/32 heads, D128, fp16, "
+                  "BS16, HBM tier 2048 blocks, per-row host fraction {0,.25,.5,.75,1}",
+            "c0": "single-layer paged decode (config 0): 16 rows, ctx U[64,2048], 32/32 heads, D128, fp16, "
+                  "4096-block pool",
+            "c2": "GQA decode (config 2): 256 rows, ctx lognormal(median 1024, sigma 0.75) clip [32,8192], "
+                  "32/8 heads, D128, bf16",
+            "c3": f"long-context sharded decode (config 3): 8 rows x 131072 ctx, 32/8 heads, D128, bf16, "
+                  f"KV sharded over {ws} GPU(s), NCCL all-gather + LSE merge",
+        }[args.workload],
+        "rows": batch.n, "heads": batch.H, "kv_heads": batch.KVH, "head_size": batch.D, "block_size": batch.BS,
+        "hbm_kv_bytes": hbm_b, "host_kv_bytes": host_b, "hbm_layout": batch.hbm_layout,
+        "tiles_per_split": tps, "split_combine": has_combine,
+        "l2": "no flush: each step streams more KV than the 126 MB L2" if hbm_b + host_b > (126 << 20)
+              else "KV smaller than L2",
+        "parallelism": f"replicas x{ws}" if args.workload != "c3" else f"kv-shard x{ws}",
+    }
+
+
+# ---------------------------------------------------------------- reference arm
+
+
+def run_reference(args, ws, rank, device):
+    from vllm_fastdecoder_b200 import workloads
+
+    if args.workload == "c3":
+        batch = workloads.config3(world=1, rank=0)
+    else:
+        batch = workloads.CONFIGS[args.workload]()
+    res = workloads.materialize(batch, device) if batch.num_host_blocks > 0 else None
+    t, th, r, kind = time_reference(batch, res, steps=args.steps, warmup=args.warmup)
+    v = round(r / t, 2)
+    return {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "impl": "reference",
+        "scaling": "weak", "vs_baseline": None, "dtype": _dtype_name(batch.dtype),
+        "data": "synthetic (seeded N(0,1) q/K/V, configuration shapes)",
+        "config": _config(batch, args, 1, 0, False),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": th, "kind": kind, "sample": _sample_text(batch, r),
+                         "cpu": _cpu_model()},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's AVX2 decode_attn (fastdecode/csrc/cpu_attn.cpp) compiled from its source, "
+                "timed on this host; for c1 only its CPU leg (host-tier blocks) is timed, its GPU "
+                "FlashAttention leg would run concurrently",
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=0)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3"], default="c1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.steps <= 0:
+        args.steps = {"c1": 60, "c0": 400, "c2": 200, "c3": 100}[args.workload]
+    args.warmup = max(3, args.warmup)
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        device = torch.device("cuda", local) if torch.cuda.is_available() else None
+        if device is not None:
+            torch.cuda.set_device(device)
+        print(json.dumps(run_reference(args, ws, rank, device)), flush=True)
+        return 0
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if ws > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    try:
+        line = run_ours(args, ws, rank, device)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -154,6 +154,18 @@ FD_API size_t fd_decode_workspace_size(const fd_decode_args *a);
  * the unified table covers both tiers. */
 FD_API int fd_decode_attn(const fd_decode_args *a, void *stream);
 
+/* The two launches fd_decode_attn makes, for callers that want to place
+ * other work (or timing events) between them:
+ *   fd_decode_attn_partials  the split-KV kernel; rows that fit in one split
+ *                            are final after it, others leave fp32 partials
+ *                            in the workspace
+ *   fd_decode_attn_combine   the log-sum-exp combine of those partials
+ * Both take the same arguments; calling them in order on one stream equals
+ * fd_decode_attn.  fd_decode_attn_combine launches nothing when every row
+ * fits in one split. */
+FD_API int fd_decode_attn_partials(const fd_decode_args *a, void *stream);
+FD_API int fd_decode_attn_combine(const fd_decode_args *a, void *stream);
+
 /* Drop-in for the reference pybind op
  *   decode_attn(q, k_cache, v_cache, block_table, lens, scale, out, lse)
  * (fastdecode/csrc/cpu_attn.cpp:456-489): contiguous q [n,H,D], caches

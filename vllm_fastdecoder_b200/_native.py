@@ -54,6 +54,8 @@ class FdDecodeArgs(ctypes.Structure):
 SIGNATURES = {
     "fd_decode_workspace_size": (c_size_t, [POINTER(FdDecodeArgs)]),
     "fd_decode_attn": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
+    "fd_decode_attn_partials": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
+    "fd_decode_attn_combine": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
     "fd_decode_attn_paged": (c_int32, [
         c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_int32,
         c_int32, c_int32, c_int64, c_int32, c_float, c_int32, c_void_p, c_void_p, c_void_p,

@@ -609,7 +609,11 @@ extern "C" size_t fd_decode_workspace_size(const fd_decode_args* a) {
   return g.ws_bytes;
 }
 
-extern "C" int fd_decode_attn(const fd_decode_args* a, void* stream) {
+namespace {
+
+// Validate `a` and fill the kernel parameters; launch_main / launch_combine
+// select which of the two kernels run.
+int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool launch_combine) {
   if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_decode_attn: null args");
   if (a->n < 0) return fdh::fail(FD_ERR_INVALID, "n must be >= 0");
   if (a->n == 0) return FD_OK;
@@ -691,12 +695,14 @@ extern "C" int fd_decode_attn(const fd_decode_args* a, void* stream) {
   }
   if ((int64_t)a->num_kv_heads * g.gcs > 65535)
     return fdh::fail(FD_ERR_UNSUPPORTED, "too many heads for the grid");
-  launch_fn fn = pick_kernel(a->dtype, D, g.GQ);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 grid(g.max_splits, a->num_kv_heads * g.gcs, a->n);
-  st = fn(p, grid, s);
-  if (st != FD_OK) return st;
-  if (g.max_splits > 1) {
+  if (launch_main) {
+    launch_fn fn = pick_kernel(a->dtype, D, g.GQ);
+    dim3 grid(g.max_splits, a->num_kv_heads * g.gcs, a->n);
+    st = fn(p, grid, s);
+    if (st != FD_OK) return st;
+  }
+  if (launch_combine && g.max_splits > 1) {
     const int threads = D <= 128 ? 128 : 256;
     const size_t sm = (size_t)g.max_splits * sizeof(float);
     if (sm > 48 * 1024) return fdh::fail(FD_ERR_UNSUPPORTED, "too many splits (%d)", g.max_splits);
@@ -704,6 +710,20 @@ extern "C" int fd_decode_attn(const fd_decode_args* a, void* stream) {
     st = fdh::cuda_status(cudaGetLastError(), "fd_split_merge_kernel launch");
   }
   return st;
+}
+
+}  // namespace
+
+extern "C" int fd_decode_attn(const fd_decode_args* a, void* stream) {
+  return decode_impl(a, stream, true, true);
+}
+
+extern "C" int fd_decode_attn_partials(const fd_decode_args* a, void* stream) {
+  return decode_impl(a, stream, true, false);
+}
+
+extern "C" int fd_decode_attn_combine(const fd_decode_args* a, void* stream) {
+  return decode_impl(a, stream, false, true);
 }
 
 namespace {

@@ -168,17 +168,13 @@ def choose_tiles_per_split(total_tokens: int, n_ctas_per_row: int, block_size: i
     return (tps + 3) // 4 * 4
 
 
-def decode_tiered(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tier_split: int,
-                  block_table: torch.Tensor, lens: torch.Tensor, scale: float, out: torch.Tensor,
-                  lse: torch.Tensor | None = None, *, q_rows: torch.Tensor | None = None,
-                  out_rows: torch.Tensor | None = None, max_len: int = 0,
-                  tiles_per_split: int = 0, n: int | None = None) -> None:
-    """Paged decode attention over a two-tier block table (fd_decode_attn).
-
-    q [T, H, D] (rows q_rows[i] or i), tiers[0]/tiers[1] the HBM and host
-    tiers (ids < tier_split and >= tier_split), block_table [n, W] int32,
-    lens [n] int32, out [*, H, D] (rows out_rows[i] or i; q dtype or fp32),
-    lse [H, n] fp32 or None."""
+def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tier_split: int,
+                block_table: torch.Tensor, lens: torch.Tensor, scale: float, out: torch.Tensor,
+                lse: torch.Tensor | None = None, *, q_rows: torch.Tensor | None = None,
+                out_rows: torch.Tensor | None = None, max_len: int = 0,
+                tiles_per_split: int = 0, n: int | None = None) -> nat.FdDecodeArgs:
+    """Validate and pack the arguments of fd_decode_attn (workspace included).
+    The tensors must stay alive, unmoved, while the returned args are used."""
     lib = nat.load()
     dev = q.device
     _check(dev.type == "cuda", "q must be a CUDA tensor")
@@ -235,7 +231,30 @@ def decode_tiered(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], t
         ws = workspace(dev, need)
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
-    nat.check(lib.fd_decode_attn(ctypes.byref(a), _stream(dev)), "fd_decode_attn")
+    return a
+
+
+def launch_decode(a: nat.FdDecodeArgs, device: torch.device, phase: str = "all") -> None:
+    """Launch fd_decode_attn ("all") or one of its two kernels ("partials",
+    "combine") on the current stream of `device`."""
+    lib = nat.load()
+    fn = {"all": lib.fd_decode_attn, "partials": lib.fd_decode_attn_partials,
+          "combine": lib.fd_decode_attn_combine}[phase]
+    nat.check(fn(ctypes.byref(a), _stream(device)), f"fd_decode_attn[{phase}]")
+
+
+def decode_tiered(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tier_split: int,
+                  block_table: torch.Tensor, lens: torch.Tensor, scale: float, out: torch.Tensor,
+                  lse: torch.Tensor | None = None, **kw) -> None:
+    """Paged decode attention over a two-tier block table (fd_decode_attn).
+
+    q [T, H, D] (rows q_rows[i] or i), tiers[0]/tiers[1] the HBM and host
+    tiers (ids < tier_split and >= tier_split), block_table [n, W] int32,
+    lens [n] int32, out [*, H, D] (rows out_rows[i] or i; q dtype or fp32),
+    lse [H, n] fp32 or None.  Keywords: q_rows, out_rows, max_len,
+    tiles_per_split, n (see decode_args)."""
+    a = decode_args(q, tiers, tier_split, block_table, lens, scale, out, lse, **kw)
+    launch_decode(a, q.device)
 
 
 def decode_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

@@ -61,6 +61,12 @@ class HostPlan:
     pd_tok: torch.Tensor = field(default_factory=lambda: torch.zeros(0, dtype=_I64))
     pd_seq_lens: torch.Tensor = field(default_factory=lambda: torch.zeros(0, dtype=_I32))
     pd_max_len: int = 0
+    pp_req: torch.Tensor = field(default_factory=lambda: torch.zeros(0, dtype=_I64))  # P prefills
+    pp_tok: torch.Tensor = field(default_factory=lambda: torch.zeros(0, dtype=_I64))
+    pp_cu: torch.Tensor = field(default_factory=lambda: torch.zeros(1, dtype=_I32))
+    pp_seqlens: torch.Tensor = field(default_factory=lambda: torch.zeros(0, dtype=_I32))
+    pp_max_q: int = 0
+    pp_max_k: int = 0
     num_gpu_blocks: int = 0
     block_size: int = 0
 
@@ -190,6 +196,9 @@ def build_host_plan(
     f_q = q_len[f_req]
 
     pd_req = (cls_p & (q_len == 1)).nonzero().flatten()
+    pp_req = (cls_p & (q_len > 1)).nonzero().flatten()
+    pp_q = q_len[pp_req]
+    pp_seq = seq[pp_req].to(_I32)
     s_seq = seq[s_req].to(_I32)
     pd_seq = seq[pd_req].to(_I32)
 
@@ -220,6 +229,12 @@ def build_host_plan(
         pd_tok=qsl[pd_req],
         pd_seq_lens=pd_seq,
         pd_max_len=int(pd_seq.max()) if pd_seq.numel() else 0,
+        pp_req=pp_req,
+        pp_tok=spans(qsl[pp_req], pp_q),
+        pp_cu=prefix_offsets(pp_q),
+        pp_seqlens=pp_seq,
+        pp_max_q=int(pp_q.max()) if pp_q.numel() else 0,
+        pp_max_k=int(pp_seq.max()) if pp_seq.numel() else 0,
         num_gpu_blocks=G,
         block_size=bs,
     )
@@ -253,6 +268,10 @@ class DevicePlan:
     pd_seq_lens: torch.Tensor | None = None
     s_cpu_bt: torch.Tensor | None = None  # host-relative compacted table on the device
     s_cpu_lens: torch.Tensor | None = None
+    pp_tok: torch.Tensor | None = None
+    pp_cu: torch.Tensor | None = None
+    pp_seqlens: torch.Tensor | None = None
+    pp_bt: torch.Tensor | None = None
 
 
 def to_device(hp: HostPlan, block_table_dev: torch.Tensor, device) -> DevicePlan:
@@ -298,4 +317,8 @@ def to_device(hp: HostPlan, block_table_dev: torch.Tensor, device) -> DevicePlan
         pd_seq_lens=put(hp.pd_seq_lens),
         s_cpu_bt=put(hp.s_cpu_bt),
         s_cpu_lens=put(hp.s_cpu_lens),
+        pp_tok=put(hp.pp_tok),
+        pp_cu=put(hp.pp_cu),
+        pp_seqlens=put(hp.pp_seqlens),
+        pp_bt=rows(hp.pp_req),
     )
