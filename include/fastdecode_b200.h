@@ -166,6 +166,35 @@ FD_API int fd_decode_attn(const fd_decode_args *a, void *stream);
 FD_API int fd_decode_attn_partials(const fd_decode_args *a, void *stream);
 FD_API int fd_decode_attn_combine(const fd_decode_args *a, void *stream);
 
+/* Size of the scratch array built into the library for
+ * fd_decode_attn_noalloc (32 MiB of device memory on every GPU that loads
+ * the library, held until the process exits). */
+#define FD_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* fd_decode_attn for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference.
+ *
+ * Some callers of this kernel must not call cudaMalloc: code that runs after
+ * vLLM has sized its KV cache to fill the memory its profiler left free (a
+ * late allocation can fail), code inside a framework that owns all device
+ * memory through its own allocator, and loops where cudaMalloc / cudaFree
+ * would synchronise the device.  This entry point takes the same arguments
+ * as fd_decode_attn but ignores `workspace` / `workspace_bytes`: the split
+ * partials go to a file-scope __device__ array of FD_NOALLOC_SCRATCH_BYTES
+ * inside the library, so it calls no cudaMalloc, cudaFree or other allocating
+ * routine.  Arguments whose partials would not fit (fd_decode_workspace_size()
+ * larger than FD_NOALLOC_SCRATCH_BYTES) are rejected with FD_ERR_WORKSPACE
+ * before anything is launched; a larger tiles_per_split needs less scratch.
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and caches it; make that
+ * first call before any stream capture.  All calls share the one array and it
+ * keeps the last call's contents; nothing in it needs to start at zero (every
+ * partial is written by its split before the combine reads it).  Calls whose
+ * executions overlap on the GPU (other streams of the same device) race on
+ * the array: order them, e.g. on one stream. */
+FD_API int fd_decode_attn_noalloc(const fd_decode_args *a, void *stream);
+
 /* Drop-in for the reference pybind op
  *   decode_attn(q, k_cache, v_cache, block_table, lens, scale, out, lse)
  * (fastdecode/csrc/cpu_attn.cpp:456-489): contiguous q [n,H,D], caches

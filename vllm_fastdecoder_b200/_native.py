@@ -20,6 +20,8 @@ FD_DTYPE_BF16 = 1
 FD_DTYPE_F32 = 2
 
 FD_OK = 0
+FD_ERR_WORKSPACE = 4
+NOALLOC_SCRATCH_BYTES = 32 << 20  # FD_NOALLOC_SCRATCH_BYTES
 STATUS_NAMES = {
     1: "FD_ERR_INVALID", 2: "FD_ERR_UNSUPPORTED", 3: "FD_ERR_ALIGN",
     4: "FD_ERR_WORKSPACE", 5: "FD_ERR_CUDA", 6: "FD_ERR_RANGE",
@@ -56,6 +58,7 @@ SIGNATURES = {
     "fd_decode_attn": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
     "fd_decode_attn_partials": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
     "fd_decode_attn_combine": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
+    "fd_decode_attn_noalloc": (c_int32, [POINTER(FdDecodeArgs), c_void_p]),
     "fd_decode_attn_paged": (c_int32, [
         c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_int32,
         c_int32, c_int32, c_int64, c_int32, c_float, c_int32, c_void_p, c_void_p, c_void_p,

@@ -23,6 +23,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "fd_common.cuh"
 #include "fd_internal.h"
@@ -613,7 +614,8 @@ namespace {
 
 // Validate `a` and fill the kernel parameters; launch_main / launch_combine
 // select which of the two kernels run.
-int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool launch_combine) {
+int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool launch_combine,
+                void* ws_override = nullptr, size_t ws_override_bytes = 0) {
   if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_decode_attn: null args");
   if (a->n < 0) return fdh::fail(FD_ERR_INVALID, "n must be >= 0");
   if (a->n == 0) return FD_OK;
@@ -683,15 +685,16 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
   p.lse_sn = a->lse_stride_n;
   p.err = a->error;
   if (g.max_splits > 1) {
-    if (a->workspace == nullptr || a->workspace_bytes < g.ws_bytes)
-      return fdh::fail(FD_ERR_WORKSPACE, "workspace of %zu bytes needed, got %zu", g.ws_bytes,
-                       a->workspace_bytes);
-    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+    void* ws = ws_override != nullptr ? ws_override : a->workspace;
+    const size_t ws_bytes = ws_override != nullptr ? ws_override_bytes : a->workspace_bytes;
+    if (ws == nullptr || ws_bytes < g.ws_bytes)
+      return fdh::fail(FD_ERR_WORKSPACE, "workspace of %zu bytes needed, got %zu", g.ws_bytes, ws_bytes);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
       return fdh::fail(FD_ERR_ALIGN, "workspace must be 256-byte aligned");
     const size_t rows = (size_t)a->n * (size_t)a->num_heads * (size_t)g.max_splits;
     const size_t o_bytes = (rows * (size_t)D * 4 + 255) / 256 * 256;
-    p.part_o = static_cast<float*>(a->workspace);
-    p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(a->workspace) + o_bytes);
+    p.part_o = static_cast<float*>(ws);
+    p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + o_bytes);
   }
   if ((int64_t)a->num_kv_heads * g.gcs > 65535)
     return fdh::fail(FD_ERR_UNSUPPORTED, "too many heads for the grid");
@@ -725,6 +728,58 @@ extern "C" int fd_decode_attn_partials(const fd_decode_args* a, void* stream) {
 extern "C" int fd_decode_attn_combine(const fd_decode_args* a, void* stream) {
   return decode_impl(a, stream, false, true);
 }
+
+// ------------------------------------------------------------ no-allocation variant
+
+// Scratch of fd_decode_attn_noalloc: a file-scope device array, so the entry
+// point needs no cudaMalloc.  Every GPU that loads this library holds these
+// FD_NOALLOC_SCRATCH_BYTES until the process exits.  In host code the name is
+// only a handle for cudaGetSymbolAddress, never a device address.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FD_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device ordinal
+
+// Device address of the scratch on the current device, looked up on the first
+// call for that device (with the device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fdh::cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fdh::fail(FD_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return fdh::cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return FD_OK;
+}
+}  // namespace
+
+extern "C" int fd_decode_attn_noalloc(const fd_decode_args* a, void* stream) {
+  if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_decode_attn_noalloc: null args");
+  if (a->n <= 0) return decode_impl(a, stream, true, true);
+  Geometry g;
+  const int st = geometry(a, &g);
+  if (st != FD_OK) return st;
+  if (g.ws_bytes > (size_t)FD_NOALLOC_SCRATCH_BYTES)
+    return fdh::fail(FD_ERR_WORKSPACE,
+                     "fd_decode_attn_noalloc: these arguments need %zu bytes of split scratch but the "
+                     "built-in scratch holds %zu (FD_NOALLOC_SCRATCH_BYTES); use fd_decode_attn with a "
+                     "caller workspace, or a larger tiles_per_split",
+                     g.ws_bytes, (size_t)FD_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (g.ws_bytes > 0) {
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != FD_OK) return rc;
+  }
+  return decode_impl(a, stream, true, true, scratch, (size_t)FD_NOALLOC_SCRATCH_BYTES);
+}
+
 
 namespace {
 void paged_args(fd_decode_args* a, const void* q, const void* k_cache, const void* v_cache,
