@@ -25,12 +25,19 @@
 #include <algorithm>
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "fd_common.cuh"
 #include "fd_internal.h"
 
 namespace fdk {
 
-struct DecodeParams {
+struct alignas(64) DecodeParams {
+  // tiled-TMA descriptors of device tiers whose tiles are not contiguous
+  // (dims {D, KVH, BS, blocks}, box {D, 1, TT, 1}); used when use_tmap[t]
+  CUtensorMap tmap_k[2];
+  CUtensorMap tmap_v[2];
+  int use_tmap[2];
   const unsigned char* q;
   int64_t q_sn, q_sh;  // bytes
   const int64_t* q_rows;
@@ -82,7 +89,9 @@ struct Cfg {
   static constexpr int kRPI = 32 / kNCH;
   static constexpr int kPVL = kRPI * kNCH;
   static constexpr int kTileBytes = kMaxTT * kRB;
-  static constexpr int kStageBytes = kNW * 2 * kTileBytes;
+  // smem slot of one K or V tile, 128-byte aligned for tiled TMA
+  static constexpr int kTileSlot = ((kTileBytes + 127) / 128) * 128;
+  static constexpr int kStageBytes = kNW * 2 * kTileSlot;
   static constexpr int kNST = cmax(2, cmin(4, 98304 / kStageBytes));
   static constexpr int kBarBytes = 128;
   static constexpr int kPsBytes = ((kNW * kMaxTT * GQ * 4 + 127) / 128) * 128;
@@ -168,9 +177,10 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
       bool valid = false;
       const unsigned char* ks = nullptr;
       const unsigned char* vs = nullptr;
+      int blk_id = 0, r0 = 0;
       if (lane < C::kNW && tile < tend) {
         const int b = tile / p.tiles_per_block;
-        const int r0 = (tile - b * p.tiles_per_block) * p.TT;
+        r0 = (tile - b * p.tiles_per_block) * p.TT;
         int64_t id = btrow[b];
         if (id >= p.split) {
           tier = 1;
@@ -178,6 +188,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         }
         if (id >= 0 && id < p.nblk[tier]) {
           valid = true;
+          blk_id = (int)id;
           const int64_t off = id * p.blk_sb[tier] + (int64_t)kh * p.head_sb[tier] + (int64_t)r0 * p.tok_sb[tier];
           ks = p.k[tier] + off;
           vs = p.v[tier] + off;
@@ -198,12 +209,19 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         const unsigned char* vw = reinterpret_cast<const unsigned char*>(
             __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
         const int tr = __shfl_sync(0xffffffffu, tier, w);
-        unsigned char* kd = sbase + (2 * w) * tile_bytes;
-        unsigned char* vd = kd + tile_bytes;
+        const int bid = __shfl_sync(0xffffffffu, blk_id, w);
+        const int row0 = __shfl_sync(0xffffffffu, r0, w);
+        unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
+        unsigned char* vd = kd + C::kTileSlot;
         if (p.contig[tr]) {
           if (lane == 0) {
             bulk_g2s(kd, kw, tile_bytes, &full[st], pol);
             bulk_g2s(vd, vw, tile_bytes, &full[st], pol);
+          }
+        } else if (p.use_tmap[tr]) {
+          if (lane == 0) {
+            tma_load_4d(kd, &p.tmap_k[tr], 0, kh, row0, bid, &full[st], pol);
+            tma_load_4d(vd, &p.tmap_v[tr], 0, kh, row0, bid, &full[st], pol);
           }
         } else {
           for (int r = lane; r < p.TT; r += 32) {
@@ -220,8 +238,8 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
             __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
         const int tr = __shfl_sync(0xffffffffu, tier, w);
         const int64_t tsb = p.tok_sb[tr];
-        unsigned char* kd = sbase + (2 * w) * tile_bytes;
-        unsigned char* vd = kd + tile_bytes;
+        unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
+        unsigned char* vd = kd + C::kTileSlot;
         const int nch = p.TT * C::kNCH;
         constexpr int U = 4;
         for (int c0 = 0; c0 < nch; c0 += 32 * U) {
@@ -301,8 +319,8 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     const int tile = tbeg + k * C::kNW + warp;
     if (tile < tend) {
       const int ntok = min(p.TT, len - tile * p.TT);
-      const unsigned char* ks = stages + st * C::kStageBytes + (2 * warp) * tile_bytes;
-      const unsigned char* vs = ks + tile_bytes;
+      const unsigned char* ks = stages + st * C::kStageBytes + (2 * warp) * C::kTileSlot;
+      const unsigned char* vs = ks + C::kTileSlot;
 
       // ---- scores s = q.k (log2 domain), one token per lane group per pass
       float s[GQ][C::kNPASS];
@@ -612,6 +630,42 @@ extern "C" size_t fd_decode_workspace_size(const fd_decode_args* a) {
 
 namespace {
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// Describe one K or V view of a device tier as a 4-D tensor {D, KVH, BS,
+// blocks} with byte strides {head, token, block} and a box of one tile
+// {D, 1, TT, 1}.  Returns false when the driver rejects it (the caller then
+// copies tile rows one by one).
+bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
+                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr || nblk <= 0 || nblk > (int64_t)0xffffffff) return false;
+  CUtensorMapDataType dt = dtype == FD_DTYPE_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                           : dtype == FD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)KVH, (cuuint64_t)BS, (cuuint64_t)nblk};
+  const cuuint64_t strides[3] = {(cuuint64_t)head_sb, (cuuint64_t)tok_sb, (cuuint64_t)blk_sb};
+  const cuuint32_t box[4] = {(cuuint32_t)D, 1u, (cuuint32_t)TT, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Validate `a` and fill the kernel parameters; launch_main / launch_combine
 // select which of the two kernels run.
 int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool launch_combine,
@@ -651,12 +705,21 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     p.nblk[t] = tr.num_blocks > 0 ? tr.num_blocks : 0;
     p.host[t] = tr.host_mapped ? 1 : 0;
     p.contig[t] = (p.tok_sb[t] == row_bytes) ? 1 : 0;
+    p.use_tmap[t] = 0;
     if (p.nblk[t] > 0) {
       if (tr.k == nullptr || tr.v == nullptr)
         return fdh::fail(FD_ERR_INVALID, "tier %d has blocks but no K/V pointer", t);
       if (!fdh::aligned16(tr.k) || !fdh::aligned16(tr.v) || p.blk_sb[t] % 16 != 0 ||
           p.head_sb[t] % 16 != 0 || p.tok_sb[t] % 16 != 0)
         return fdh::fail(FD_ERR_ALIGN, "tier %d K/V pointers and strides must be 16-byte aligned", t);
+      if (!p.host[t] && !p.contig[t] && launch_main) {
+        const bool ok_k = encode_tier_map(&p.tmap_k[t], tr.k, a->dtype, D, a->num_kv_heads, a->block_size,
+                                          p.nblk[t], p.head_sb[t], p.tok_sb[t], p.blk_sb[t], g.TT);
+        const bool ok_v = ok_k && encode_tier_map(&p.tmap_v[t], tr.v, a->dtype, D, a->num_kv_heads,
+                                                  a->block_size, p.nblk[t], p.head_sb[t], p.tok_sb[t],
+                                                  p.blk_sb[t], g.TT);
+        p.use_tmap[t] = (ok_k && ok_v) ? 1 : 0;
+      }
     }
   }
   p.split = a->tier_split;
@@ -779,7 +842,6 @@ extern "C" int fd_decode_attn_noalloc(const fd_decode_args* a, void* stream) {
   }
   return decode_impl(a, stream, true, true, scratch, (size_t)FD_NOALLOC_SCRATCH_BYTES);
 }
-
 
 namespace {
 void paged_args(fd_decode_args* a, const void* q, const void* k_cache, const void* v_cache,
