@@ -139,6 +139,34 @@ __device__ __forceinline__ void sts128(void* p, const uint4& v) {
                : "memory");
 }
 
+// ------------------------------------------------------------- packed fp32x2
+
+// Two fp32 values in one 64-bit register pair, operated on by the packed
+// fp32 pipe of sm_100 (fma/mul .f32x2: two lanes per instruction).
+typedef unsigned long long f2_t;
+
+__device__ __forceinline__ f2_t f2_pack(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(f2_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
+  f2_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // ------------------------------------------------------------- dtypes
 
 template <typename T>
@@ -156,6 +184,15 @@ struct Dt<__half> {
       f[2 * i + 1] = x.y;
     }
   }
+  // 16 bytes -> 4 packed pairs
+  __device__ static __forceinline__ void widen2(const uint4& v, f2_t* f) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __half22float2(h[i]);
+      f[i] = f2_pack(x.x, x.y);
+    }
+  }
   __device__ static __forceinline__ __half narrow(float x) { return __float2half_rn(x); }
   __device__ static __forceinline__ float to_f32(__half x) { return __half2float(x); }
 };
@@ -171,6 +208,11 @@ struct Dt<__nv_bfloat16> {
       f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
   }
+  __device__ static __forceinline__ void widen2(const uint4& v, f2_t* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = f2_pack(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+  }
   __device__ static __forceinline__ __nv_bfloat16 narrow(float x) { return __float2bfloat16_rn(x); }
   __device__ static __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
 };
@@ -183,6 +225,10 @@ struct Dt<float> {
     f[1] = __uint_as_float(v.y);
     f[2] = __uint_as_float(v.z);
     f[3] = __uint_as_float(v.w);
+  }
+  __device__ static __forceinline__ void widen2(const uint4& v, f2_t* f) {
+    f[0] = f2_pack(__uint_as_float(v.x), __uint_as_float(v.y));
+    f[1] = f2_pack(__uint_as_float(v.z), __uint_as_float(v.w));
   }
   __device__ static __forceinline__ float narrow(float x) { return x; }
   __device__ static __forceinline__ float to_f32(float x) { return x; }

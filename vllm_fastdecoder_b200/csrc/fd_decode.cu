@@ -277,31 +277,35 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   const int rot = tp % C::kCPL;
 
   // q for this lane's chunks, widened and pre-scaled (reference :334-339),
-  // stored in the rotated order the K reads use (bank-conflict free).
-  float qr[GQ][C::kCPL][EPC];
+  // stored in the rotated order the K reads use (bank-conflict free), as
+  // packed fp32 pairs.
+  constexpr int EP2 = EPC / 2;
+  f2_t qr[GQ][C::kCPL][EP2];
   {
     const int64_t qrow = p.q_rows ? p.q_rows[i] : i;
     const unsigned char* qb = p.q + qrow * p.q_sn + (int64_t)h0 * p.q_sh;
+    const f2_t qs2 = f2_pack(p.qscale, p.qscale);
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
 #pragma unroll
       for (int jj = 0; jj < C::kCPL; ++jj) {
         const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(qb + g * p.q_sh + c * 16));
-        DT::widen(v, qr[g][jj]);
+        DT::widen2(v, qr[g][jj]);
 #pragma unroll
-        for (int e = 0; e < EPC; ++e) qr[g][jj][e] *= p.qscale;
+        for (int e = 0; e < EP2; ++e) qr[g][jj][e] = f2_mul(qr[g][jj][e], qs2);
       }
     }
   }
 
-  float m_run[GQ], l_run[GQ], acc[GQ][EPC];
+  float m_run[GQ], l_run[GQ];
+  f2_t acc[GQ][EP2];
 #pragma unroll
   for (int g = 0; g < GQ; ++g) {
     m_run[g] = -INFINITY;
     l_run[g] = 0.f;
 #pragma unroll
-    for (int e = 0; e < EPC; ++e) acc[g][e] = 0.f;
+    for (int e = 0; e < EP2; ++e) acc[g][e] = f2_pack(0.f, 0.f);
   }
   const int cpv = lane % C::kNCH;
   const int rg = lane / C::kNCH;
@@ -327,21 +331,28 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
 #pragma unroll
       for (int pp = 0; pp < C::kNPASS; ++pp) {
         const int t = pp * C::kTPP + tp;
-        float dot[GQ];
+        f2_t dot2[GQ];
 #pragma unroll
-        for (int g = 0; g < GQ; ++g) dot[g] = 0.f;
+        for (int g = 0; g < GQ; ++g) dot2[g] = f2_pack(0.f, 0.f);
         if (t < ntok) {
 #pragma unroll
           for (int jj = 0; jj < C::kCPL; ++jj) {
             const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
             const uint4 kv = lds128(ks + t * C::kRB + c * 16);
-            float kf[EPC];
-            DT::widen(kv, kf);
+            f2_t kf[EP2];
+            DT::widen2(kv, kf);
 #pragma unroll
             for (int g = 0; g < GQ; ++g)
 #pragma unroll
-              for (int e = 0; e < EPC; ++e) dot[g] = fmaf(qr[g][jj][e], kf[e], dot[g]);
+              for (int e = 0; e < EP2; ++e) dot2[g] = f2_fma(qr[g][jj][e], kf[e], dot2[g]);
           }
+        }
+        float dot[GQ];
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) {
+          float lo, hi;
+          f2_unpack(dot2[g], lo, hi);
+          dot[g] = lo + hi;
         }
 #pragma unroll
         for (int off = C::kTPT / 2; off >= 1; off >>= 1)
@@ -387,22 +398,24 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
 
       // ---- acc = acc * alpha + P.V
 #pragma unroll
-      for (int g = 0; g < GQ; ++g)
+      for (int g = 0; g < GQ; ++g) {
+        const f2_t a2 = f2_pack(alpha[g], alpha[g]);
 #pragma unroll
-        for (int e = 0; e < EPC; ++e) acc[g][e] *= alpha[g];
+        for (int e = 0; e < EP2; ++e) acc[g][e] = f2_mul(acc[g][e], a2);
+      }
       if (pv_on) {
 #pragma unroll 4
         for (int r = rg; r < ntok; r += C::kRPI) {
           const uint4 vv = lds128(vs + r * C::kRB + cpv * 16);
-          float vf[EPC];
-          DT::widen(vv, vf);
-          float pr[GQ];
+          f2_t vf[EP2];
+          DT::widen2(vv, vf);
 #pragma unroll
-          for (int g = 0; g < GQ; ++g) pr[g] = psw[r * GQ + g];
+          for (int g = 0; g < GQ; ++g) {
+            const float pg = psw[r * GQ + g];
+            const f2_t p2 = f2_pack(pg, pg);
 #pragma unroll
-          for (int g = 0; g < GQ; ++g)
-#pragma unroll
-            for (int e = 0; e < EPC; ++e) acc[g][e] = fmaf(pr[g], vf[e], acc[g][e]);
+            for (int e = 0; e < EP2; ++e) acc[g][e] = f2_fma(p2, vf[e], acc[g][e]);
+          }
         }
       }
     }
@@ -426,8 +439,12 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
 #pragma unroll
     for (int g = 0; g < GQ; ++g)
 #pragma unroll
-      for (int e = 0; e < EPC; ++e)
-        red_acc[((warp * C::kRPI + rg) * GQ + g) * D + cpv * EPC + e] = acc[g][e];
+      for (int e = 0; e < EP2; ++e) {
+        float lo, hi;
+        f2_unpack(acc[g][e], lo, hi);
+        red_acc[((warp * C::kRPI + rg) * GQ + g) * D + cpv * EPC + 2 * e] = lo;
+        red_acc[((warp * C::kRPI + rg) * GQ + g) * D + cpv * EPC + 2 * e + 1] = hi;
+      }
   }
   named_barrier_sync(1, C::kNW * 32);
 
