@@ -260,7 +260,8 @@ def run_ours(args, ws, rank, device):
     else:
         out = torch.empty(n, H, D, dtype=batch.dtype, device=device)
         lse = torch.empty(H, n, dtype=torch.float32, device=device)
-    tps = gpu_ops.choose_tiles_per_split(int(batch.lens.sum()), batch.KVH, batch.BS)
+    # 0: the persistent, length-balanced schedule; --split-grid: fixed splits
+    tps = gpu_ops.choose_tiles_per_split(int(batch.lens.sum()), batch.KVH, batch.BS) if args.split_grid else 0
     max_len = int(batch.lens.max())
     a = gpu_ops.decode_args(res.q, res.tiers, batch.G, res.block_table, res.lens, batch.scale, out, lse,
                             max_len=max_len, tiles_per_split=tps)
@@ -435,6 +436,7 @@ def _config(batch, args, ws, tps, has_combine) -> dict:
         }[args.workload],
         "rows": batch.n, "heads": batch.H, "kv_heads": batch.KVH, "head_size": batch.D, "block_size": batch.BS,
         "hbm_kv_bytes": hbm_b, "host_kv_bytes": host_b, "hbm_layout": batch.hbm_layout,
+        "schedule": "split grid" if tps else "persistent (one CTA pair per SM, equal tile ranges)",
         "tiles_per_split": tps, "split_combine": has_combine,
         "l2": "no flush: each step streams more KV than the 126 MB L2" if hbm_b + host_b > (126 << 20)
               else "KV smaller than L2",
@@ -478,7 +480,10 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3"], default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
     args = ap.parse_args()
+    if args.impl == "reference":
+        args.split_grid = False
     if args.steps <= 0:
         args.steps = {"c1": 60, "c0": 400, "c2": 200, "c3": 100}[args.workload]
     args.warmup = max(3, args.warmup)

@@ -33,7 +33,9 @@ def ops():
     return gpu_ops
 
 
-def _run_paged(ops, q, kc, vc, bt, lens, scale, host_cache=False):
+def _run_paged(ops, q, kc, vc, bt, lens, scale, host_cache=False, tiles_per_split=0):
+    """Run the kernel through the C ABI; tiles_per_split 0 selects the
+    persistent schedule (rows <= 1024), > 0 the fixed split grid."""
     dev = torch.device("cuda")
     n, H, D = q.shape
     if host_cache:
@@ -42,7 +44,13 @@ def _run_paged(ops, q, kc, vc, bt, lens, scale, host_cache=False):
         kd, vd = kc.to(dev), vc.to(dev)
     out = torch.full((n, H, D), float("nan"), dtype=q.dtype, device=dev)
     lse = torch.full((H, n), float("nan"), dtype=torch.float32, device=dev)
-    ops.decode_attn(q.to(dev), kd, vd, bt.to(dev), lens.to(dev), scale, out, lse)
+    if tiles_per_split:
+        from vllm_fastdecoder_b200.gpu_ops import KVTier
+
+        ops.decode_tiered(q.to(dev), (KVTier(kd, vd), None), 1 << 40, bt.to(dev), lens.to(dev), scale, out, lse,
+                          tiles_per_split=tiles_per_split)
+    else:
+        ops.decode_attn(q.to(dev), kd, vd, bt.to(dev), lens.to(dev), scale, out, lse)
     ops.check_device_errors(dev)
     return out.cpu(), lse.cpu()
 
@@ -110,15 +118,41 @@ def test_decode_attn_block_sizes(ops, BS):
     _compare(q, kc, vc, bt, lens, scale, out, lse)
 
 
+@pytest.mark.parametrize("tiles_per_split", [0, 8, 36])
 @pytest.mark.parametrize("dtype,H,KVH", [(torch.float16, 32, 32), (torch.bfloat16, 32, 8)])
-def test_decode_attn_many_splits(ops, dtype, H, KVH):
-    """Rows long enough to be cut into many splits (exercises the split merge)."""
+def test_decode_attn_many_splits(ops, dtype, H, KVH, tiles_per_split):
+    """Rows long enough to be cut across many CTAs: the persistent schedule
+    (0) and the fixed split grid (8, 36 tiles per split), both through their
+    combine kernels."""
     n, D, BS = 3, 128, 16
     L = 9000
     C = 3 * ((L + BS - 1) // BS) + 4
     q, kc, vc, bt, lens = O.rand_case(n, H, KVH, D, BS, C, dtype, max_len=L, seed=5)
     lens[1] = 17
     lens[2] = 4097
+    scale = D ** -0.5
+    out, lse = _run_paged(ops, q, kc, vc, bt, lens, scale, tiles_per_split=tiles_per_split)
+    _compare(q, kc, vc, bt, lens, scale, out, lse)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_decode_persistent_ragged_batch(ops, seed):
+    """Many rows of very different lengths (empty, single-token, long) so CTA
+    ranges start and end at every kind of boundary."""
+    import random
+
+    rng = random.Random(seed)
+    n, H, KVH, D, BS = 37, 8, 2, 128, 16
+    lens_l = [rng.choice([0, 1, 15, 16, 17, rng.randint(1, 3000)]) for _ in range(n)]
+    C = sum((x + BS - 1) // BS for x in lens_l) + 8
+    q, kc, vc, bt, lens = O.rand_case(n, H, KVH, D, BS, C, torch.bfloat16, max_len=max(lens_l), seed=seed)
+    lens = torch.tensor(lens_l, dtype=torch.int32)
+    W = bt.shape[1]
+    perm = torch.randperm(C, generator=torch.Generator().manual_seed(seed)).tolist()
+    bt = torch.zeros(n, W, dtype=torch.int32)
+    for i, L in enumerate(lens_l):
+        nb = (L + BS - 1) // BS
+        bt[i, :nb] = torch.tensor([perm.pop() for _ in range(nb)], dtype=torch.int32)
     scale = D ** -0.5
     out, lse = _run_paged(ops, q, kc, vc, bt, lens, scale)
     _compare(q, kc, vc, bt, lens, scale, out, lse)

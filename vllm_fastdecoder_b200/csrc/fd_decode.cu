@@ -52,8 +52,12 @@ struct alignas(64) DecodeParams {
   int64_t bt_stride;
   int bt_width;
   const int32_t* lens;
-  int n, H, KVH, BS, G, gcs;
+  int n, H, KVH, BS, G, gcs, gq;
   int TT, tiles_per_block, tiles_per_split, max_splits;
+  // persistent schedule: ncta CTAs share the flattened (row, kv-head chunk,
+  // tile) space evenly; prefix of per-row tile counts published in ws_prefix
+  int persistent, ncta;
+  int* ws_prefix;
   float qscale;  // scale * log2(e)
   void* out;
   int out_dtype;
@@ -70,6 +74,14 @@ constexpr int p2div(int x, int p) { return (x % (2 * p) == 0 && 2 * p <= 32) ? p
 constexpr int ceil_pow2(int x, int p) { return p >= x ? p : ceil_pow2(x, 2 * p); }
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
+constexpr int round128(int x) { return (x + 127) / 128 * 128; }
+
+// Largest row count handled by the persistent schedule (its per-row tile
+// prefix sits in shared memory).
+constexpr int kMaxPersistentRows = 1024;
+// Upper bound on persistent CTAs (2 per SM on 148 SMs, with headroom); sizes
+// the partial slots of the workspace.
+constexpr int kMaxPersistentCtas = 320;
 
 template <typename T, int D, int GQ>
 struct Cfg {
@@ -88,18 +100,30 @@ struct Cfg {
   // P.V: lane owns chunk (lane % kNCH) of token rows (lane / kNCH) + k*kRPI
   static constexpr int kRPI = 32 / kNCH;
   static constexpr int kPVL = kRPI * kNCH;
+  // the kRPI row groups of a warp are summed with shuffles when they tile
+  // the warp exactly, otherwise through shared memory
+  static constexpr bool kShflRed = (kPVL == 32);
+  static constexpr int kRedRows = kShflRed ? 1 : kRPI;
   static constexpr int kTileBytes = kMaxTT * kRB;
   // smem slot of one K or V tile, 128-byte aligned for tiled TMA
-  static constexpr int kTileSlot = ((kTileBytes + 127) / 128) * 128;
+  static constexpr int kTileSlot = round128(kTileBytes);
   static constexpr int kStageBytes = kNW * 2 * kTileSlot;
   static constexpr int kNST = cmax(2, cmin(4, 98304 / kStageBytes));
   static constexpr int kBarBytes = 128;
-  static constexpr int kPsBytes = ((kNW * kMaxTT * GQ * 4 + 127) / 128) * 128;
-  static constexpr int kRedBytes = (2 * kNW * GQ + kNW * kRPI * GQ * D) * 4;
-  static constexpr int kSmem = kBarBytes + kPsBytes + kNST * kStageBytes;
-  static constexpr bool kValid =
-      (kRB % 16 == 0) && kNCH <= 32 && (GQ * kCPL * kEPC <= 64 || GQ == 1) &&
-      kRedBytes <= kNST * kStageBytes && 2 * kNST * 8 <= kBarBytes && kSmem <= 227 * 1024;
+  static constexpr int kPsBytes = round128(kNW * kMaxTT * GQ * 4);
+  static constexpr int kRedBytes = round128((2 * kNW * GQ + kNW * kRedRows * GQ * D) * 4);
+  static constexpr int kSmem = kBarBytes + kPsBytes + kRedBytes + kNST * kStageBytes;
+  static constexpr int kPrefixMax = round128((kMaxPersistentRows + 1) * 4);
+  static constexpr bool kValid = (kRB % 16 == 0) && kNCH <= 32 && (GQ * kCPL * kEPC <= 64 || GQ == 1) &&
+                                 2 * kNST * 8 <= kBarBytes && kSmem + kPrefixMax <= 227 * 1024;
+};
+
+// One piece of work: tiles [t0, t1) of row `row` for kv-head chunk y.  A piece
+// covering its whole (row, chunk) segment writes the final output; otherwise
+// it writes an fp32 partial into `slot`.
+struct Piece {
+  int row, y, t0, t1, len, slot;
+  bool whole;
 };
 
 template <typename T, int D, int GQ>
@@ -108,52 +132,47 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   using C = Cfg<T, D, GQ>;
   using DT = Dt<T>;
   constexpr int EPC = C::kEPC;
+  constexpr int EP2 = EPC / 2;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + C::kNST;
   float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes);
-  unsigned char* stages = smem + C::kBarBytes + C::kPsBytes;
+  float* red_m = reinterpret_cast<float*>(smem + C::kBarBytes + C::kPsBytes);
+  float* red_l = red_m + C::kNW * GQ;
+  float* red_acc = red_l + C::kNW * GQ;
+  unsigned char* stages = smem + C::kBarBytes + C::kPsBytes + C::kRedBytes;
+  int* prefix = reinterpret_cast<int*>(stages + C::kNST * C::kStageBytes);
+  __shared__ int abort_flag;
 
-  const int split = blockIdx.x;
-  const int kh = blockIdx.y / p.gcs;
-  const int gc = blockIdx.y - kh * p.gcs;
-  const int i = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h0 = kh * p.G + gc * GQ;
-  const int len = p.lens[i];
+  const int Y = p.KVH * p.gcs;
 
-  if (len <= 0) {
-    // empty row: o = 0, lse = -inf (reference cpu_attn.cpp:324-331)
-    if (split == 0) {
-      const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-      for (int o = threadIdx.x; o < GQ * D; o += blockDim.x) {
-        const int g = o / D, d = o - g * D;
-        store_out(p.out, orow * p.out_sn + (int64_t)(h0 + g) * p.out_sh + d, p.out_dtype, 0.f);
+  // ---------------------------------------------------------------- setup
+  if (p.persistent && warp == 0) {
+    // prefix[i] = tiles of rows < i (0 for empty rows and rows whose length
+    // overruns their table row)
+    int carry = 0;
+    for (int base = 0; base < p.n; base += 32) {
+      const int i = base + lane;
+      int nt = 0;
+      if (i < p.n) {
+        const int len = p.lens[i];
+        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + p.TT - 1) / p.TT;
       }
-      if (p.lse != nullptr && threadIdx.x < GQ)
-        p.lse[(int64_t)(h0 + threadIdx.x) * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
+      int v = nt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += u;
+      }
+      if (i < p.n) prefix[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
     }
-    return;
+    if (lane == 0) prefix[0] = 0;
   }
-  const int nblk = (len + p.BS - 1) / p.BS;
-  if (nblk > p.bt_width) {
-    if (threadIdx.x == 0 && split == 0) set_error(p.err, FD_DEVERR_LEN);
-    return;
-  }
-  const int ntiles = (len + p.TT - 1) / p.TT;
-  const int nsplits = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
-  if (nsplits > p.max_splits) {
-    if (threadIdx.x == 0 && split == 0) set_error(p.err, FD_DEVERR_SPLITS);
-    return;
-  }
-  if (split >= nsplits) return;
-  const int tbeg = split * p.tiles_per_split;
-  const int tend = min(ntiles, tbeg + p.tiles_per_split);
-  const int nstages = (tend - tbeg + C::kNW - 1) / C::kNW;
-  const uint32_t tile_bytes = (uint32_t)p.TT * C::kRB;
-
   if (threadIdx.x == 0) {
+    abort_flag = 0;
 #pragma unroll
     for (int s = 0; s < C::kNST; ++s) {
       mbar_init(&full[s], 32);
@@ -163,110 +182,220 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   }
   __syncthreads();
 
+  int64_t g_cur = 0, g_end = 0;
+  int row_cur = 0;
+  if (p.persistent) {
+    if (blockIdx.x == 0 && p.ws_prefix != nullptr)
+      for (int i = threadIdx.x; i <= p.n; i += blockDim.x) p.ws_prefix[i] = prefix[i];
+    // rows without tiles: empty -> o = 0, lse = -inf (reference
+    // cpu_attn.cpp:324-331); overrun -> error word
+    for (int i = blockIdx.x; i < p.n; i += gridDim.x) {
+      if (prefix[i + 1] != prefix[i]) continue;
+      const int len = p.lens[i];
+      if (len > 0) {
+        if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
+        continue;
+      }
+      const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+      for (int o = threadIdx.x; o < p.H * D; o += blockDim.x) {
+        const int h = o / D, d = o - h * D;
+        store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
+      }
+      if (p.lse != nullptr)
+        for (int h = threadIdx.x; h < p.H; h += blockDim.x) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
+    }
+    const int64_t total = (int64_t)prefix[p.n] * Y;
+    g_cur = (int64_t)blockIdx.x * total / gridDim.x;
+    g_end = (int64_t)(blockIdx.x + 1) * total / gridDim.x;
+    if (g_cur < g_end) {
+      int lo = 0, hi = p.n - 1;  // last row whose first tile is <= g_cur
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if ((int64_t)prefix[mid] * Y <= g_cur) lo = mid; else hi = mid - 1;
+      }
+      row_cur = lo;
+    }
+  } else {
+    // split grid: x = split, y = kv-head chunk, z = row
+    const int i = blockIdx.z;
+    const int len = p.lens[i];
+    if (len <= 0) {
+      if (blockIdx.x == 0) {
+        const int kh = blockIdx.y / p.gcs, gc = blockIdx.y - kh * p.gcs;
+        const int h0 = kh * p.G + gc * GQ;
+        const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+        for (int o = threadIdx.x; o < GQ * D; o += blockDim.x) {
+          const int g = o / D, d = o - g * D;
+          store_out(p.out, orow * p.out_sn + (int64_t)(h0 + g) * p.out_sh + d, p.out_dtype, 0.f);
+        }
+        if (p.lse != nullptr && threadIdx.x < GQ)
+          p.lse[(int64_t)(h0 + threadIdx.x) * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
+      }
+      return;
+    }
+    const int nblk = (len + p.BS - 1) / p.BS;
+    const int ntiles = (len + p.TT - 1) / p.TT;
+    const int nsplits = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
+    if (nblk > p.bt_width || nsplits > p.max_splits) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) set_error(p.err, nblk > p.bt_width ? FD_DEVERR_LEN : FD_DEVERR_SPLITS);
+      return;
+    }
+    if ((int)blockIdx.x >= nsplits) return;
+  }
+
+  // Pieces of this CTA, enumerated identically by the producer and consumers.
+  bool split_done = false, first_piece = true;
+  auto next_piece = [&](Piece& pc) -> bool {
+    if (!p.persistent) {
+      if (split_done) return false;
+      split_done = true;
+      const int i = blockIdx.z;
+      const int len = p.lens[i];
+      const int ntiles = (len + p.TT - 1) / p.TT;
+      const int nsplits = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
+      pc.row = i;
+      pc.y = blockIdx.y;
+      pc.t0 = blockIdx.x * p.tiles_per_split;
+      pc.t1 = min(ntiles, pc.t0 + p.tiles_per_split);
+      pc.len = len;
+      pc.whole = (nsplits == 1);
+      pc.slot = blockIdx.x;
+      return true;
+    }
+    if (g_cur >= g_end) return false;
+    const int nt = prefix[row_cur + 1] - prefix[row_cur];
+    const int64_t local = g_cur - (int64_t)prefix[row_cur] * Y;
+    const int y = (int)(local / nt);
+    const int t0 = (int)(local - (int64_t)y * nt);
+    const int t1 = (int)min((int64_t)nt, (int64_t)t0 + (g_end - g_cur));
+    pc.row = row_cur;
+    pc.y = y;
+    pc.t0 = t0;
+    pc.t1 = t1;
+    pc.len = p.lens[row_cur];
+    pc.whole = (t0 == 0 && t1 == nt);
+    pc.slot = first_piece ? 0 : 1;
+    first_piece = false;
+    g_cur += t1 - t0;
+    if (t1 == nt && y == Y - 1) {
+      do {
+        ++row_cur;
+      } while (row_cur < p.n && prefix[row_cur + 1] == prefix[row_cur]);
+    }
+    return true;
+  };
+
+  const uint32_t tile_bytes = (uint32_t)p.TT * C::kRB;
+
   if (warp == C::kNW) {
     // ------------------------------------------------------------ producer
     const uint64_t pol = l2_evict_first_policy();
-    const int32_t* btrow = p.bt + (int64_t)i * p.bt_stride;
-    for (int k = 0; k < nstages; ++k) {
-      const int st = k % C::kNST;
-      const uint32_t use = (uint32_t)(k / C::kNST);
-      if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1u, p.err)) return;
-      unsigned char* sbase = stages + st * C::kStageBytes;
-      const int tile = tbeg + k * C::kNW + lane;
-      int tier = 0;
-      bool valid = false;
-      const unsigned char* ks = nullptr;
-      const unsigned char* vs = nullptr;
-      int blk_id = 0, r0 = 0;
-      if (lane < C::kNW && tile < tend) {
-        const int b = tile / p.tiles_per_block;
-        r0 = (tile - b * p.tiles_per_block) * p.TT;
-        int64_t id = btrow[b];
-        if (id >= p.split) {
-          tier = 1;
-          id -= p.split;
-        }
-        if (id >= 0 && id < p.nblk[tier]) {
-          valid = true;
-          blk_id = (int)id;
-          const int64_t off = id * p.blk_sb[tier] + (int64_t)kh * p.head_sb[tier] + (int64_t)r0 * p.tok_sb[tier];
-          ks = p.k[tier] + off;
-          vs = p.v[tier] + off;
-        } else {
-          set_error(p.err, FD_DEVERR_BLOCK_ID);
-        }
-      }
-      const bool bulk = valid && !p.host[tier];
-      const unsigned bulk_mask = __ballot_sync(0xffffffffu, bulk);
-      const unsigned host_mask = __ballot_sync(0xffffffffu, valid && !bulk);
-      if (lane == 0 && bulk_mask != 0u)
-        mbar_expect_tx(&full[st], (uint32_t)__popc(bulk_mask) * 2u * tile_bytes);
-      __syncwarp();
-      for (unsigned m = bulk_mask; m != 0u; m &= m - 1u) {
-        const int w = __ffs(m) - 1;
-        const unsigned char* kw = reinterpret_cast<const unsigned char*>(
-            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
-        const unsigned char* vw = reinterpret_cast<const unsigned char*>(
-            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
-        const int tr = __shfl_sync(0xffffffffu, tier, w);
-        const int bid = __shfl_sync(0xffffffffu, blk_id, w);
-        const int row0 = __shfl_sync(0xffffffffu, r0, w);
-        unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
-        unsigned char* vd = kd + C::kTileSlot;
-        if (p.contig[tr]) {
-          if (lane == 0) {
-            bulk_g2s(kd, kw, tile_bytes, &full[st], pol);
-            bulk_g2s(vd, vw, tile_bytes, &full[st], pol);
+    int k = 0;
+    Piece pc;
+    while (next_piece(pc)) {
+      const int kh = pc.y / p.gcs;
+      const int32_t* btrow = p.bt + (int64_t)pc.row * p.bt_stride;
+      for (int t = pc.t0; t < pc.t1; t += C::kNW, ++k) {
+        const int st = k % C::kNST;
+        const uint32_t use = (uint32_t)(k / C::kNST);
+        if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1u, p.err)) return;
+        unsigned char* sbase = stages + st * C::kStageBytes;
+        const int tile = t + lane;
+        int tier = 0;
+        bool valid = false;
+        const unsigned char* ks = nullptr;
+        const unsigned char* vs = nullptr;
+        int blk_id = 0, r0 = 0;
+        if (lane < C::kNW && tile < pc.t1) {
+          const int b = tile / p.tiles_per_block;
+          r0 = (tile - b * p.tiles_per_block) * p.TT;
+          int64_t id = btrow[b];
+          if (id >= p.split) {
+            tier = 1;
+            id -= p.split;
           }
-        } else if (p.use_tmap[tr]) {
-          if (lane == 0) {
-            tma_load_4d(kd, &p.tmap_k[tr], 0, kh, row0, bid, &full[st], pol);
-            tma_load_4d(vd, &p.tmap_v[tr], 0, kh, row0, bid, &full[st], pol);
-          }
-        } else {
-          for (int r = lane; r < p.TT; r += 32) {
-            bulk_g2s(kd + r * C::kRB, kw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
-            bulk_g2s(vd + r * C::kRB, vw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
+          if (id >= 0 && id < p.nblk[tier]) {
+            valid = true;
+            blk_id = (int)id;
+            const int64_t off = id * p.blk_sb[tier] + (int64_t)kh * p.head_sb[tier] + (int64_t)r0 * p.tok_sb[tier];
+            ks = p.k[tier] + off;
+            vs = p.v[tier] + off;
+          } else {
+            set_error(p.err, FD_DEVERR_BLOCK_ID);
           }
         }
-      }
-      for (unsigned m = host_mask; m != 0u; m &= m - 1u) {
-        const int w = __ffs(m) - 1;
-        const unsigned char* kw = reinterpret_cast<const unsigned char*>(
-            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
-        const unsigned char* vw = reinterpret_cast<const unsigned char*>(
-            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
-        const int tr = __shfl_sync(0xffffffffu, tier, w);
-        const int64_t tsb = p.tok_sb[tr];
-        unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
-        unsigned char* vd = kd + C::kTileSlot;
-        const int nch = p.TT * C::kNCH;
-        constexpr int U = 4;
-        for (int c0 = 0; c0 < nch; c0 += 32 * U) {
-          uint4 kb[U], vb[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int c = c0 + u * 32 + lane;
-            if (c < nch) {
-              const int row = c / C::kNCH;
-              const int64_t off = row * tsb + (c - row * C::kNCH) * 16;
-              kb[u] = *reinterpret_cast<const uint4*>(kw + off);
-              vb[u] = *reinterpret_cast<const uint4*>(vw + off);
+        const bool bulk = valid && !p.host[tier];
+        const unsigned bulk_mask = __ballot_sync(0xffffffffu, bulk);
+        const unsigned host_mask = __ballot_sync(0xffffffffu, valid && !bulk);
+        if (lane == 0 && bulk_mask != 0u)
+          mbar_expect_tx(&full[st], (uint32_t)__popc(bulk_mask) * 2u * tile_bytes);
+        __syncwarp();
+        for (unsigned m = bulk_mask; m != 0u; m &= m - 1u) {
+          const int w = __ffs(m) - 1;
+          const unsigned char* kw = reinterpret_cast<const unsigned char*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
+          const unsigned char* vw = reinterpret_cast<const unsigned char*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
+          const int tr = __shfl_sync(0xffffffffu, tier, w);
+          const int bid = __shfl_sync(0xffffffffu, blk_id, w);
+          const int row0 = __shfl_sync(0xffffffffu, r0, w);
+          unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
+          unsigned char* vd = kd + C::kTileSlot;
+          if (p.contig[tr]) {
+            if (lane == 0) {
+              bulk_g2s(kd, kw, tile_bytes, &full[st], pol);
+              bulk_g2s(vd, vw, tile_bytes, &full[st], pol);
             }
-          }
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int c = c0 + u * 32 + lane;
-            if (c < nch) {
-              sts128(kd + c * 16, kb[u]);
-              sts128(vd + c * 16, vb[u]);
+          } else if (p.use_tmap[tr]) {
+            if (lane == 0) {
+              tma_load_4d(kd, &p.tmap_k[tr], 0, kh, row0, bid, &full[st], pol);
+              tma_load_4d(vd, &p.tmap_v[tr], 0, kh, row0, bid, &full[st], pol);
+            }
+          } else {
+            for (int r = lane; r < p.TT; r += 32) {
+              bulk_g2s(kd + r * C::kRB, kw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
+              bulk_g2s(vd + r * C::kRB, vw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
             }
           }
         }
+        for (unsigned m = host_mask; m != 0u; m &= m - 1u) {
+          const int w = __ffs(m) - 1;
+          const unsigned char* kw = reinterpret_cast<const unsigned char*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
+          const unsigned char* vw = reinterpret_cast<const unsigned char*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
+          const int tr = __shfl_sync(0xffffffffu, tier, w);
+          const int64_t tsb = p.tok_sb[tr];
+          unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
+          unsigned char* vd = kd + C::kTileSlot;
+          const int nch = p.TT * C::kNCH;
+          constexpr int U = 4;
+          for (int c0 = 0; c0 < nch; c0 += 32 * U) {
+            uint4 kb[U], vb[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int c = c0 + u * 32 + lane;
+              if (c < nch) {
+                const int row = c / C::kNCH;
+                const int64_t off = row * tsb + (c - row * C::kNCH) * 16;
+                kb[u] = *reinterpret_cast<const uint4*>(kw + off);
+                vb[u] = *reinterpret_cast<const uint4*>(vw + off);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int c = c0 + u * 32 + lane;
+              if (c < nch) {
+                sts128(kd + c * 16, kb[u]);
+                sts128(vd + c * 16, vb[u]);
+              }
+            }
+          }
+        }
+        // order this stage's generic smem writes before later TMA writes to it
+        if (host_mask != 0u) fence_proxy_async_smem();
+        mbar_arrive(&full[st]);
       }
-      // order this stage's generic smem writes before later TMA writes to it
-      if (host_mask != 0u) fence_proxy_async_smem();
-      mbar_arrive(&full[st]);
     }
     return;
   }
@@ -275,212 +404,233 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   const int tp = lane / C::kTPT;
   const int sub = lane - tp * C::kTPT;
   const int rot = tp % C::kCPL;
-
-  // q for this lane's chunks, widened and pre-scaled (reference :334-339),
-  // stored in the rotated order the K reads use (bank-conflict free), as
-  // packed fp32 pairs.
-  constexpr int EP2 = EPC / 2;
-  f2_t qr[GQ][C::kCPL][EP2];
-  {
-    const int64_t qrow = p.q_rows ? p.q_rows[i] : i;
-    const unsigned char* qb = p.q + qrow * p.q_sn + (int64_t)h0 * p.q_sh;
-    const f2_t qs2 = f2_pack(p.qscale, p.qscale);
-#pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-#pragma unroll
-      for (int jj = 0; jj < C::kCPL; ++jj) {
-        const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(qb + g * p.q_sh + c * 16));
-        DT::widen2(v, qr[g][jj]);
-#pragma unroll
-        for (int e = 0; e < EP2; ++e) qr[g][jj][e] = f2_mul(qr[g][jj][e], qs2);
-      }
-    }
-  }
-
-  float m_run[GQ], l_run[GQ];
-  f2_t acc[GQ][EP2];
-#pragma unroll
-  for (int g = 0; g < GQ; ++g) {
-    m_run[g] = -INFINITY;
-    l_run[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < EP2; ++e) acc[g][e] = f2_pack(0.f, 0.f);
-  }
   const int cpv = lane % C::kNCH;
   const int rg = lane / C::kNCH;
   const bool pv_on = lane < C::kPVL;
   float* psw = ps_all + warp * C::kMaxTT * GQ;
-  bool ok = true;
+  int k = 0;
+  Piece pc;
+  while (next_piece(pc)) {
+    const int kh = pc.y / p.gcs;
+    const int gc = pc.y - kh * p.gcs;
+    const int h0 = kh * p.G + gc * GQ;
 
-  for (int k = 0; k < nstages; ++k) {
-    const int st = k % C::kNST;
-    const uint32_t use = (uint32_t)(k / C::kNST);
-    if (!mbar_wait(&full[st], use & 1u, p.err)) {
-      ok = false;
-      break;
-    }
-    const int tile = tbeg + k * C::kNW + warp;
-    if (tile < tend) {
-      const int ntok = min(p.TT, len - tile * p.TT);
-      const unsigned char* ks = stages + st * C::kStageBytes + (2 * warp) * C::kTileSlot;
-      const unsigned char* vs = ks + C::kTileSlot;
-
-      // ---- scores s = q.k (log2 domain), one token per lane group per pass
-      float s[GQ][C::kNPASS];
-#pragma unroll
-      for (int pp = 0; pp < C::kNPASS; ++pp) {
-        const int t = pp * C::kTPP + tp;
-        f2_t dot2[GQ];
-#pragma unroll
-        for (int g = 0; g < GQ; ++g) dot2[g] = f2_pack(0.f, 0.f);
-        if (t < ntok) {
-#pragma unroll
-          for (int jj = 0; jj < C::kCPL; ++jj) {
-            const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
-            const uint4 kv = lds128(ks + t * C::kRB + c * 16);
-            f2_t kf[EP2];
-            DT::widen2(kv, kf);
-#pragma unroll
-            for (int g = 0; g < GQ; ++g)
-#pragma unroll
-              for (int e = 0; e < EP2; ++e) dot2[g] = f2_fma(qr[g][jj][e], kf[e], dot2[g]);
-          }
-        }
-        float dot[GQ];
-#pragma unroll
-        for (int g = 0; g < GQ; ++g) {
-          float lo, hi;
-          f2_unpack(dot2[g], lo, hi);
-          dot[g] = lo + hi;
-        }
-#pragma unroll
-        for (int off = C::kTPT / 2; off >= 1; off >>= 1)
-#pragma unroll
-          for (int g = 0; g < GQ; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
-#pragma unroll
-        for (int g = 0; g < GQ; ++g) s[g][pp] = (t < ntok) ? dot[g] : -INFINITY;
-      }
-
-      // ---- online softmax update for this tile
-      float alpha[GQ];
+    // q for this lane's chunks, widened and pre-scaled (reference :334-339),
+    // in the rotated order the K reads use (bank-conflict free), as packed
+    // fp32 pairs
+    f2_t qr[GQ][C::kCPL][EP2];
+    {
+      const int64_t qrow = p.q_rows ? p.q_rows[pc.row] : pc.row;
+      const unsigned char* qb = p.q + qrow * p.q_sn + (int64_t)h0 * p.q_sh;
+      const f2_t qs2 = f2_pack(p.qscale, p.qscale);
 #pragma unroll
       for (int g = 0; g < GQ; ++g) {
-        float bm = s[g][0];
 #pragma unroll
-        for (int pp = 1; pp < C::kNPASS; ++pp) bm = fmaxf(bm, s[g][pp]);
+        for (int jj = 0; jj < C::kCPL; ++jj) {
+          const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(qb + g * p.q_sh + c * 16));
+          DT::widen2(v, qr[g][jj]);
 #pragma unroll
-        for (int off = C::kTPT; off < 32; off <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
-        const float mn = fmaxf(m_run[g], bm);
-        alpha[g] = exp2f(m_run[g] - mn);
-        float sum = 0.f;
-#pragma unroll
-        for (int pp = 0; pp < C::kNPASS; ++pp) {
-          const float e = exp2f(s[g][pp] - mn);
-          s[g][pp] = e;
-          sum += e;
+          for (int e = 0; e < EP2; ++e) qr[g][jj][e] = f2_mul(qr[g][jj][e], qs2);
         }
-#pragma unroll
-        for (int off = C::kTPT; off < 32; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        l_run[g] = l_run[g] * alpha[g] + sum;
-        m_run[g] = mn;
       }
-      if (sub == 0) {
+    }
+
+    float m_run[GQ], l_run[GQ];
+    f2_t acc[GQ][EP2];
+#pragma unroll
+    for (int g = 0; g < GQ; ++g) {
+      m_run[g] = -INFINITY;
+      l_run[g] = 0.f;
+#pragma unroll
+      for (int e = 0; e < EP2; ++e) acc[g][e] = f2_pack(0.f, 0.f);
+    }
+    bool ok = true;
+
+    for (int t = pc.t0; t < pc.t1; t += C::kNW, ++k) {
+      const int st = k % C::kNST;
+      const uint32_t use = (uint32_t)(k / C::kNST);
+      if (!mbar_wait(&full[st], use & 1u, p.err)) {
+        ok = false;
+        break;
+      }
+      const int tile = t + warp;
+      if (tile < pc.t1) {
+        const int ntok = min(p.TT, pc.len - tile * p.TT);
+        const unsigned char* ks = stages + st * C::kStageBytes + (2 * warp) * C::kTileSlot;
+        const unsigned char* vs = ks + C::kTileSlot;
+
+        // ---- scores s = q.k (log2 domain), one token per lane group per pass
+        float s[GQ][C::kNPASS];
 #pragma unroll
         for (int pp = 0; pp < C::kNPASS; ++pp) {
-          const int t = pp * C::kTPP + tp;
-          if (t < C::kMaxTT)
+          const int tk = pp * C::kTPP + tp;
+          f2_t dot2[GQ];
 #pragma unroll
-            for (int g = 0; g < GQ; ++g) psw[t * GQ + g] = s[g][pp];
+          for (int g = 0; g < GQ; ++g) dot2[g] = f2_pack(0.f, 0.f);
+          if (tk < ntok) {
+#pragma unroll
+            for (int jj = 0; jj < C::kCPL; ++jj) {
+              const int c = sub + C::kTPT * ((jj + rot) % C::kCPL);
+              const uint4 kv = lds128(ks + tk * C::kRB + c * 16);
+              f2_t kf[EP2];
+              DT::widen2(kv, kf);
+#pragma unroll
+              for (int g = 0; g < GQ; ++g)
+#pragma unroll
+                for (int e = 0; e < EP2; ++e) dot2[g] = f2_fma(qr[g][jj][e], kf[e], dot2[g]);
+            }
+          }
+          float dot[GQ];
+#pragma unroll
+          for (int g = 0; g < GQ; ++g) {
+            float lo, hi;
+            f2_unpack(dot2[g], lo, hi);
+            dot[g] = lo + hi;
+          }
+#pragma unroll
+          for (int off = C::kTPT / 2; off >= 1; off >>= 1)
+#pragma unroll
+            for (int g = 0; g < GQ; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+#pragma unroll
+          for (int g = 0; g < GQ; ++g) s[g][pp] = (tk < ntok) ? dot[g] : -INFINITY;
+        }
+
+        // ---- online softmax update for this tile
+        float alpha[GQ];
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) {
+          float bm = s[g][0];
+#pragma unroll
+          for (int pp = 1; pp < C::kNPASS; ++pp) bm = fmaxf(bm, s[g][pp]);
+#pragma unroll
+          for (int off = C::kTPT; off < 32; off <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+          const float mn = fmaxf(m_run[g], bm);
+          alpha[g] = exp2f(m_run[g] - mn);
+          float sum = 0.f;
+#pragma unroll
+          for (int pp = 0; pp < C::kNPASS; ++pp) {
+            const float e = exp2f(s[g][pp] - mn);
+            s[g][pp] = e;
+            sum += e;
+          }
+#pragma unroll
+          for (int off = C::kTPT; off < 32; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+          l_run[g] = l_run[g] * alpha[g] + sum;
+          m_run[g] = mn;
+        }
+        if (sub == 0) {
+#pragma unroll
+          for (int pp = 0; pp < C::kNPASS; ++pp) {
+            const int tk = pp * C::kTPP + tp;
+            if (tk < C::kMaxTT)
+#pragma unroll
+              for (int g = 0; g < GQ; ++g) psw[tk * GQ + g] = s[g][pp];
+          }
+        }
+        __syncwarp();
+
+        // ---- acc = acc * alpha + P.V
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) {
+          const f2_t a2 = f2_pack(alpha[g], alpha[g]);
+#pragma unroll
+          for (int e = 0; e < EP2; ++e) acc[g][e] = f2_mul(acc[g][e], a2);
+        }
+        if (pv_on) {
+#pragma unroll 4
+          for (int r = rg; r < ntok; r += C::kRPI) {
+            const uint4 vv = lds128(vs + r * C::kRB + cpv * 16);
+            f2_t vf[EP2];
+            DT::widen2(vv, vf);
+#pragma unroll
+            for (int g = 0; g < GQ; ++g) {
+              const float pg = psw[r * GQ + g];
+              const f2_t p2 = f2_pack(pg, pg);
+#pragma unroll
+              for (int e = 0; e < EP2; ++e) acc[g][e] = f2_fma(p2, vf[e], acc[g][e]);
+            }
+          }
         }
       }
       __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
 
-      // ---- acc = acc * alpha + P.V
+    // ------------------------------------------------------------ combine
+    if (C::kShflRed) {
+#pragma unroll
+      for (int off = C::kNCH; off < 32; off <<= 1)
+#pragma unroll
+        for (int g = 0; g < GQ; ++g)
+#pragma unroll
+          for (int e = 0; e < EP2; ++e) {
+            float lo, hi, lo2, hi2;
+            f2_unpack(acc[g][e], lo, hi);
+            lo2 = __shfl_xor_sync(0xffffffffu, lo, off);
+            hi2 = __shfl_xor_sync(0xffffffffu, hi, off);
+            acc[g][e] = f2_pack(lo + lo2, hi + hi2);
+          }
+    }
+    if (lane == 0) {
 #pragma unroll
       for (int g = 0; g < GQ; ++g) {
-        const f2_t a2 = f2_pack(alpha[g], alpha[g]);
-#pragma unroll
-        for (int e = 0; e < EP2; ++e) acc[g][e] = f2_mul(acc[g][e], a2);
+        red_m[warp * GQ + g] = ok ? m_run[g] : -INFINITY;
+        red_l[warp * GQ + g] = ok ? l_run[g] : 0.f;
       }
-      if (pv_on) {
-#pragma unroll 4
-        for (int r = rg; r < ntok; r += C::kRPI) {
-          const uint4 vv = lds128(vs + r * C::kRB + cpv * 16);
-          f2_t vf[EP2];
-          DT::widen2(vv, vf);
+      if (!ok) atomicExch(&abort_flag, 1);
+    }
+    if (pv_on && (!C::kShflRed || rg == 0)) {
+      const int rr = C::kShflRed ? 0 : rg;
 #pragma unroll
-          for (int g = 0; g < GQ; ++g) {
-            const float pg = psw[r * GQ + g];
-            const f2_t p2 = f2_pack(pg, pg);
+      for (int g = 0; g < GQ; ++g)
 #pragma unroll
-            for (int e = 0; e < EP2; ++e) acc[g][e] = f2_fma(p2, vf[e], acc[g][e]);
-          }
+        for (int e = 0; e < EP2; ++e) {
+          float lo, hi;
+          f2_unpack(acc[g][e], lo, hi);
+          red_acc[((warp * C::kRedRows + rr) * GQ + g) * D + cpv * EPC + 2 * e] = lo;
+          red_acc[((warp * C::kRedRows + rr) * GQ + g) * D + cpv * EPC + 2 * e + 1] = hi;
         }
+    }
+    named_barrier_sync(1, C::kNW * 32);
+
+    const int64_t orow = p.out_rows ? p.out_rows[pc.row] : pc.row;
+    for (int o = threadIdx.x; o < GQ * D; o += C::kNW * 32) {
+      const int g = o / D;
+      const int d = o - g * D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < C::kNW; ++w) M = fmaxf(M, red_m[w * GQ + g]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < C::kNW; ++w) {
+        const float sc = exp2f(red_m[w * GQ + g] - M);
+        L += red_l[w * GQ + g] * sc;
+        float a = 0.f;
+#pragma unroll
+        for (int r = 0; r < C::kRedRows; ++r) a += red_acc[((w * C::kRedRows + r) * GQ + g) * D + d];
+        O += a * sc;
+      }
+      const float inv = 1.f / L;
+      const float lse_nat = (M + log2f(L)) * kLn2;
+      const int h = h0 + g;
+      if (pc.whole) {
+        store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
+        if (d == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)pc.row * p.lse_sn] = lse_nat;
+      } else {
+        const int64_t pidx = p.persistent ? ((int64_t)blockIdx.x * 2 + pc.slot) * GQ + g
+                                          : ((int64_t)pc.row * p.H + h) * p.max_splits + pc.slot;
+        p.part_o[pidx * D + d] = O * inv;
+        if (d == 0) p.part_lse[pidx] = lse_nat;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-  }
-
-  // -------------------------------------------------------------- combine
-  named_barrier_sync(1, C::kNW * 32);
-  float* red_m = reinterpret_cast<float*>(stages);
-  float* red_l = red_m + C::kNW * GQ;
-  float* red_acc = red_l + C::kNW * GQ;
-  if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-      red_m[warp * GQ + g] = ok ? m_run[g] : -INFINITY;
-      red_l[warp * GQ + g] = ok ? l_run[g] : 0.f;
-    }
-  }
-  if (pv_on) {
-#pragma unroll
-    for (int g = 0; g < GQ; ++g)
-#pragma unroll
-      for (int e = 0; e < EP2; ++e) {
-        float lo, hi;
-        f2_unpack(acc[g][e], lo, hi);
-        red_acc[((warp * C::kRPI + rg) * GQ + g) * D + cpv * EPC + 2 * e] = lo;
-        red_acc[((warp * C::kRPI + rg) * GQ + g) * D + cpv * EPC + 2 * e + 1] = hi;
-      }
-  }
-  named_barrier_sync(1, C::kNW * 32);
-
-  const bool single = (nsplits == 1);
-  const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-  for (int o = threadIdx.x; o < GQ * D; o += C::kNW * 32) {
-    const int g = o / D;
-    const int d = o - g * D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < C::kNW; ++w) M = fmaxf(M, red_m[w * GQ + g]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < C::kNW; ++w) {
-      const float sc = exp2f(red_m[w * GQ + g] - M);
-      L += red_l[w * GQ + g] * sc;
-      float a = 0.f;
-#pragma unroll
-      for (int r = 0; r < C::kRPI; ++r) a += red_acc[((w * C::kRPI + r) * GQ + g) * D + d];
-      O += a * sc;
-    }
-    const float inv = 1.f / L;
-    const float lse_nat = (M + log2f(L)) * kLn2;
-    const int h = h0 + g;
-    if (single) {
-      store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
-      if (d == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = lse_nat;
-    } else {
-      const int64_t pidx = ((int64_t)i * p.H + h) * p.max_splits + split;
-      p.part_o[pidx * D + d] = O * inv;
-      if (d == 0) p.part_lse[pidx] = lse_nat;
-    }
+    named_barrier_sync(1, C::kNW * 32);  // red_* is rewritten by the next piece
+    if (abort_flag) return;
   }
 }
 
-// Combine the split partials of rows that needed more than one split.
+// Split-grid schedule: combine the split partials of rows that needed more
+// than one split.
 __global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, int D) {
   extern __shared__ float wsm[];
   const int h = blockIdx.x;
@@ -509,6 +659,54 @@ __global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, in
   if (threadIdx.x == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = M + logf(L);
 }
 
+// Persistent schedule: a (row, kv-head chunk) segment cut by CTA range
+// boundaries has one partial per CTA that touched it; CTA c's range is
+// [c*T/N, (c+1)*T/N) of the T flattened tiles, so those CTAs are
+// cta(g0) .. cta(g1-1) with cta(t) = ((t+1)*N - 1) / T.  The first of them
+// holds the partial in its slot 0 if its range starts at the segment, else in
+// slot 1; every later one in slot 0 (CTAs with an empty range, possible when
+// T < N, wrote nothing and are skipped).  One CTA per (chunk, row).
+__global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
+  const int y = blockIdx.x;
+  const int i = blockIdx.y;
+  const int* P = p.ws_prefix;
+  const int nt = P[i + 1] - P[i];
+  if (nt == 0) return;
+  const int Y = p.KVH * p.gcs;
+  const int64_t N = p.ncta;
+  const int64_t T = (int64_t)P[p.n] * Y;
+  const int64_t g0 = (int64_t)P[i] * Y + (int64_t)y * nt;
+  const int64_t g1 = g0 + nt;
+  const int64_t c0 = ((g0 + 1) * N - 1) / T;
+  const int64_t c1 = (g1 * N - 1) / T;
+  if (c0 == c1) return;
+  const int first_slot = ((c0 * T) / N == g0) ? 0 : 1;
+  const int GQ = p.gq;
+  const int kh = y / p.gcs, gc = y - kh * p.gcs;
+  const int h0 = kh * p.G + gc * GQ;
+  const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+  for (int o = threadIdx.x; o < GQ * D; o += blockDim.x) {
+    const int g = o / D, d = o - g * D;
+    float M = -INFINITY;
+    for (int64_t c = c0; c <= c1; ++c) {
+      if ((c * T) / N == ((c + 1) * T) / N) continue;
+      const int64_t s = (c * 2 + (c == c0 ? first_slot : 0)) * GQ + g;
+      M = fmaxf(M, p.part_lse[s]);
+    }
+    float L = 0.f, O = 0.f;
+    for (int64_t c = c0; c <= c1; ++c) {
+      if ((c * T) / N == ((c + 1) * T) / N) continue;
+      const int64_t s = (c * 2 + (c == c0 ? first_slot : 0)) * GQ + g;
+      const float w = exp2f((p.part_lse[s] - M) * kLog2e);
+      L += w;
+      O = fmaf(w, p.part_o[s * D + d], O);
+    }
+    const int h = h0 + g;
+    store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O / L);
+    if (d == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = M + logf(L);
+  }
+}
+
 }  // namespace fdk
 
 // ============================================================== host side
@@ -518,37 +716,59 @@ namespace {
 using fdk::Cfg;
 using fdk::DecodeParams;
 
-constexpr int kTargetCtas = 148 * 2 * 8;  // ~8 waves at 2 CTAs per SM
+constexpr int kTargetCtas = 148 * 2 * 8;  // split grid: ~8 waves at 2 CTAs per SM
 
 struct Geometry {
   int TT, tiles_per_block, tiles_per_split, max_splits, G, GQ, gcs;
+  bool persistent;
   size_t ws_bytes;
+  // persistent workspace layout: partial o | partial lse | row-tile prefix
+  size_t off_lse, off_prefix;
 };
 
-typedef int (*launch_fn)(const DecodeParams&, dim3, cudaStream_t);
+// launch(p, grid, extra dynamic smem, stream) / resident CTAs per SM
+typedef int (*launch_fn)(const DecodeParams&, dim3, size_t, cudaStream_t);
+typedef int (*occ_fn)(int*);
 
 template <typename T, int D, int GQ>
-int launch_impl(const DecodeParams& p, dim3 grid, cudaStream_t s) {
+int launch_impl(const DecodeParams& p, dim3 grid, size_t extra, cudaStream_t s) {
   using C = Cfg<T, D, GQ>;
   static unsigned long long done = 0;
   auto kern = fdk::fd_decode_kernel<T, D, GQ>;
-  int st = fdh::ensure_smem(reinterpret_cast<const void*>(kern), C::kSmem, &done);
+  int st = fdh::ensure_smem(reinterpret_cast<const void*>(kern), C::kSmem + C::kPrefixMax, &done);
   if (st != FD_OK) return st;
-  kern<<<grid, C::kThreads, C::kSmem, s>>>(p);
+  kern<<<grid, C::kThreads, C::kSmem + extra, s>>>(p);
   return fdh::cuda_status(cudaGetLastError(), "fd_decode_kernel launch");
 }
 
 template <typename T, int D, int GQ>
-constexpr launch_fn pick() {
+int occupancy_impl(int* per_sm) {
+  using C = Cfg<T, D, GQ>;
+  static unsigned long long done = 0;
+  auto kern = fdk::fd_decode_kernel<T, D, GQ>;
+  int st = fdh::ensure_smem(reinterpret_cast<const void*>(kern), C::kSmem + C::kPrefixMax, &done);
+  if (st != FD_OK) return st;
+  return fdh::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, C::kThreads,
+                                                                        C::kSmem + C::kPrefixMax),
+                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+}
+
+struct KernelFns {
+  launch_fn launch;
+  occ_fn occupancy;
+};
+
+template <typename T, int D, int GQ>
+constexpr KernelFns pick() {
   if constexpr (Cfg<T, D, GQ>::kValid) {
-    return &launch_impl<T, D, GQ>;
+    return KernelFns{&launch_impl<T, D, GQ>, &occupancy_impl<T, D, GQ>};
   } else {
-    return nullptr;
+    return KernelFns{nullptr, nullptr};
   }
 }
 
 template <typename T, int D>
-launch_fn pick_gq(int gq) {
+KernelFns pick_gq(int gq) {
   switch (gq) {
     case 1:
       return pick<T, D, 1>();
@@ -557,12 +777,12 @@ launch_fn pick_gq(int gq) {
     case 4:
       return pick<T, D, 4>();
     default:
-      return nullptr;
+      return KernelFns{nullptr, nullptr};
   }
 }
 
 template <typename T>
-launch_fn pick_d(int D, int gq) {
+KernelFns pick_d(int D, int gq) {
   switch (D) {
     case 64:
       return pick_gq<T, 64>(gq);
@@ -575,11 +795,11 @@ launch_fn pick_d(int D, int gq) {
     case 256:
       return pick_gq<T, 256>(gq);
     default:
-      return nullptr;
+      return KernelFns{nullptr, nullptr};
   }
 }
 
-launch_fn pick_kernel(int dtype, int D, int gq) {
+KernelFns pick_kernel(int dtype, int D, int gq) {
   switch (dtype) {
     case FD_DTYPE_F16:
       return pick_d<__half>(D, gq);
@@ -588,7 +808,7 @@ launch_fn pick_kernel(int dtype, int D, int gq) {
     case FD_DTYPE_F32:
       return pick_d<float>(D, gq);
     default:
-      return nullptr;
+      return KernelFns{nullptr, nullptr};
   }
 }
 
@@ -596,7 +816,7 @@ launch_fn pick_kernel(int dtype, int D, int gq) {
 int choose_gq(int dtype, int D, int G) {
   const int opts[3] = {4, 2, 1};
   for (int gq : opts)
-    if (G % gq == 0 && pick_kernel(dtype, D, gq) != nullptr) return gq;
+    if (G % gq == 0 && pick_kernel(dtype, D, gq).launch != nullptr) return gq;
   return 0;
 }
 
@@ -618,6 +838,18 @@ int geometry(const fd_decode_args* a, Geometry* g) {
   const int64_t max_len =
       a->max_len > 0 ? (int64_t)a->max_len : (int64_t)a->bt_width * (int64_t)BS;
   const int64_t ntiles_max = std::max<int64_t>(1, (max_len + g->TT - 1) / g->TT);
+  g->persistent = (a->tiles_per_split <= 0 && a->n > 0 && a->n <= fdk::kMaxPersistentRows);
+  g->off_lse = g->off_prefix = 0;
+  if (g->persistent) {
+    // every CTA owns two partial slots of GQ heads
+    const size_t slots = (size_t)fdk::kMaxPersistentCtas * 2 * (size_t)g->GQ;
+    g->tiles_per_split = 0;
+    g->max_splits = 1;
+    g->off_lse = (slots * (size_t)a->head_size * 4 + 255) / 256 * 256;
+    g->off_prefix = g->off_lse + (slots * 4 + 255) / 256 * 256;
+    g->ws_bytes = g->off_prefix + ((size_t)(a->n + 1) * 4 + 255) / 256 * 256;
+    return FD_OK;
+  }
   int64_t tps = a->tiles_per_split;
   if (tps <= 0) {
     const int64_t ctas_per_row = (int64_t)a->num_kv_heads * g->gcs;
@@ -764,25 +996,61 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
   p.lse_sh = a->lse_stride_h;
   p.lse_sn = a->lse_stride_n;
   p.err = a->error;
-  if (g.max_splits > 1) {
+  p.gq = g.GQ;
+  if (g.ws_bytes > 0) {
     void* ws = ws_override != nullptr ? ws_override : a->workspace;
     const size_t ws_bytes = ws_override != nullptr ? ws_override_bytes : a->workspace_bytes;
     if (ws == nullptr || ws_bytes < g.ws_bytes)
       return fdh::fail(FD_ERR_WORKSPACE, "workspace of %zu bytes needed, got %zu", g.ws_bytes, ws_bytes);
     if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
       return fdh::fail(FD_ERR_ALIGN, "workspace must be 256-byte aligned");
-    const size_t rows = (size_t)a->n * (size_t)a->num_heads * (size_t)g.max_splits;
-    const size_t o_bytes = (rows * (size_t)D * 4 + 255) / 256 * 256;
-    p.part_o = static_cast<float*>(ws);
-    p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + o_bytes);
+    unsigned char* wb = static_cast<unsigned char*>(ws);
+    if (g.persistent) {
+      p.part_o = reinterpret_cast<float*>(wb);
+      p.part_lse = reinterpret_cast<float*>(wb + g.off_lse);
+      p.ws_prefix = reinterpret_cast<int*>(wb + g.off_prefix);
+    } else {
+      const size_t rows = (size_t)a->n * (size_t)a->num_heads * (size_t)g.max_splits;
+      const size_t o_bytes = (rows * (size_t)D * 4 + 255) / 256 * 256;
+      p.part_o = reinterpret_cast<float*>(wb);
+      p.part_lse = reinterpret_cast<float*>(wb + o_bytes);
+    }
   }
   if ((int64_t)a->num_kv_heads * g.gcs > 65535)
     return fdh::fail(FD_ERR_UNSUPPORTED, "too many heads for the grid");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const KernelFns fns = pick_kernel(a->dtype, D, g.GQ);
+  if (g.persistent) {
+    // as many CTAs as fit on the device at once (capped by the partial slots
+    // and by the tile count, at least 16 tiles each)
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fdh::cuda_status(e, "device attributes");
+    st = fns.occupancy(&per_sm);
+    if (st != FD_OK) return st;
+    const int64_t max_len =
+        a->max_len > 0 ? (int64_t)a->max_len : (int64_t)a->bt_width * (int64_t)a->block_size;
+    const int64_t tiles_max = (int64_t)a->n * ((max_len + g.TT - 1) / g.TT) * a->num_kv_heads * g.gcs;
+    int64_t ncta = std::min<int64_t>((int64_t)std::max(1, sms * std::max(1, per_sm)), fdk::kMaxPersistentCtas);
+    ncta = std::max<int64_t>(1, std::min<int64_t>(ncta, (tiles_max + 15) / 16));
+    p.persistent = 1;
+    p.ncta = (int)ncta;
+    if (launch_main) {
+      const size_t extra = ((size_t)(a->n + 1) * 4 + 15) / 16 * 16;
+      st = fns.launch(p, dim3((unsigned)ncta), extra, s);
+      if (st != FD_OK) return st;
+    }
+    if (launch_combine && ncta > 1) {
+      const int threads = g.GQ * D <= 128 ? 128 : 256;
+      fdk::fd_persistent_combine_kernel<<<dim3(a->num_kv_heads * g.gcs, a->n), threads, 0, s>>>(p, D);
+      st = fdh::cuda_status(cudaGetLastError(), "fd_persistent_combine_kernel launch");
+    }
+    return st;
+  }
   if (launch_main) {
-    launch_fn fn = pick_kernel(a->dtype, D, g.GQ);
     dim3 grid(g.max_splits, a->num_kv_heads * g.gcs, a->n);
-    st = fn(p, grid, s);
+    st = fns.launch(p, grid, 0, s);
     if (st != FD_OK) return st;
   }
   if (launch_combine && g.max_splits > 1) {
