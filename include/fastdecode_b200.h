@@ -190,7 +190,8 @@ FD_API int fd_decode_attn_combine(const fd_decode_args *a, void *stream);
  * (cudaGetSymbolAddress, with that device current) and caches it; make that
  * first call before any stream capture.  All calls share the one array and it
  * keeps the last call's contents; nothing in it needs to start at zero (every
- * partial is written by its split before the combine reads it).  Calls whose
+ * partial, and the row-tile prefix, is written by the decode kernel before
+ * the combine kernel of the same call reads it).  Calls whose
  * executions overlap on the GPU (other streams of the same device) race on
  * the array: order them, e.g. on one stream. */
 FD_API int fd_decode_attn_noalloc(const fd_decode_args *a, void *stream);

@@ -60,8 +60,13 @@ def test_host_side_argument_checks_need_no_gpu():
 
 def test_workspace_size_arithmetic():
     lib = nat.load()
-    # 16 rows of 32 heads, table width 128 blocks of 16: several splits -> nonzero
+    # persistent schedule (<= 1024 rows): partial slots + row prefix, always
     ws = lib.fd_decode_attn_paged_workspace_size(16, 32, 32, 128, 16, 128, 0)
     assert ws > 0 and ws % 256 == 0
-    # one tile per row: a single split, no scratch
-    assert lib.fd_decode_attn_paged_workspace_size(4, 8, 8, 64, 16, 1, 0) == 0
+    # the split grid (explicit tiles_per_split): none when every row fits one split
+    a = nat.FdDecodeArgs()
+    a.n, a.num_heads, a.num_kv_heads, a.head_size, a.block_size = 4, 8, 8, 64, 16
+    a.bt_width, a.dtype, a.tiles_per_split = 1, 0, 8
+    assert lib.fd_decode_workspace_size(ctypes.byref(a)) == 0
+    a.bt_width = 64  # 64 tiles per row, 8 per split -> 8 splits of partials
+    assert lib.fd_decode_workspace_size(ctypes.byref(a)) >= 4 * 8 * 8 * 64 * 4
