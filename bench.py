@@ -472,7 +472,17 @@ def run_reference(args, ws, rank, device):
     }
 
 
+def _emit(fd: int, line: dict) -> None:
+    os.write(fd, (json.dumps(line) + "\n").encode())
+
+
 def main() -> int:
+    # Only the JSON line may reach stdout: libraries (NCCL's version banner,
+    # warnings) write to fd 1 as well, so fd 1 points at stderr for the run
+    # and the result goes to the saved original stdout.
+    sys.stdout.flush()
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=0)
@@ -494,7 +504,7 @@ def main() -> int:
         device = torch.device("cuda", local) if torch.cuda.is_available() else None
         if device is not None:
             torch.cuda.set_device(device)
-        print(json.dumps(run_reference(args, ws, rank, device)), flush=True)
+        _emit(out_fd, run_reference(args, ws, rank, device))
         return 0
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -505,7 +515,7 @@ def main() -> int:
     try:
         line = run_ours(args, ws, rank, device)
         if rank == 0:
-            print(json.dumps(line), flush=True)
+            _emit(out_fd, line)
     finally:
         if ws > 1:
             torch.distributed.destroy_process_group()
