@@ -232,7 +232,8 @@ def test_decode_fp32_partials_and_row_maps(ops):
     o_or = torch.empty(n, H, D, dtype=torch.float32)
     O.decode_attn_tiered(q, (kc, vc), None, 1 << 40, bt, lens, D ** -0.5, o_or, None)
     got = out.cpu()
-    torch.testing.assert_close(got[out_rows], o_or, atol=2e-6, rtol=2e-6)
+    # fp32 output of 16-bit inputs: only the fp32 accumulation order differs
+    torch.testing.assert_close(got[out_rows], o_or, atol=1e-5, rtol=1e-5)
     untouched = torch.ones(T, dtype=torch.bool)
     untouched[out_rows] = False
     assert torch.all(got[untouched] == 0)
@@ -250,3 +251,31 @@ def test_decode_bad_block_id_sets_error(ops):
     with pytest.raises(RuntimeError, match="block id"):
         ops.check_device_errors(dev)
     ops.check_device_errors(dev)  # cleared
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("H,KVH", [(32, 8), (16, 8), (64, 8)])
+def test_decode_tensor_core_path_matches_cuda_core_path(ops, monkeypatch, dtype, H, KVH):
+    """The tcgen05 GQA kernel (query groups 2, 4, 8; head size 128) and the
+    CUDA-core kernel agree with each other and with the oracle, including rows
+    whose last stage is partial and an empty row."""
+    n, D, BS = 6, 128, 16
+    lens_l = [1, 129, 0, 1000, 2049, 77]
+    C = sum((x + BS - 1) // BS for x in lens_l) + 8
+    q, kc, vc, bt, lens = O.rand_case(n, H, KVH, D, BS, C, dtype, max_len=max(lens_l), seed=H)
+    lens = torch.tensor(lens_l, dtype=torch.int32)
+    perm = torch.randperm(C, generator=torch.Generator().manual_seed(H + 1)).tolist()
+    bt = torch.zeros(n, bt.shape[1], dtype=torch.int32)
+    for i, L in enumerate(lens_l):
+        nb = (L + BS - 1) // BS
+        bt[i, :nb] = torch.tensor([perm.pop() for _ in range(nb)], dtype=torch.int32)
+    scale = D ** -0.5
+    out_tc, lse_tc = _run_paged(ops, q, kc, vc, bt, lens, scale)
+    _compare(q, kc, vc, bt, lens, scale, out_tc, lse_tc)
+    monkeypatch.setenv("FASTDECODE_B200_MMA", "0")
+    out_cc, lse_cc = _run_paged(ops, q, kc, vc, bt, lens, scale)
+    _compare(q, kc, vc, bt, lens, scale, out_cc, lse_cc)
+    nz = lens > 0
+    t = TOL_ORACLE[dtype]
+    torch.testing.assert_close(out_tc[nz].float(), out_cc[nz].float(), atol=t, rtol=t)
+    assert (lse_tc[:, nz] - lse_cc[:, nz]).abs().max().item() <= LSE_TOL

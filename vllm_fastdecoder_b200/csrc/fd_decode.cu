@@ -22,66 +22,24 @@
 
 #include <math.h>
 
+#include <stdlib.h>
+
 #include <algorithm>
 #include <mutex>
 
 #include <cudaTypedefs.h>
 
 #include "fd_common.cuh"
+#include "fd_decode.cuh"
 #include "fd_internal.h"
 
 namespace fdk {
-
-struct alignas(64) DecodeParams {
-  // tiled-TMA descriptors of device tiers whose tiles are not contiguous
-  // (dims {D, KVH, BS, blocks}, box {D, 1, TT, 1}); used when use_tmap[t]
-  CUtensorMap tmap_k[2];
-  CUtensorMap tmap_v[2];
-  int use_tmap[2];
-  const unsigned char* q;
-  int64_t q_sn, q_sh;  // bytes
-  const int64_t* q_rows;
-  const unsigned char* k[2];
-  const unsigned char* v[2];
-  int64_t blk_sb[2], head_sb[2], tok_sb[2];  // bytes
-  int64_t nblk[2];
-  int host[2];
-  int contig[2];
-  int64_t split;
-  const int32_t* bt;
-  int64_t bt_stride;
-  int bt_width;
-  const int32_t* lens;
-  int n, H, KVH, BS, G, gcs, gq;
-  int TT, tiles_per_block, tiles_per_split, max_splits;
-  // persistent schedule: ncta CTAs share the flattened (row, kv-head chunk,
-  // tile) space evenly; prefix of per-row tile counts published in ws_prefix
-  int persistent, ncta;
-  int* ws_prefix;
-  float qscale;  // scale * log2(e)
-  void* out;
-  int out_dtype;
-  int64_t out_sn, out_sh;  // elements
-  const int64_t* out_rows;
-  float* lse;
-  int64_t lse_sh, lse_sn;
-  float* part_o;
-  float* part_lse;
-  int32_t* err;
-};
 
 constexpr int p2div(int x, int p) { return (x % (2 * p) == 0 && 2 * p <= 32) ? p2div(x, 2 * p) : p; }
 constexpr int ceil_pow2(int x, int p) { return p >= x ? p : ceil_pow2(x, 2 * p); }
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 constexpr int round128(int x) { return (x + 127) / 128 * 128; }
-
-// Largest row count handled by the persistent schedule (its per-row tile
-// prefix sits in shared memory).
-constexpr int kMaxPersistentRows = 1024;
-// Upper bound on persistent CTAs (2 per SM on 148 SMs, with headroom); sizes
-// the partial slots of the workspace.
-constexpr int kMaxPersistentCtas = 320;
 
 template <typename T, int D, int GQ>
 struct Cfg {
@@ -115,15 +73,7 @@ struct Cfg {
   static constexpr int kSmem = kBarBytes + kPsBytes + kRedBytes + kNST * kStageBytes;
   static constexpr int kPrefixMax = round128((kMaxPersistentRows + 1) * 4);
   static constexpr bool kValid = (kRB % 16 == 0) && kNCH <= 32 && (GQ * kCPL * kEPC <= 64 || GQ == 1) &&
-                                 2 * kNST * 8 <= kBarBytes && kSmem + kPrefixMax <= 227 * 1024;
-};
-
-// One piece of work: tiles [t0, t1) of row `row` for kv-head chunk y.  A piece
-// covering its whole (row, chunk) segment writes the final output; otherwise
-// it writes an fp32 partial into `slot`.
-struct Piece {
-  int row, y, t0, t1, len, slot;
-  bool whole;
+                                 (2 * kNST + 2) * 8 <= kBarBytes && kSmem + kPrefixMax <= 227 * 1024;
 };
 
 template <typename T, int D, int GQ>
@@ -136,6 +86,8 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + C::kNST;
+  uint64_t* comb_full = empty + C::kNST;  // 4 consumer warps wrote their piece state
+  uint64_t* comb_done = comb_full + 1;    // 4 consumer warps finished the piece outputs
   float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes);
   float* red_m = reinterpret_cast<float*>(smem + C::kBarBytes + C::kPsBytes);
   float* red_l = red_m + C::kNW * GQ;
@@ -178,6 +130,8 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
       mbar_init(&full[s], 32);
       mbar_init(&empty[s], C::kNW);
     }
+    mbar_init(comb_full, C::kNW);
+    mbar_init(comb_done, C::kNW);
     fence_barrier_init();
   }
   __syncthreads();
@@ -409,6 +363,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   const bool pv_on = lane < C::kPVL;
   float* psw = ps_all + warp * C::kMaxTT * GQ;
   int k = 0;
+  uint32_t npieces = 0;
   Piece pc;
   while (next_piece(pc)) {
     const int kh = pc.y / p.gcs;
@@ -592,7 +547,9 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
           red_acc[((warp * C::kRedRows + rr) * GQ + g) * D + cpv * EPC + 2 * e + 1] = hi;
         }
     }
-    named_barrier_sync(1, C::kNW * 32);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(comb_full);
+    if (!mbar_wait(comb_full, npieces & 1u, p.err)) return;
 
     const int64_t orow = p.out_rows ? p.out_rows[pc.row] : pc.row;
     for (int o = threadIdx.x; o < GQ * D; o += C::kNW * 32) {
@@ -624,7 +581,11 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         if (d == 0) p.part_lse[pidx] = lse_nat;
       }
     }
-    named_barrier_sync(1, C::kNW * 32);  // red_* is rewritten by the next piece
+    // red_* is rewritten by the next piece
+    __syncwarp();
+    if (lane == 0) mbar_arrive(comb_done);
+    if (!mbar_wait(comb_done, npieces & 1u, p.err)) return;
+    ++npieces;
     if (abort_flag) return;
   }
 }
@@ -721,6 +682,7 @@ constexpr int kTargetCtas = 148 * 2 * 8;  // split grid: ~8 waves at 2 CTAs per 
 struct Geometry {
   int TT, tiles_per_block, tiles_per_split, max_splits, G, GQ, gcs;
   bool persistent;
+  bool mma;  // tcgen05 GQA kernel (fd_decode_mma.cu)
   size_t ws_bytes;
   // persistent workspace layout: partial o | partial lse | row-tile prefix
   size_t off_lse, off_prefix;
@@ -840,6 +802,13 @@ int geometry(const fd_decode_args* a, Geometry* g) {
   const int64_t ntiles_max = std::max<int64_t>(1, (max_len + g->TT - 1) / g->TT);
   g->persistent = (a->tiles_per_split <= 0 && a->n > 0 && a->n <= fdk::kMaxPersistentRows);
   g->off_lse = g->off_prefix = 0;
+  const char* mma_env = getenv("FASTDECODE_B200_MMA");
+  g->mma = g->persistent && fdk::mma_eligible(a->dtype, a->head_size, g->G, BS) &&
+           !(mma_env != nullptr && mma_env[0] == '0');
+  if (g->mma) {  // one CTA handles the whole query group of a kv head
+    g->GQ = g->G;
+    g->gcs = 1;
+  }
   if (g->persistent) {
     // every CTA owns two partial slots of GQ heads
     const size_t slots = (size_t)fdk::kMaxPersistentCtas * 2 * (size_t)g->GQ;
@@ -899,7 +868,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // {D, 1, TT, 1}.  Returns false when the driver rejects it (the caller then
 // copies tile rows one by one).
 bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
-                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT) {
+                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128 = false) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (enc == nullptr || nblk <= 0 || nblk > (int64_t)0xffffffff) return false;
   CUtensorMapDataType dt = dtype == FD_DTYPE_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -907,11 +876,12 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)KVH, (cuuint64_t)BS, (cuuint64_t)nblk};
   const cuuint64_t strides[3] = {(cuuint64_t)head_sb, (cuuint64_t)tok_sb, (cuuint64_t)blk_sb};
-  const cuuint32_t box[4] = {(cuuint32_t)D, 1u, (cuuint32_t)TT, 1u};
+  // swizzled: 128-byte box rows (64 16-bit dims), the layout the UMMA reads
+  const cuuint32_t box[4] = {swizzle128 ? 64u : (cuuint32_t)D, 1u, (cuuint32_t)TT, 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -961,13 +931,21 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
       if (!fdh::aligned16(tr.k) || !fdh::aligned16(tr.v) || p.blk_sb[t] % 16 != 0 ||
           p.head_sb[t] % 16 != 0 || p.tok_sb[t] % 16 != 0)
         return fdh::fail(FD_ERR_ALIGN, "tier %d K/V pointers and strides must be 16-byte aligned", t);
-      if (!p.host[t] && !p.contig[t] && launch_main) {
+      if (!p.host[t] && (!p.contig[t] || g.mma)) {
         const bool ok_k = encode_tier_map(&p.tmap_k[t], tr.k, a->dtype, D, a->num_kv_heads, a->block_size,
-                                          p.nblk[t], p.head_sb[t], p.tok_sb[t], p.blk_sb[t], g.TT);
+                                          p.nblk[t], p.head_sb[t], p.tok_sb[t], p.blk_sb[t], g.TT, g.mma);
         const bool ok_v = ok_k && encode_tier_map(&p.tmap_v[t], tr.v, a->dtype, D, a->num_kv_heads,
                                                   a->block_size, p.nblk[t], p.head_sb[t], p.tok_sb[t],
-                                                  p.blk_sb[t], g.TT);
+                                                  p.blk_sb[t], g.TT, g.mma);
         p.use_tmap[t] = (ok_k && ok_v) ? 1 : 0;
+        if (g.mma && !p.use_tmap[t]) {
+          // the tensor-core kernel needs swizzled tiles: use the CUDA-core kernel
+          g.mma = false;
+          g.GQ = choose_gq(a->dtype, D, g.G);
+          g.gcs = g.G / g.GQ;
+          t = -1;  // re-encode every tier for the CUDA-core kernel
+          continue;
+        }
       }
     }
   }
@@ -1027,8 +1005,12 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return fdh::cuda_status(e, "device attributes");
-    st = fns.occupancy(&per_sm);
-    if (st != FD_OK) return st;
+    if (g.mma) {
+      per_sm = 1;  // the tensor-core kernel takes most of an SM's shared memory
+    } else {
+      st = fns.occupancy(&per_sm);
+      if (st != FD_OK) return st;
+    }
     const int64_t max_len =
         a->max_len > 0 ? (int64_t)a->max_len : (int64_t)a->bt_width * (int64_t)a->block_size;
     const int64_t tiles_max = (int64_t)a->n * ((max_len + g.TT - 1) / g.TT) * a->num_kv_heads * g.gcs;
@@ -1036,8 +1018,24 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     ncta = std::max<int64_t>(1, std::min<int64_t>(ncta, (tiles_max + 15) / 16));
     p.persistent = 1;
     p.ncta = (int)ncta;
-    if (launch_main) {
-      const size_t extra = ((size_t)(a->n + 1) * 4 + 15) / 16 * 16;
+    const size_t extra = ((size_t)(a->n + 1) * 4 + 15) / 16 * 16;
+    if (g.mma) {
+      // the tensor-core kernel runs one CTA per SM; the combine must see the
+      // same CTA count, so it is computed even when only combining
+      int n_mma = (int)ncta;
+      bool launched = false;
+      DecodeParams pm = p;
+      pm.ncta = n_mma;
+      if (launch_main) {
+        st = fdk::launch_decode_mma(pm, a->dtype, D, extra, s, &n_mma, &launched);
+        if (st != FD_OK) return st;
+        if (!launched) return fdh::fail(FD_ERR_UNSUPPORTED, "tensor-core decode kernel declined the call");
+      } else {
+        n_mma = std::max(1, std::min((int)ncta, std::min(sms, fdk::kMaxPersistentCtas)));
+      }
+      p.ncta = n_mma;
+      ncta = n_mma;
+    } else if (launch_main) {
       st = fns.launch(p, dim3((unsigned)ncta), extra, s);
       if (st != FD_OK) return st;
     }
