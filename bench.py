@@ -29,6 +29,7 @@ source into oracle/_ref) on this host's cores.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -247,6 +248,8 @@ def run_ours(args, ws, rank, device):
         batch = workloads.config3(world=ws, rank=rank)
     else:
         batch = workloads.CONFIGS[args.workload]()
+    if args.layout and batch.num_hbm_blocks > 0:
+        batch = dataclasses.replace(batch, hbm_layout=args.layout)
     res = workloads.materialize(batch, device)
     n, H, D = batch.n, batch.H, batch.D
     sharded = args.workload == "c3" and ws > 1
@@ -491,6 +494,9 @@ def main() -> int:
     ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3"], default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
+    ap.add_argument("--layout", choices=["nhd", "hnd"], default=None,
+                    help="HBM-tier layout: nhd = vLLM [B, BS, KVH, 2D]; hnd = [2, B, KVH, BS, D] "
+                         "(default: the workload's own)")
     args = ap.parse_args()
     if args.impl == "reference":
         args.split_grid = False

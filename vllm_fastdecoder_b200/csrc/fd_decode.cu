@@ -70,7 +70,7 @@ struct Cfg {
   static constexpr int kBarBytes = 128;
   static constexpr int kPsBytes = round128(kNW * kMaxTT * GQ * 4);
   static constexpr int kRedBytes = round128((2 * kNW * GQ + kNW * kRedRows * GQ * D) * 4);
-  static constexpr int kSmem = kBarBytes + kPsBytes + kRedBytes + kNST * kStageBytes;
+  static constexpr int kSmem = kBarBytes + kIdRingBytes + kPsBytes + kRedBytes + kNST * kStageBytes;
   static constexpr int kPrefixMax = round128((kMaxPersistentRows + 1) * 4);
   static constexpr bool kValid = (kRB % 16 == 0) && kNCH <= 32 && (GQ * kCPL * kEPC <= 64 || GQ == 1) &&
                                  (2 * kNST + 2) * 8 <= kBarBytes && kSmem + kPrefixMax <= 227 * 1024;
@@ -88,11 +88,12 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   uint64_t* empty = full + C::kNST;
   uint64_t* comb_full = empty + C::kNST;  // 4 consumer warps wrote their piece state
   uint64_t* comb_done = comb_full + 1;    // 4 consumer warps finished the piece outputs
-  float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes);
-  float* red_m = reinterpret_cast<float*>(smem + C::kBarBytes + C::kPsBytes);
+  int* id_ring = reinterpret_cast<int*>(smem + C::kBarBytes);
+  float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes + kIdRingBytes);
+  float* red_m = reinterpret_cast<float*>(smem + C::kBarBytes + kIdRingBytes + C::kPsBytes);
   float* red_l = red_m + C::kNW * GQ;
   float* red_acc = red_l + C::kNW * GQ;
-  unsigned char* stages = smem + C::kBarBytes + C::kPsBytes + C::kRedBytes;
+  unsigned char* stages = smem + C::kBarBytes + kIdRingBytes + C::kPsBytes + C::kRedBytes;
   int* prefix = reinterpret_cast<int*>(stages + C::kNST * C::kStageBytes);
   __shared__ int abort_flag;
 
@@ -244,15 +245,40 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   if (warp == C::kNW) {
     // ------------------------------------------------------------ producer
     const uint64_t pol = l2_evict_first_policy();
+    // block ids kIdAhead stages ahead (cp.async ring), q of coming pieces
+    // prefetched into L2 for the consumers
+    IdPrefetch ids;
+    if (p.persistent) {
+      ids.it.init(g_cur, g_end, row_cur, prefix, nullptr, p.n, Y, C::kNW);
+    } else {
+      Piece sp;
+      const int i = blockIdx.z;
+      const int ntiles = (p.lens[i] + p.TT - 1) / p.TT;
+      sp.row = i;
+      sp.y = blockIdx.y;
+      sp.t0 = blockIdx.x * p.tiles_per_split;
+      sp.t1 = min(ntiles, sp.t0 + p.tiles_per_split);
+      sp.len = 0;
+      sp.whole = false;
+      sp.slot = 0;
+      ids.it.init_single(sp, C::kNW);
+    }
+    ids.ring = id_ring;
+    ids.issued = 0;
+    for (int i = 0; i < kIdAhead; ++i) ids.push(p, lane, GQ, C::kRB);
     int k = 0;
     Piece pc;
     while (next_piece(pc)) {
       const int kh = pc.y / p.gcs;
-      const int32_t* btrow = p.bt + (int64_t)pc.row * p.bt_stride;
       for (int t = pc.t0; t < pc.t1; t += C::kNW, ++k) {
+        ids.push(p, lane, GQ, C::kRB);  // stage k + kIdAhead
+        const int64_t id_k = ids.take(k, lane);
         const int st = k % C::kNST;
         const uint32_t use = (uint32_t)(k / C::kNST);
-        if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1u, p.err)) return;
+        if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1u, p.err)) {
+          cp_async_wait<0>();
+          return;
+        }
         unsigned char* sbase = stages + st * C::kStageBytes;
         const int tile = t + lane;
         int tier = 0;
@@ -263,7 +289,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         if (lane < C::kNW && tile < pc.t1) {
           const int b = tile / p.tiles_per_block;
           r0 = (tile - b * p.tiles_per_block) * p.TT;
-          int64_t id = btrow[b];
+          int64_t id = id_k;
           if (id >= p.split) {
             tier = 1;
             id -= p.split;
@@ -284,32 +310,33 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         if (lane == 0 && bulk_mask != 0u)
           mbar_expect_tx(&full[st], (uint32_t)__popc(bulk_mask) * 2u * tile_bytes);
         __syncwarp();
-        for (unsigned m = bulk_mask; m != 0u; m &= m - 1u) {
+        // contiguous tiles and tensor-map tiles: each lane issues its own
+        // tile's two copies (no cross-lane traffic on the issue path)
+        const bool own = bulk && (p.contig[tier] || p.use_tmap[tier]);
+        if (own) {
+          unsigned char* kd = sbase + (2 * lane) * C::kTileSlot;
+          unsigned char* vd = kd + C::kTileSlot;
+          if (p.contig[tier]) {
+            bulk_g2s(kd, ks, tile_bytes, &full[st], pol);
+            bulk_g2s(vd, vs, tile_bytes, &full[st], pol);
+          } else {
+            tma_load_4d(kd, &p.tmap_k[tier], 0, kh, r0, blk_id, &full[st], pol);
+            tma_load_4d(vd, &p.tmap_v[tier], 0, kh, r0, blk_id, &full[st], pol);
+          }
+        }
+        // other device tiles: one bulk copy per token row, rows spread over lanes
+        for (unsigned m = bulk_mask & ~__ballot_sync(0xffffffffu, own); m != 0u; m &= m - 1u) {
           const int w = __ffs(m) - 1;
           const unsigned char* kw = reinterpret_cast<const unsigned char*>(
               __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ks), w));
           const unsigned char* vw = reinterpret_cast<const unsigned char*>(
               __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
           const int tr = __shfl_sync(0xffffffffu, tier, w);
-          const int bid = __shfl_sync(0xffffffffu, blk_id, w);
-          const int row0 = __shfl_sync(0xffffffffu, r0, w);
           unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
           unsigned char* vd = kd + C::kTileSlot;
-          if (p.contig[tr]) {
-            if (lane == 0) {
-              bulk_g2s(kd, kw, tile_bytes, &full[st], pol);
-              bulk_g2s(vd, vw, tile_bytes, &full[st], pol);
-            }
-          } else if (p.use_tmap[tr]) {
-            if (lane == 0) {
-              tma_load_4d(kd, &p.tmap_k[tr], 0, kh, row0, bid, &full[st], pol);
-              tma_load_4d(vd, &p.tmap_v[tr], 0, kh, row0, bid, &full[st], pol);
-            }
-          } else {
-            for (int r = lane; r < p.TT; r += 32) {
-              bulk_g2s(kd + r * C::kRB, kw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
-              bulk_g2s(vd + r * C::kRB, vw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
-            }
+          for (int r = lane; r < p.TT; r += 32) {
+            bulk_g2s(kd + r * C::kRB, kw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
+            bulk_g2s(vd + r * C::kRB, vw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
           }
         }
         for (unsigned m = host_mask; m != 0u; m &= m - 1u) {
@@ -351,6 +378,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         mbar_arrive(&full[st]);
       }
     }
+    cp_async_wait<0>();  // no id copy outlives the CTA
     return;
   }
 

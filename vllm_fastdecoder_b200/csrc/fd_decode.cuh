@@ -8,6 +8,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "fd_common.cuh"
+
 namespace fdk {
 
 struct alignas(64) DecodeParams {
@@ -61,6 +63,154 @@ constexpr int kMaxPersistentCtas = 320;
 struct Piece {
   int row, y, t0, t1, len, slot;
   bool whole;
+};
+
+// Enumerates one CTA's stages (up to `tps` consecutive tiles of one piece):
+// the pieces of its persistent tile range [g0, g1), or the single piece of a
+// split-grid CTA.  Every role of a kernel runs its own copy over the same
+// sequence.  prefix/lens may live in shared memory; lens may be null when
+// the caller does not need Piece::len.
+struct StageIter {
+  int64_t g_cur, g_end;
+  const int* prefix;
+  const int* lens;
+  int n, Y, tps;
+  int row_cur;
+  bool first, have, single;
+  Piece pc;
+  int t;       // first tile of the next stage of pc
+  int pieces;  // pieces started so far
+
+  __device__ void init(int64_t g0, int64_t g1, int row, const int* prefix_s, const int* lens_s, int n_rows, int y,
+                       int tiles_per_stage) {
+    g_cur = g0;
+    g_end = g1;
+    prefix = prefix_s;
+    lens = lens_s;
+    n = n_rows;
+    Y = y;
+    tps = tiles_per_stage;
+    row_cur = row;
+    first = true;
+    have = false;
+    single = false;
+    t = 0;
+    pieces = 0;
+  }
+
+  __device__ void init_single(const Piece& piece, int tiles_per_stage) {
+    pc = piece;
+    g_cur = 0;
+    g_end = 1;
+    tps = tiles_per_stage;
+    first = false;
+    have = false;
+    single = true;
+    t = 0;
+    pieces = 0;
+  }
+
+  __device__ bool next_piece() {
+    if (g_cur >= g_end) return false;
+    if (single) {
+      g_cur = g_end;
+      return true;
+    }
+    const int nt = prefix[row_cur + 1] - prefix[row_cur];
+    const int64_t local = g_cur - (int64_t)prefix[row_cur] * Y;
+    const int y = (int)(local / nt);
+    const int t0 = (int)(local - (int64_t)y * nt);
+    const int t1 = (int)min((int64_t)nt, (int64_t)t0 + (g_end - g_cur));
+    pc.row = row_cur;
+    pc.y = y;
+    pc.t0 = t0;
+    pc.t1 = t1;
+    pc.len = lens != nullptr ? lens[row_cur] : 0;
+    pc.whole = (t0 == 0 && t1 == nt);
+    pc.slot = first ? 0 : 1;
+    first = false;
+    g_cur += t1 - t0;
+    if (t1 == nt && y == Y - 1) {
+      do {
+        ++row_cur;
+      } while (row_cur < n && prefix[row_cur + 1] == prefix[row_cur]);
+    }
+    return true;
+  }
+
+  // Next stage: tiles [st_t0, st_t1) of piece pc; flags for piece bounds.
+  __device__ bool next(int& st_t0, int& st_t1, bool& piece_first, bool& piece_last) {
+    if (!have || t >= pc.t1) {
+      if (!next_piece()) return false;
+      have = true;
+      t = pc.t0;
+      ++pieces;
+      piece_first = true;
+    } else {
+      piece_first = false;
+    }
+    st_t0 = t;
+    st_t1 = min(pc.t1, t + tps);
+    t = st_t1;
+    piece_last = (t >= pc.t1);
+    return true;
+  }
+};
+
+// Producer-side lookahead of block-table entries.  A table entry read at the
+// moment its tiles are issued costs a loaded-HBM round trip (1-2 us) per
+// stage, which alone caps a CTA's stream; instead lane j fetches the entry of
+// tile j of stage k + kIdAhead with cp.async into ring slot
+// (k + kIdAhead) % kIdRing, one commit group per stage, and stage k reads its
+// slot after cp.async.wait_group(kIdAhead).  At a piece's first stage the
+// piece's q rows are prefetched into L2 at the same distance.
+constexpr int kIdAhead = 6;
+constexpr int kIdRing = 8;   // > kIdAhead: a slot is rewritten only after its stage read it
+constexpr int kIdLanes = 8;  // tiles per stage, at most
+constexpr int kIdRingBytes = kIdRing * kIdLanes * 4;
+
+struct IdPrefetch {
+  StageIter it;  // runs kIdAhead stages ahead of the producer
+  int* ring;     // shared memory [kIdRing][kIdLanes]
+  int issued;    // stages whose ids were requested
+
+  // Request stage `issued`'s ids and commit one group, possibly empty, so
+  // group counting stays uniform.  Lane j < nlanes fetches tile
+  // first_tile + j of the stage.  A piece's q is heads_per_piece rows of
+  // row_bytes from head y * heads_per_piece on (heads_per_piece 0: no q
+  // prefetch).
+  __device__ void push(const DecodeParams& p, int lane, int heads_per_piece, int row_bytes, int first_tile = 0,
+                       int nlanes = kIdLanes) {
+    int a0, a1;
+    bool apf, apl;
+    if (it.next(a0, a1, apf, apl)) {
+      const int tile = a0 + first_tile + lane;
+      if (lane < nlanes && tile < a1)
+        cp_async4(ring + (issued % kIdRing) * kIdLanes + lane,
+                  p.bt + (int64_t)it.pc.row * p.bt_stride + tile / p.tiles_per_block);
+      if (apf && heads_per_piece > 0) {
+        if (p.q_rows != nullptr) {
+          if (lane == 0) prefetch_l2(p.q_rows + it.pc.row);
+        } else {
+          const unsigned char* q0 = p.q + (int64_t)it.pc.row * p.q_sn;
+          const int lph = (row_bytes + 127) >> 7;  // lines per head row, each starting inside the row
+          for (int l = lane; l < heads_per_piece * lph; l += 32) {
+            const int h = l / lph;
+            prefetch_l2(q0 + (int64_t)(it.pc.y * heads_per_piece + h) * p.q_sh + (l - h * lph) * 128);
+          }
+        }
+      }
+      ++issued;
+    }
+    cp_async_commit();
+  }
+
+  // The ids of stage k (this lane's tile) after the prologue pushed
+  // kIdAhead stages and stage k pushed its own lookahead.
+  __device__ int64_t take(int k, int lane) {
+    cp_async_wait<kIdAhead>();
+    return (int64_t)ring[(k % kIdRing) * kIdLanes + (lane & (kIdLanes - 1))];
+  }
 };
 
 // Launch hook of the tcgen05 GQA kernel (fd_decode_mma.cu): returns FD_OK and

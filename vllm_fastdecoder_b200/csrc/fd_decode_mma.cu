@@ -4,24 +4,30 @@
 // decode attention are small matrix products per 128-token stage:
 //   S^T [128 tokens x 8] = K [128 x 128] . q^T [128 x 8]       (q.K^T)
 //   O^T [128 dims  x 8] = V^T [128 x 128] . P^T [128 x 8]      (P.V)
-// (the group padded to the MMA's N = 16).  One CTA per SM, six warps:
-//   warp 4   TMA producer: K and V tiles (16 tokens, one kv head) into a
-//            3-stage ring in the 128-byte-swizzled layout the MMA reads
-//            (tiled TMA, box {64 dims, 1, 16, 1}); host-tier tiles by
-//            16-byte loads stored with the same swizzle; q of each piece
-//   warp 5   MMA issuer: one thread issues tcgen05.mma into TMEM (S and O
-//            double-buffered, 64 columns) and tcgen05.commit to mbarriers;
-//            q.K^T of stage k+1 is issued before P.V of stage k
+// (the group padded to the MMA's N = 16).  One CTA per SM, seven warps:
+//   warps 4, 6  TMA producers: K and V tiles (16 tokens, one kv head) into
+//            a 3-stage ring in the 128-byte-swizzled layout the MMA reads
+//            (tiled TMA, box {64 dims, 1, 16, 1}), four tiles of a stage
+//            each; host-tier tiles by 16-byte loads stored with the same
+//            swizzle; warp 4 also stages q of each piece.  Block ids are
+//            fetched six stages ahead (cp.async ring).
+//   warp 5   MMA issuer: one thread polls the barriers and issues
+//            tcgen05.mma into TMEM (S and O double-buffered, 64 columns) for
+//            whichever product is ready, q.K^T up to two stages ahead of
+//            P.V; tcgen05.commit to mbarriers
 //   warps 0-3  softmax: thread r owns token row r of S (TMEM lane r): scale,
-//            mask, block max (per stage), exp2, P written as 16-bit into the
-//            swizzled B operand; then thread d owns dim d of O (TMEM lane d)
-//            and folds it into an fp32 accumulator with the online-softmax
-//            rescale.  Per-thread partial sums of p give the denominator.
+//            mask, block max (per stage, butterfly over the group), exp2, P
+//            written as 16-bit pairs into the swizzled B operand; then thread
+//            d owns dim d of O (TMEM lane d) and folds the PREVIOUS stage's O
+//            into an fp32 accumulator with the online-softmax rescale, so a
+//            stage's P.V round trip overlaps the next stage's softmax.
+//            Per-thread partial sums of p give the denominator.
 // The schedule is the persistent one of fd_decode.cu (equal tile ranges per
 // CTA, pieces, two partial slots per CTA, fd_persistent_combine_kernel).
 // Numerics: scores and softmax in fp32 from the exact 16-bit q and K; P
-// enters the P.V product as a sum of two 16-bit values (hi + lo, in the
-// padding rows of the N = 16 operand), so P.V keeps nearly fp32 precision;
+// enters the P.V product as a sum of two 16-bit values (hi in rows 0..G-1,
+// lo in rows G..2G-1 of the N = 16 operand), so P.V keeps nearly fp32
+// precision;
 // all accumulation fp32.
 
 #include <math.h>
@@ -45,9 +51,12 @@ constexpr int kNST = 3;             // stages in the ring
 constexpr int kPanel = kTok * 128;  // 128 token rows x 128 B (64 dims)
 constexpr int kKV = 2 * kPanel;     // K or V of one stage (32 KB)
 constexpr int kStage = 2 * kKV;     // K + V (64 KB)
+static_assert(kTilesPerStage % 2 == 0, "tiles split between two producer warps");
 constexpr int kQB = 2 * kN * 128;   // q: two panels of 16 rows x 128 B
 constexpr int kPB = 2 * kN * 128;   // P: two panels (tokens 0-63, 64-127) x 16 rows
-constexpr int kThreads = 6 * 32;
+constexpr int kProd = 2;                         // producer warps (4 and 6), 4 tiles of a stage each
+constexpr int kTilesPerProd = kTilesPerStage / kProd;
+constexpr int kThreads = (4 + 1 + kProd) * 32;
 constexpr int kTmemCols = 4 * kN;  // S0 S1 O0 O1, kN columns each
 
 constexpr int kOffQ = kNST * kStage;
@@ -57,9 +66,12 @@ constexpr int kOffL = kOffRed + 2 * 4 * kN * 4;  // [4 warps][kN] floats: per-pi
 constexpr int kOffBar = kOffL + 4 * kN * 4;
 constexpr int kNumBars = 3 + 3 + 2 * 7 + 1 + 2 + 1;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
-constexpr int kOffPrefix = (kOffTmem + 16 + 127) / 128 * 128;
+constexpr int kOffIds = (kOffTmem + 16 + 127) / 128 * 128;  // producer's block-id ring
+constexpr int kOffPrefix = kOffIds + kProd * kIdRingBytes;
 constexpr int kSmemFixed = kOffPrefix + 1024;  // + 1024 for aligning the base
-static_assert(kSmemFixed + (kMaxPersistentRows + 1) * 4 <= 227 * 1024, "smem budget");
+// the tile prefix [n + 1] and the lengths [n] follow, 16-byte aligned each
+constexpr int kRowsBytes = (kMaxPersistentRows + 1 + 3) / 4 * 16;
+static_assert(kSmemFixed + 2 * kRowsBytes <= 227 * 1024, "smem budget");
 
 // UMMA shared-memory descriptor, 128-byte swizzle, sm_100 version bits.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -102,81 +114,42 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 16 consecutive 32-bit columns starting at taddr.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t bits16(__half x) { return __half_as_ushort(x); }
+__device__ __forceinline__ uint32_t bits16(__nv_bfloat16 x) { return __bfloat16_as_ushort(x); }
+
 // Byte offset of 16-byte chunk c (0..7) of row r inside 128-byte-swizzled
 // rows (the 8-row atom pattern of TMA SWIZZLE_128B / UMMA SWIZZLE_128B).
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-// Stage enumeration shared by the three roles: a stage is up to 8 tiles of
-// one piece.
-struct StageIter {
-  int64_t g_cur, g_end;
-  int row_cur;
-  bool first, split_done, have;
+// One stage as the producer sees it, fetched one stage ahead.
+struct ProdStage {
   Piece pc;
-  int t;       // first tile of the next stage of pc
-  int pieces;  // pieces started so far
-
-  __device__ void init(int64_t g0, int64_t g1, int row) {
-    g_cur = g0;
-    g_end = g1;
-    row_cur = row;
-    first = true;
-    split_done = false;
-    have = false;
-    t = 0;
-    pieces = 0;
-  }
-
-  __device__ bool next_piece(const DecodeParams& p, const int* prefix, int Y) {
-    if (g_cur >= g_end) return false;
-    const int nt = prefix[row_cur + 1] - prefix[row_cur];
-    const int64_t local = g_cur - (int64_t)prefix[row_cur] * Y;
-    const int y = (int)(local / nt);
-    const int t0 = (int)(local - (int64_t)y * nt);
-    const int t1 = (int)min((int64_t)nt, (int64_t)t0 + (g_end - g_cur));
-    pc.row = row_cur;
-    pc.y = y;
-    pc.t0 = t0;
-    pc.t1 = t1;
-    pc.len = p.lens[row_cur];
-    pc.whole = (t0 == 0 && t1 == nt);
-    pc.slot = first ? 0 : 1;
-    first = false;
-    g_cur += t1 - t0;
-    if (t1 == nt && y == Y - 1) {
-      do {
-        ++row_cur;
-      } while (row_cur < p.n && prefix[row_cur + 1] == prefix[row_cur]);
-    }
-    return true;
-  }
-
-  // Next stage: tiles [st_t0, st_t1) of piece *pc; flags for piece bounds.
-  __device__ bool next(const DecodeParams& p, const int* prefix, int Y, int& st_t0, int& st_t1, bool& piece_first,
-                       bool& piece_last) {
-    if (!have || t >= pc.t1) {
-      if (!next_piece(p, prefix, Y)) return false;
-      have = true;
-      t = pc.t0;
-      ++pieces;
-      piece_first = true;
-    } else {
-      piece_first = false;
-    }
-    st_t0 = t;
-    st_t1 = min(pc.t1, t + kTilesPerStage);
-    t = st_t1;
-    piece_last = (t >= pc.t1);
-    return true;
-  }
+  int st0, st1, qi;
+  bool pf;
 };
 
 template <typename T, int GM>
 __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid_constant__ DecodeParams p) {
-  static_assert(GM >= 1 && 2 * GM <= kN, "query group (hi and lo rows of P) must fit the MMA N");
+  static_assert(GM >= 2 && 2 * GM <= kN && (GM * 16) % 32 == 0, "query group (hi and lo rows of P) must fit the MMA N");
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdQK = instr_desc(kBF16, false, kTok, kN);
   constexpr uint32_t kIdPV = instr_desc(kBF16, true, kD, kN);
+  constexpr int G = GM;
+  constexpr int kQV = G * 16 / 32;  // 16-byte chunks of a piece's q per producer lane
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((((raw + 1023u) & ~1023u)) - raw);
@@ -185,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   unsigned char* pbuf = smem + kOffP;
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full = bars;          // [3] TMA bytes + 32 producer lanes
+  uint64_t* full = bars;          // [3] TMA bytes + 32 lanes of each producer warp
   uint64_t* empty = bars + 3;     // [3] MMA commit: stage consumed
   uint64_t* s_full = bars + 6;    // [2] MMA commit: S ready
   uint64_t* s_empty = bars + 8;   // [2] 4 softmax warps read S
@@ -199,12 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   uint64_t* l_full = bars + 23;   // [1] 4 softmax warps wrote their piece sums
   float* lsum = reinterpret_cast<float*>(smem + kOffL);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
-  int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);
+  int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);  // [n + 1] tile prefix
+  int* lens_s = prefix + ((p.n + 4) & ~3);                   // [n] lengths
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr int G = GM;
   const int Y = p.KVH;
 
   // ---------------------------------------------------------------- setup
@@ -215,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       int nt = 0;
       if (i < p.n) {
         const int len = p.lens[i];
+        lens_s[i] = len;
         if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + kTT - 1) / kTT;
       }
       int v = nt;
@@ -228,14 +202,14 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     }
     if (lane == 0) prefix[0] = 0;
   }
-  // q and P buffers start zeroed: the padding rows g >= G stay zero
+  // q and P buffers start zeroed: the padding rows stay zero
   for (int o = threadIdx.x * 16; o < 2 * kQB + 2 * kPB; o += kThreads * 16)
     sts128(qbuf + o, make_uint4(0u, 0u, 0u, 0u));
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int s = 0; s < 3; ++s) {
-      mbar_init(&full[s], 32);
+      mbar_init(&full[s], 32 * kProd);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -268,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     for (int i = threadIdx.x; i <= p.n; i += blockDim.x) p.ws_prefix[i] = prefix[i];
   for (int i = blockIdx.x; i < p.n; i += gridDim.x) {
     if (prefix[i + 1] != prefix[i]) continue;
-    const int len = p.lens[i];
+    const int len = lens_s[i];
     if (len > 0) {
       if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
       continue;
@@ -294,36 +268,70 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     row0 = lo;
   }
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
+  if (warp == 4 || warp >= 6) {
+    // ------------------------------------------------------------ producers
+    // Warp 4 fills tiles 0-3 of every stage, warp 6 tiles 4-7: one warp
+    // issues its TMA boxes one after another (~45 ns each), so two warps
+    // halve a stage's issue time.  Block ids come kIdAhead stages ahead
+    // through a cp.async ring per warp (q of the coming pieces is prefetched
+    // into L2 there); warp 4 also loads q into registers one stage ahead of
+    // its piece and stores it for the MMA.
+    const int pw = warp == 4 ? 0 : 1;
+    const bool q_owner = pw == 0;
     const uint64_t pol = l2_evict_first_policy();
     StageIter it;
-    it.init(g0, g1, row0);
-    int k = 0, last_piece = 0;
-    int st0, st1;
-    bool pf, pl;
+    it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage);
+    IdPrefetch ids;
+    ids.it.init(g0, g1, row0, prefix, nullptr, p.n, Y, kTilesPerStage);
+    ids.ring = reinterpret_cast<int*>(smem + kOffIds + pw * kIdRingBytes);
+    ids.issued = 0;
+    const int q_heads = q_owner ? G : 0;
+    for (int i = 0; i < kIdAhead; ++i) ids.push(p, lane, q_heads, kD * (int)sizeof(T), pw * kTilesPerProd, kTilesPerProd);
+    ProdStage cur, nxt;
+    uint4 q_c[kQV], q_n[kQV];
+    auto advance = [&](ProdStage& s) -> bool {
+      bool pl;
+      if (!it.next(s.st0, s.st1, s.pf, pl)) return false;
+      s.pc = it.pc;
+      s.qi = it.pieces - 1;
+      return true;
+    };
+    auto fetch = [&](const ProdStage& s, uint4 (&qr)[kQV]) {
+      if (q_owner && s.pf) {
+        const int64_t qrow = p.q_rows ? p.q_rows[s.pc.row] : s.pc.row;
+        const unsigned char* qsrc = p.q + qrow * p.q_sn + (int64_t)(s.pc.y * G) * p.q_sh;
+#pragma unroll
+        for (int u = 0; u < kQV; ++u) {
+          const int c = u * 32 + lane;
+          qr[u] = __ldg(reinterpret_cast<const uint4*>(qsrc + (c >> 4) * p.q_sh + (c & 15) * 16));
+        }
+      }
+    };
+    int k = 0;
     bool aborted = false;
-    while (!aborted && it.next(p, prefix, Y, st0, st1, pf, pl)) {
-      const Piece& pc = it.pc;
-      const int kh = pc.y;
-      if (pf) {
-        // q of this piece into q buffer (pieces-1) % 2
-        const int qi = it.pieces - 1;
-        const int qb = qi & 1;
-        if (qi >= 2 && !mbar_wait(&q_empty[qb], ((qi >> 1) - 1) & 1u, p.err)) {
+    bool have = advance(cur);
+    if (have) fetch(cur, q_c);
+    while (have) {
+      const bool have_n = advance(nxt);
+      if (have_n) fetch(nxt, q_n);
+      ids.push(p, lane, q_heads, kD * (int)sizeof(T), pw * kTilesPerProd, kTilesPerProd);  // stage k + kIdAhead
+      const int64_t id_c = ids.take(k, lane);
+      const int kh = cur.pc.y;
+      if (q_owner && cur.pf) {
+        // q of this piece into q buffer qi % 2
+        const int qb = cur.qi & 1;
+        if (cur.qi >= 2 && !mbar_wait(&q_empty[qb], ((cur.qi >> 1) - 1) & 1u, p.err)) {
           aborted = true;
           break;
         }
-        const int64_t qrow = p.q_rows ? p.q_rows[pc.row] : pc.row;
-        const unsigned char* qsrc = p.q + qrow * p.q_sn + (int64_t)(kh * G) * p.q_sh;
-        for (int c = lane; c < G * 16; c += 32) {
+#pragma unroll
+        for (int u = 0; u < kQV; ++u) {
+          const int c = u * 32 + lane;
           const int g = c >> 4, ch = c & 15;
-          const uint4 v = __ldg(reinterpret_cast<const uint4*>(qsrc + g * p.q_sh + ch * 16));
-          sts128(qbuf + qb * kQB + (ch >> 3) * (kN * 128) + swz(g, ch & 7), v);
+          sts128(qbuf + qb * kQB + (ch >> 3) * (kN * 128) + swz(g, ch & 7), q_c[u]);
         }
         fence_proxy_async_smem();
         mbar_arrive(&q_full[qb]);
-        last_piece = qi;
       }
       const int st = k % kNST;
       const uint32_t use = (uint32_t)(k / kNST);
@@ -333,15 +341,14 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       }
       unsigned char* sk = stages + st * kStage;
       unsigned char* sv = sk + kKV;
-      const int32_t* btrow = p.bt + (int64_t)pc.row * p.bt_stride;
-      const int j = lane;  // lanes 0..7 own tiles j of this stage
-      const int tile = st0 + j;
+      const int j = pw * kTilesPerProd + lane;  // lanes 0..3 own tiles j of this stage
+      const int tile = cur.st0 + j;
       int tier = 0, blk_id = 0, r0 = 0;
       bool valid = false;
-      if (j < kTilesPerStage && tile < st1) {
+      if (lane < kTilesPerProd && tile < cur.st1) {
         const int b = tile / p.tiles_per_block;
         r0 = (tile - b * p.tiles_per_block) * kTT;
-        int64_t id = btrow[b];
+        int64_t id = id_c;
         if (id >= p.split) {
           tier = 1;
           id -= p.split;
@@ -380,129 +387,153 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
           const int row = c >> 4, ch = c & 15;
           const uint4 kv = *reinterpret_cast<const uint4*>(kw + row * p.tok_sb[tr] + ch * 16);
           const uint4 vv = *reinterpret_cast<const uint4*>(vw + row * p.tok_sb[tr] + ch * 16);
-          const int r = w * kTT + row;
+          const int r = (pw * kTilesPerProd + w) * kTT + row;
           sts128(sk + (ch >> 3) * kPanel + swz(r, ch & 7), kv);
           sts128(sv + (ch >> 3) * kPanel + swz(r, ch & 7), vv);
         }
       }
-      fence_proxy_async_smem();
+      if (host_mask != 0u) fence_proxy_async_smem();  // generic smem writes before the MMA reads them
       mbar_arrive(&full[st]);
       ++k;
+      cur = nxt;
+#pragma unroll
+      for (int u = 0; u < kQV; ++u) q_c[u] = q_n[u];
+      have = have_n;
     }
-    (void)last_piece;
     if (aborted) atomicExch(&abort_flag, 1);
+    cp_async_wait<0>();  // no id copy outlives the CTA
     // every issued stage has landed before shared memory goes away (in a
     // normal run the MMA warp already waited on all of them)
     for (int q = std::max(0, k - kNST); q < k; ++q) mbar_wait(&full[q % kNST], (uint32_t)(q / kNST) & 1u, p.err);
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
-    StageIter qk_it, pv_it;
-    qk_it.init(g0, g1, row0);
-    pv_it.init(g0, g1, row0);
-    int kq = 0, kp = 0;  // next q.K^T stage, next P.V stage
-    int st0, st1;
-    bool pf, pl;
-    bool have_qk = qk_it.next(p, prefix, Y, st0, st1, pf, pl);
-    bool qk_first = pf, qk_last = pl;
-    bool ok = true;
-    // issue q.K^T for stage kq (its inputs landed, S buffer free, q ready)
-    auto issue_qk = [&]() -> bool {
-      const int st = kq % kNST, b = kq & 1;
-      const int qi = qk_it.pieces - 1, qb = qi & 1;
-      if (qk_first && !mbar_wait(&q_full[qb], (qi >> 1) & 1u, p.err)) return false;
-      if (!mbar_wait(&full[st], (kq / kNST) & 1u, p.err)) return false;
-      if (kq >= 2 && !mbar_wait(&s_empty[b], ((kq >> 1) - 1) & 1u, p.err)) return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t sk = smem_u32(stages + st * kStage);
-        const uint32_t sq = smem_u32(qbuf + qb * kQB);
+    // One thread polls the barriers of both products and issues whichever is
+    // ready: q.K^T of a stage as soon as its tiles landed (at most two ahead,
+    // bounded by the two S buffers), P.V as soon as the softmax wrote P.
+    if (lane == 0) {
+      StageIter it;
+      it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage);
+      int kq = 0, kp = 0;  // next q.K^T stage, next P.V stage
+      int st0, st1;
+      bool qf, ql;
+      bool have_qk = it.next(st0, st1, qf, ql);
+      int qi = it.pieces - 1;
+      bool ok = true;
+      uint32_t spins = 0;
+      uint64_t t_idle = 0;
+      while (have_qk || kp < kq) {
+        bool prog = false;
+        if (have_qk) {
+          const int st = kq % kNST, b = kq & 1, qb = qi & 1;
+          if ((!qf || mbar_test_wait(&q_full[qb], (uint32_t)(qi >> 1) & 1u)) &&
+              mbar_test_wait(&full[st], (uint32_t)(kq / kNST) & 1u) &&
+              (kq < 2 || mbar_test_wait(&s_empty[b], (uint32_t)((kq >> 1) - 1) & 1u))) {
+            tc_fence_after();
+            const uint32_t sk = smem_u32(stages + st * kStage);
+            const uint32_t sq = smem_u32(qbuf + qb * kQB);
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t koff = (ks >> 2) * kPanel + (ks & 3) * 32;
-          const uint32_t qoff = (ks >> 2) * (kN * 128) + (ks & 3) * 32;
-          umma_f16(tmem + kN * b, sw128_desc(sk + koff, 16, 1024), sw128_desc(sq + qoff, 16, 1024), kIdQK,
-                   ks > 0 ? 1u : 0u);
+            for (int ks = 0; ks < kD / 16; ++ks) {
+              const uint32_t koff = (ks >> 2) * kPanel + (ks & 3) * 32;
+              const uint32_t qoff = (ks >> 2) * (kN * 128) + (ks & 3) * 32;
+              umma_f16(tmem + kN * b, sw128_desc(sk + koff, 16, 1024), sw128_desc(sq + qoff, 16, 1024), kIdQK,
+                       ks > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[b]);
+            if (ql) umma_commit(&q_empty[qb]);
+            ++kq;
+            have_qk = it.next(st0, st1, qf, ql);
+            qi = it.pieces - 1;
+            prog = true;
+          }
         }
-        umma_commit(&s_full[b]);
-        if (qk_last) umma_commit(&q_empty[qb]);
-      }
-      __syncwarp();
-      return true;
-    };
-    if (have_qk) ok = issue_qk();
-    while (ok && have_qk) {
-      // look one stage ahead so q.K^T(k+1) overlaps the softmax of stage k
-      const int cur = kq;
-      ++kq;
-      have_qk = qk_it.next(p, prefix, Y, st0, st1, pf, pl);
-      qk_first = pf;
-      qk_last = pl;
-      if (have_qk && !issue_qk()) {
-        ok = false;
-        break;
-      }
-      // P.V for stage cur
-      int pst0, pst1;
-      bool ppf, ppl;
-      pv_it.next(p, prefix, Y, pst0, pst1, ppf, ppl);
-      const int st = cur % kNST, b = cur & 1;
-      if (!mbar_wait(&p_full[b], (cur >> 1) & 1u, p.err)) {
-        ok = false;
-        break;
-      }
-      if (cur >= 2 && !mbar_wait(&o_empty[b], ((cur >> 1) - 1) & 1u, p.err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t sv = smem_u32(stages + st * kStage + kKV);
-        const uint32_t sp = smem_u32(pbuf + b * kPB);
+        if (kp < kq) {
+          const int st = kp % kNST, b = kp & 1;
+          if (mbar_test_wait(&p_full[b], (uint32_t)(kp >> 1) & 1u) &&
+              (kp < 2 || mbar_test_wait(&o_empty[b], (uint32_t)((kp >> 1) - 1) & 1u))) {
+            tc_fence_after();
+            const uint32_t sv = smem_u32(stages + st * kStage + kKV);
+            const uint32_t sp = smem_u32(pbuf + b * kPB);
 #pragma unroll
-        for (int ks = 0; ks < kTok / 16; ++ks) {
-          const uint32_t voff = ks * 2048;  // 16 token rows
-          const uint32_t poff = (ks >> 2) * (kN * 128) + (ks & 3) * 32;
-          umma_f16(tmem + 2 * kN + kN * b, sw128_desc(sv + voff, kPanel, 1024), sw128_desc(sp + poff, 16, 1024), kIdPV,
-                   ks > 0 ? 1u : 0u);
+            for (int ks = 0; ks < kTok / 16; ++ks) {
+              const uint32_t voff = ks * 2048;  // 16 token rows
+              const uint32_t poff = (ks >> 2) * (kN * 128) + (ks & 3) * 32;
+              umma_f16(tmem + 2 * kN + kN * b, sw128_desc(sv + voff, kPanel, 1024), sw128_desc(sp + poff, 16, 1024),
+                       kIdPV, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(&o_full[b]);
+            umma_commit(&empty[st]);
+            ++kp;
+            prog = true;
+          }
         }
-        umma_commit(&o_full[b]);
-        umma_commit(&empty[st]);
+        if (prog) {
+          spins = 0;
+          t_idle = 0;
+        } else if ((++spins & 255u) == 0u) {
+          const uint64_t now = globaltimer_ns();
+          if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitLimitNs) {
+            set_error(p.err, FD_DEVERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+        }
       }
-      __syncwarp();
-      ++kp;
+      if (!ok) atomicExch(&abort_flag, 1);
+      // all MMAs issued by this thread complete before TMEM is released
+      umma_commit(drain);
+      mbar_wait(drain, 0u, p.err);
     }
-    if (!ok) atomicExch(&abort_flag, 1);
-    // all MMAs issued by this thread complete before TMEM is released
-    if (lane == 0) umma_commit(drain);
     __syncwarp();
-    mbar_wait(drain, 0u, p.err);
   } else {
     // ------------------------------------------------------------ softmax warps 0-3
+    // Per stage: S -> block max -> P (published) -> fold O of the PREVIOUS
+    // stage, so the P.V round trip of stage k overlaps the softmax of k + 1;
+    // the last stage of a piece is folded at once.
     const int r = threadIdx.x;  // token row of S, dim of O (TMEM lane)
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     StageIter it;
-    it.init(g0, g1, row0);
+    it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage);
     int k = 0;
     int st0, st1;
     bool pf, pl;
-    float m_run[G], l_part[G], acc[G];
+    float m_run[G], l_part[G], acc[G], alpha_prev[G];
     int h0 = 0;
-    bool ok = true;
-    while (ok && it.next(p, prefix, Y, st0, st1, pf, pl)) {
+    int64_t orow = 0;
+    bool ok = true, pend = false;
+    // fold O of stage kk (TMEM buffer kk & 1) into acc with the rescale a;
+    // column g holds the hi part, column G + g the lo part of P.V
+    auto fold = [&](int kk, const float (&a)[G]) -> bool {
+      const int bb = kk & 1;
+      if (!mbar_wait(&o_full[bb], (uint32_t)(kk >> 1) & 1u, p.err)) return false;
+      tc_fence_after();
+      float o[16];
+      tmem_ld16(tmem + lane_base + 2 * kN + kN * bb, o);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[bb]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = acc[g] * a[g] + (o[g] + o[G + g]);
+      return true;
+    };
+    while (ok && it.next(st0, st1, pf, pl)) {
       const Piece& pc = it.pc;
       if (pf) {
         h0 = pc.y * G;
+        if (pc.whole) orow = p.out_rows ? p.out_rows[pc.row] : pc.row;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           m_run[g] = -INFINITY;
           l_part[g] = 0.f;
           acc[g] = 0.f;
         }
+        pend = false;
       }
       const int b = k & 1;
       const int st = k % kNST;
       // ---- S of this stage
-      if (!mbar_wait(&s_full[b], (k >> 1) & 1u, p.err)) {
+      if (!mbar_wait(&s_full[b], (uint32_t)(k >> 1) & 1u, p.err)) {
         ok = false;
         break;
       }
@@ -515,23 +546,32 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       const int tile = st0 + (r >> 4);
       const int tok = tile * kTT + (r & 15);
       const bool valid = (tile < st1) && (tok < pc.len);
+#pragma unroll
+      for (int g = 0; g < G; ++g) s[g] = valid ? s[g] * p.qscale : -INFINITY;
+      // warp max of each of the G columns by a halving butterfly: after it
+      // this lane holds the max of column gm (set by lane bits 4, 3, 2)
       float bm[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        s[g] = valid ? s[g] * p.qscale : -INFINITY;
-        bm[g] = s[g];
+      for (int g = 0; g < G; ++g) bm[g] = s[g];
+      int gm = 0;
+#pragma unroll
+      for (int h = G / 2, m = 16; h >= 1; h >>= 1, m >>= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < h; ++i) {
+          const float send = upper ? bm[i] : bm[h + i];
+          const float keep = upper ? bm[h + i] : bm[i];
+          bm[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, m));
+        }
+        if (upper) gm += h;
       }
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-        for (int g = 0; g < G; ++g) bm[g] = fmaxf(bm[g], __shfl_xor_sync(0xffffffffu, bm[g], off));
+      for (int m = 16 / (G / 2) / 2; m >= 1; m >>= 1) bm[0] = fmaxf(bm[0], __shfl_xor_sync(0xffffffffu, bm[0], m));
       float* rb = red + b * 4 * kN;
-      if (lane == 0) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) rb[warp * kN + g] = bm[g];
-        mbar_arrive(&red_full[b]);
-      }
-      if (!mbar_wait(&red_full[b], (k >> 1) & 1u, p.err)) {
+      if ((lane & (32 / G - 1)) == 0) rb[warp * kN + gm] = bm[0];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[b]);
+      if (!mbar_wait(&red_full[b], (uint32_t)(k >> 1) & 1u, p.err)) {
         ok = false;
         break;
       }
@@ -545,17 +585,24 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
         l_part[g] = l_part[g] * alpha[g] + pv[g];
         m_run[g] = mn;
       }
-      // ---- P (16-bit) into the swizzled B operand; masked tokens zero their V row
+      // ---- P (16-bit) into the swizzled B operand: p = hi + lo, hi in row g
+      // and lo in row G + g, so columns g and G + g of O sum to P.V at nearly
+      // fp32 precision.  Lane pairs swap halves: the even lane stores the hi
+      // pair of its two tokens as one word, the odd lane the lo pair.
       unsigned char* pb = pbuf + b * kPB + (r >> 6) * (kN * 128);
-      const int col = r & 63;
-      // p = hi + lo in the 16-bit type: rows g and 8 + g of the B operand, so
-      // columns g and 8 + g of O sum to P.V at nearly fp32 precision
+      const int col = (r & 63) & ~1;
+      const bool odd = (lane & 1) != 0;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const T hi = Dt<T>::narrow(pv[g]);
         const T lo = Dt<T>::narrow(pv[g] - Dt<T>::to_f32(hi));
-        *reinterpret_cast<T*>(pb + swz(g, col >> 3) + (col & 7) * 2) = hi;
-        *reinterpret_cast<T*>(pb + swz(8 + g, col >> 3) + (col & 7) * 2) = lo;
+        const uint32_t hb = bits16(hi);
+        const uint32_t lb = bits16(lo);
+        // even lane r gives lo_r and takes hi_r+1; odd lane gives hi_r and takes lo_r-1
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, odd ? hb : lb, 1);
+        const uint32_t word = odd ? (other | (lb << 16)) : (hb | (other << 16));
+        const int row = odd ? G + g : g;
+        *reinterpret_cast<uint32_t*>(pb + swz(row, col >> 3) + (col & 7) * 2) = word;
       }
       if (!valid) {
         unsigned char* sv = stages + st * kStage + kKV;
@@ -569,57 +616,57 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      // ---- O of this stage, folded into the accumulator
-      if (!mbar_wait(&o_full[b], (k >> 1) & 1u, p.err)) {
+      // ---- O of the previous stage of this piece
+      if (pend && !fold(k - 1, alpha_prev)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      float o[8], o_lo[8];
-      tmem_ld8(tmem + lane_base + 2 * kN + kN * b, o);
-      tmem_ld8(tmem + lane_base + 2 * kN + kN * b + 8, o_lo);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[b]);
+      if (!pl) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = acc[g] * alpha[g] + (o[g] + o_lo[g]);
+        for (int g = 0; g < G; ++g) alpha_prev[g] = alpha[g];
+        pend = true;
+        ++k;
+        continue;
+      }
+      if (!fold(k, alpha)) {
+        ok = false;
+        break;
+      }
+      pend = false;
       ++k;
 
-      if (pl) {
-        // ---- piece epilogue: denominators, output row or partial slot
-        float L[G];
+      // ---- piece epilogue: denominators, output row or partial slot
+      float L[G];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float v = l_part[g];
+      for (int g = 0; g < G; ++g) {
+        float v = l_part[g];
 #pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-          L[g] = v;
-        }
-        float* lb = lsum;
-        if (lane == 0) {
+        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        L[g] = v;
+      }
+      float* lb = lsum;
+      if (lane == 0) {
 #pragma unroll
-          for (int g = 0; g < G; ++g) lb[warp * kN + g] = L[g];
-          mbar_arrive(l_full);
-        }
-        if (!mbar_wait(l_full, (uint32_t)(it.pieces - 1) & 1u, p.err)) {
-          ok = false;
-          break;
-        }
-        const int64_t orow = p.out_rows ? p.out_rows[pc.row] : pc.row;
+        for (int g = 0; g < G; ++g) lb[warp * kN + g] = L[g];
+        mbar_arrive(l_full);
+      }
+      if (!mbar_wait(l_full, (uint32_t)(it.pieces - 1) & 1u, p.err)) {
+        ok = false;
+        break;
+      }
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float Lg = lb[g] + lb[kN + g] + lb[2 * kN + g] + lb[3 * kN + g];
-          const float lse_nat = (m_run[g] + log2f(Lg)) * kLn2;
-          const int h = h0 + g;
-          const float val = acc[g] / Lg;
-          if (pc.whole) {
-            store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + r, p.out_dtype, val);
-            if (r == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)pc.row * p.lse_sn] = lse_nat;
-          } else {
-            const int64_t pidx = ((int64_t)blockIdx.x * 2 + pc.slot) * G + g;
-            p.part_o[pidx * kD + r] = val;
-            if (r == 0) p.part_lse[pidx] = lse_nat;
-          }
+      for (int g = 0; g < G; ++g) {
+        const float Lg = lb[g] + lb[kN + g] + lb[2 * kN + g] + lb[3 * kN + g];
+        const float lse_nat = (m_run[g] + log2f(Lg)) * kLn2;
+        const int h = h0 + g;
+        const float val = acc[g] / Lg;
+        if (pc.whole) {
+          store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + r, p.out_dtype, val);
+          if (r == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)pc.row * p.lse_sn] = lse_nat;
+        } else {
+          const int64_t pidx = ((int64_t)blockIdx.x * 2 + pc.slot) * G + g;
+          p.part_o[pidx * kD + r] = val;
+          if (r == 0) p.part_lse[pidx] = lse_nat;
         }
       }
     }
@@ -639,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
 template <int GM>
 int launch_mma_g(const DecodeParams& q, int dtype, size_t smem, int n, cudaStream_t s) {
   static unsigned long long done_h = 0, done_b = 0;
-  const int budget = mma::kSmemFixed + (kMaxPersistentRows + 1) * 4 + 16;
+  const int budget = mma::kSmemFixed + 2 * mma::kRowsBytes;
   int st;
   if (dtype == FD_DTYPE_BF16) {
     st = fdh::ensure_smem(reinterpret_cast<const void*>(mma::fd_decode_mma_kernel<__nv_bfloat16, GM>), budget, &done_b);
@@ -664,7 +711,7 @@ int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem
   if (!mma_eligible(dtype, D, p.G, p.BS) || p.gcs != 1 || p.TT != mma::kTT || !p.persistent) return FD_OK;
   for (int t = 0; t < 2; ++t)
     if (p.nblk[t] > 0 && !p.host[t] && !p.use_tmap[t]) return FD_OK;
-  const size_t smem = (size_t)mma::kSmemFixed + extra_smem;
+  const size_t smem = (size_t)mma::kSmemFixed + 2 * extra_smem;  // prefix + lengths
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
