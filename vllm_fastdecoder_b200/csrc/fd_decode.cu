@@ -103,15 +103,15 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
 
   // ---------------------------------------------------------------- setup
   if (p.persistent && warp == 0) {
-    // prefix[i] = tiles of rows < i (0 for empty rows and rows whose length
-    // overruns their table row)
+    // prefix[i] = positions of rows < i: tiles + vtiles per row (0 for empty
+    // rows and rows whose length overruns their table row)
     int carry = 0;
     for (int base = 0; base < p.n; base += 32) {
       const int i = base + lane;
       int nt = 0;
       if (i < p.n) {
         const int len = p.lens[i];
-        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + p.TT - 1) / p.TT;
+        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + p.TT - 1) / p.TT + p.vtiles;
       }
       int v = nt;
 #pragma unroll
@@ -199,44 +199,27 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   }
 
   // Pieces of this CTA, enumerated identically by the producer and consumers.
-  bool split_done = false, first_piece = true;
+  StageIter pieces;
+  if (p.persistent) {
+    pieces.init(g_cur, g_end, row_cur, prefix, p.lens, p.n, Y, C::kNW, p.vtiles);
+  } else {
+    const int i = blockIdx.z;
+    const int len = p.lens[i];
+    const int ntiles = (len + p.TT - 1) / p.TT;
+    const int nsplits = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
+    Piece sp;
+    sp.row = i;
+    sp.y = blockIdx.y;
+    sp.t0 = blockIdx.x * p.tiles_per_split;
+    sp.t1 = min(ntiles, sp.t0 + p.tiles_per_split);
+    sp.len = len;
+    sp.whole = (nsplits == 1);
+    sp.slot = blockIdx.x;
+    pieces.init_single(sp, C::kNW);
+  }
   auto next_piece = [&](Piece& pc) -> bool {
-    if (!p.persistent) {
-      if (split_done) return false;
-      split_done = true;
-      const int i = blockIdx.z;
-      const int len = p.lens[i];
-      const int ntiles = (len + p.TT - 1) / p.TT;
-      const int nsplits = (ntiles + p.tiles_per_split - 1) / p.tiles_per_split;
-      pc.row = i;
-      pc.y = blockIdx.y;
-      pc.t0 = blockIdx.x * p.tiles_per_split;
-      pc.t1 = min(ntiles, pc.t0 + p.tiles_per_split);
-      pc.len = len;
-      pc.whole = (nsplits == 1);
-      pc.slot = blockIdx.x;
-      return true;
-    }
-    if (g_cur >= g_end) return false;
-    const int nt = prefix[row_cur + 1] - prefix[row_cur];
-    const int64_t local = g_cur - (int64_t)prefix[row_cur] * Y;
-    const int y = (int)(local / nt);
-    const int t0 = (int)(local - (int64_t)y * nt);
-    const int t1 = (int)min((int64_t)nt, (int64_t)t0 + (g_end - g_cur));
-    pc.row = row_cur;
-    pc.y = y;
-    pc.t0 = t0;
-    pc.t1 = t1;
-    pc.len = p.lens[row_cur];
-    pc.whole = (t0 == 0 && t1 == nt);
-    pc.slot = first_piece ? 0 : 1;
-    first_piece = false;
-    g_cur += t1 - t0;
-    if (t1 == nt && y == Y - 1) {
-      do {
-        ++row_cur;
-      } while (row_cur < p.n && prefix[row_cur + 1] == prefix[row_cur]);
-    }
+    if (!pieces.next_piece()) return false;
+    pc = pieces.pc;
     return true;
   };
 
@@ -248,21 +231,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     // block ids kIdAhead stages ahead (cp.async ring), q of coming pieces
     // prefetched into L2 for the consumers
     IdPrefetch ids;
-    if (p.persistent) {
-      ids.it.init(g_cur, g_end, row_cur, prefix, nullptr, p.n, Y, C::kNW);
-    } else {
-      Piece sp;
-      const int i = blockIdx.z;
-      const int ntiles = (p.lens[i] + p.TT - 1) / p.TT;
-      sp.row = i;
-      sp.y = blockIdx.y;
-      sp.t0 = blockIdx.x * p.tiles_per_split;
-      sp.t1 = min(ntiles, sp.t0 + p.tiles_per_split);
-      sp.len = 0;
-      sp.whole = false;
-      sp.slot = 0;
-      ids.it.init_single(sp, C::kNW);
-    }
+    ids.it = pieces;  // a copy, before any piece was taken: the same sequence
     ids.ring = id_ring;
     ids.issued = 0;
     for (int i = 0; i < kIdAhead; ++i) ids.push(p, lane, GQ, C::kRB);
@@ -659,17 +628,21 @@ __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParam
   const int y = blockIdx.x;
   const int i = blockIdx.y;
   const int* P = p.ws_prefix;
-  const int nt = P[i + 1] - P[i];
-  if (nt == 0) return;
+  const int nv = P[i + 1] - P[i];
+  if (nv == 0) return;
+  const int nt = nv - p.vtiles;  // real tiles of the segment; the rest only weigh the split
   const int Y = p.KVH * p.gcs;
   const int64_t N = p.ncta;
   const int64_t T = (int64_t)P[p.n] * Y;
-  const int64_t g0 = (int64_t)P[i] * Y + (int64_t)y * nt;
+  const int64_t g0 = (int64_t)P[i] * Y + (int64_t)y * nv;
   const int64_t g1 = g0 + nt;
-  const int64_t c0 = ((g0 + 1) * N - 1) / T;
-  const int64_t c1 = (g1 * N - 1) / T;
+  const int64_t c0 = ((g0 + 1) * N - 1) / T;  // CTA owning position g0
+  const int64_t c1 = (g1 * N - 1) / T;        // CTA owning the last real tile
   if (c0 == c1) return;
-  const int first_slot = ((c0 * T) / N == g0) ? 0 : 1;
+  // the segment is c0's first real piece (slot 0) unless c0's range holds
+  // real tiles before g0, i.e. starts before the previous segment's weight
+  // positions
+  const int first_slot = ((c0 * T) / N >= g0 - p.vtiles) ? 0 : 1;
   const int GQ = p.gq;
   const int kh = y / p.gcs, gc = y - kh * p.gcs;
   const int h0 = kh * p.G + gc * GQ;
@@ -711,6 +684,7 @@ struct Geometry {
   int TT, tiles_per_block, tiles_per_split, max_splits, G, GQ, gcs;
   bool persistent;
   bool mma;  // tcgen05 GQA kernel (fd_decode_mma.cu)
+  int vtiles;  // persistent schedule: weight positions per (row, kv-head chunk) segment
   size_t ws_bytes;
   // persistent workspace layout: partial o | partial lse | row-tile prefix
   size_t off_lse, off_prefix;
@@ -836,6 +810,19 @@ int geometry(const fd_decode_args* a, Geometry* g) {
   if (g->mma) {  // one CTA handles the whole query group of a kv head
     g->GQ = g->G;
     g->gcs = 1;
+  }
+  // A piece costs its stages plus a fixed overhead (q load, the last stage's
+  // round trip, the epilogue, and a last stage that is on average half
+  // empty).  Measured on B200 (lognormal lengths for the tensor-core kernel,
+  // uniform ones for the CUDA-core kernel), the balance is best at a weight
+  // of 16 tiles per segment for the tensor-core kernel (8-tile stages) and
+  // 5 for the CUDA-core kernel (4-tile stages); FASTDECODE_B200_VTILES
+  // overrides it.
+  g->vtiles = 0;
+  if (g->persistent) {
+    g->vtiles = g->mma ? 16 : 5;
+    const char* vt_env = getenv("FASTDECODE_B200_VTILES");
+    if (vt_env != nullptr && vt_env[0] >= '0' && vt_env[0] <= '9') g->vtiles = std::min(atoi(vt_env), 64);
   }
   if (g->persistent) {
     // every CTA owns two partial slots of GQ heads
@@ -1046,6 +1033,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     ncta = std::max<int64_t>(1, std::min<int64_t>(ncta, (tiles_max + 15) / 16));
     p.persistent = 1;
     p.ncta = (int)ncta;
+    p.vtiles = g.vtiles;
     const size_t extra = ((size_t)(a->n + 1) * 4 + 15) / 16 * 16;
     if (g.mma) {
       // the tensor-core kernel runs one CTA per SM; the combine must see the

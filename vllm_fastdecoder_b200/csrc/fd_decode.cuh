@@ -37,6 +37,11 @@ struct alignas(64) DecodeParams {
   // persistent schedule: ncta CTAs share the flattened (row, kv-head chunk,
   // tile) space evenly; prefix of per-row tile counts published in ws_prefix
   int persistent, ncta;
+  // per-(row, kv-head chunk) cost of a piece in tile units: every segment of
+  // nt tiles occupies nt + vtiles positions of the flattened space, so the
+  // equal split also balances per-piece overheads (the extra positions carry
+  // no work)
+  int vtiles;
   int* ws_prefix;
   float qscale;  // scale * log2(e)
   void* out;
@@ -66,15 +71,20 @@ struct Piece {
 };
 
 // Enumerates one CTA's stages (up to `tps` consecutive tiles of one piece):
-// the pieces of its persistent tile range [g0, g1), or the single piece of a
-// split-grid CTA.  Every role of a kernel runs its own copy over the same
-// sequence.  prefix/lens may live in shared memory; lens may be null when
-// the caller does not need Piece::len.
+// the pieces of its persistent range [g0, g1) of the flattened space, or the
+// single piece of a split-grid CTA.  In the flattened space each (row, y)
+// segment has prefix[row+1] - prefix[row] = nt + vtiles positions: nt real
+// tiles, then vtiles positions that only weigh the split; a piece consisting
+// of those alone is skipped.  A CTA's first real piece takes partial slot 0,
+// later ones slot 1 (only its first and last piece can be partial).  Every
+// role of a kernel runs its own copy over the same sequence.  prefix/lens
+// may live in shared memory; lens may be null when the caller does not need
+// Piece::len.
 struct StageIter {
   int64_t g_cur, g_end;
   const int* prefix;
   const int* lens;
-  int n, Y, tps;
+  int n, Y, tps, vt;
   int row_cur;
   bool first, have, single;
   Piece pc;
@@ -82,7 +92,8 @@ struct StageIter {
   int pieces;  // pieces started so far
 
   __device__ void init(int64_t g0, int64_t g1, int row, const int* prefix_s, const int* lens_s, int n_rows, int y,
-                       int tiles_per_stage) {
+                       int tiles_per_stage, int vtiles) {
+    vt = vtiles;
     g_cur = g0;
     g_end = g1;
     prefix = prefix_s;
@@ -111,31 +122,37 @@ struct StageIter {
   }
 
   __device__ bool next_piece() {
-    if (g_cur >= g_end) return false;
     if (single) {
+      if (g_cur >= g_end) return false;
       g_cur = g_end;
       return true;
     }
-    const int nt = prefix[row_cur + 1] - prefix[row_cur];
-    const int64_t local = g_cur - (int64_t)prefix[row_cur] * Y;
-    const int y = (int)(local / nt);
-    const int t0 = (int)(local - (int64_t)y * nt);
-    const int t1 = (int)min((int64_t)nt, (int64_t)t0 + (g_end - g_cur));
-    pc.row = row_cur;
-    pc.y = y;
-    pc.t0 = t0;
-    pc.t1 = t1;
-    pc.len = lens != nullptr ? lens[row_cur] : 0;
-    pc.whole = (t0 == 0 && t1 == nt);
-    pc.slot = first ? 0 : 1;
-    first = false;
-    g_cur += t1 - t0;
-    if (t1 == nt && y == Y - 1) {
-      do {
-        ++row_cur;
-      } while (row_cur < n && prefix[row_cur + 1] == prefix[row_cur]);
+    while (g_cur < g_end) {
+      const int nv = prefix[row_cur + 1] - prefix[row_cur];
+      const int nt = nv - vt;  // nv > 0 for a visited row, so nt >= 1
+      const int64_t local = g_cur - (int64_t)prefix[row_cur] * Y;
+      const int y = (int)(local / nv);
+      const int t0 = (int)(local - (int64_t)y * nv);
+      const int t1 = (int)min((int64_t)nv, (int64_t)t0 + (g_end - g_cur));
+      const int row = row_cur;
+      g_cur += t1 - t0;
+      if (t1 == nv && y == Y - 1) {
+        do {
+          ++row_cur;
+        } while (row_cur < n && prefix[row_cur + 1] == prefix[row_cur]);
+      }
+      if (t0 >= nt) continue;  // weight positions only
+      pc.row = row;
+      pc.y = y;
+      pc.t0 = t0;
+      pc.t1 = min(t1, nt);
+      pc.len = lens != nullptr ? lens[row] : 0;
+      pc.whole = (t0 == 0 && t1 >= nt);
+      pc.slot = first ? 0 : 1;
+      first = false;
+      return true;
     }
-    return true;
+    return false;
   }
 
   // Next stage: tiles [st_t0, st_t1) of piece pc; flags for piece bounds.

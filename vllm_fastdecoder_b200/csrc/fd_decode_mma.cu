@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       if (i < p.n) {
         const int len = p.lens[i];
         lens_s[i] = len;
-        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + kTT - 1) / kTT;
+        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + kTT - 1) / kTT + p.vtiles;
       }
       int v = nt;
 #pragma unroll
@@ -280,9 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     const bool q_owner = pw == 0;
     const uint64_t pol = l2_evict_first_policy();
     StageIter it;
-    it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage);
+    it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage, p.vtiles);
     IdPrefetch ids;
-    ids.it.init(g0, g1, row0, prefix, nullptr, p.n, Y, kTilesPerStage);
+    ids.it.init(g0, g1, row0, prefix, nullptr, p.n, Y, kTilesPerStage, p.vtiles);
     ids.ring = reinterpret_cast<int*>(smem + kOffIds + pw * kIdRingBytes);
     ids.issued = 0;
     const int q_heads = q_owner ? G : 0;
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     // bounded by the two S buffers), P.V as soon as the softmax wrote P.
     if (lane == 0) {
       StageIter it;
-      it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage);
+      it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage, p.vtiles);
       int kq = 0, kp = 0;  // next q.K^T stage, next P.V stage
       int st0, st1;
       bool qf, ql;
@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     const int r = threadIdx.x;  // token row of S, dim of O (TMEM lane)
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     StageIter it;
-    it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage);
+    it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage, p.vtiles);
     int k = 0;
     int st0, st1;
     bool pf, pl;
