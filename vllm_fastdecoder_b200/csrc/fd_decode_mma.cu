@@ -489,8 +489,10 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   } else {
     // ------------------------------------------------------------ softmax warps 0-3
     // Per stage: S -> block max -> P (published) -> fold O of the PREVIOUS
-    // stage, so the P.V round trip of stage k overlaps the softmax of k + 1;
-    // the last stage of a piece is folded at once.
+    // stage, so the P.V round trip of stage k overlaps the softmax of k + 1.
+    // A piece's last stage is folded, and the piece finished (denominators,
+    // output or partial slot), after the NEXT piece's first P is published,
+    // so that round trip and the epilogue overlap the next piece's products.
     const int r = threadIdx.x;  // token row of S, dim of O (TMEM lane)
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     StageIter it;
@@ -502,9 +504,17 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     int h0 = 0;
     int64_t orow = 0;
     bool ok = true, pend = false;
-    // fold O of stage kk (TMEM buffer kk & 1) into acc with the rescale a;
+    // the finished piece whose last fold and epilogue are still to come
+    struct Done {
+      float m[G], l[G], acc[G], alpha[G];
+      int k_last, h0, row, slot, idx;
+      int64_t orow;
+      bool whole;
+    } dn = {};
+    bool pend_done = false;
+    // fold O of stage kk (TMEM buffer kk & 1) into a_acc with the rescale a;
     // column g holds the hi part, column G + g the lo part of P.V
-    auto fold = [&](int kk, const float (&a)[G]) -> bool {
+    auto fold = [&](int kk, const float (&a)[G], float (&a_acc)[G]) -> bool {
       const int bb = kk & 1;
       if (!mbar_wait(&o_full[bb], (uint32_t)(kk >> 1) & 1u, p.err)) return false;
       tc_fence_after();
@@ -514,7 +524,42 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_empty[bb]);
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = acc[g] * a[g] + (o[g] + o[G + g]);
+      for (int g = 0; g < G; ++g) a_acc[g] = a_acc[g] * a[g] + (o[g] + o[G + g]);
+      return true;
+    };
+    // last fold + denominators + output row or partial slot of piece dn
+    auto finish = [&]() -> bool {
+      if (!fold(dn.k_last, dn.alpha, dn.acc)) return false;
+      float L[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float v = dn.l[g];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        L[g] = v;
+      }
+      float* lb = lsum;
+      if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) lb[warp * kN + g] = L[g];
+        mbar_arrive(l_full);
+      }
+      if (!mbar_wait(l_full, (uint32_t)dn.idx & 1u, p.err)) return false;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float Lg = lb[g] + lb[kN + g] + lb[2 * kN + g] + lb[3 * kN + g];
+        const float lse_nat = (dn.m[g] + log2f(Lg)) * kLn2;
+        const int h = dn.h0 + g;
+        const float val = dn.acc[g] / Lg;
+        if (dn.whole) {
+          store_out(p.out, dn.orow * p.out_sn + (int64_t)h * p.out_sh + r, p.out_dtype, val);
+          if (r == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)dn.row * p.lse_sn] = lse_nat;
+        } else {
+          const int64_t pidx = ((int64_t)blockIdx.x * 2 + dn.slot) * G + g;
+          p.part_o[pidx * kD + r] = val;
+          if (r == 0) p.part_lse[pidx] = lse_nat;
+        }
+      }
       return true;
     };
     while (ok && it.next(st0, st1, pf, pl)) {
@@ -616,10 +661,17 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      // ---- O of the previous stage of this piece
-      if (pend && !fold(k - 1, alpha_prev)) {
+      // ---- O of the previous stage of this piece, then the previous piece
+      if (pend && !fold(k - 1, alpha_prev, acc)) {
         ok = false;
         break;
+      }
+      if (pend_done) {
+        if (!finish()) {
+          ok = false;
+          break;
+        }
+        pend_done = false;
       }
       if (!pl) {
 #pragma unroll
@@ -628,48 +680,26 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
         ++k;
         continue;
       }
-      if (!fold(k, alpha)) {
-        ok = false;
-        break;
+      // last stage of the piece: finished after the next piece's first P
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        dn.m[g] = m_run[g];
+        dn.l[g] = l_part[g];
+        dn.acc[g] = acc[g];
+        dn.alpha[g] = alpha[g];
       }
+      dn.k_last = k;
+      dn.h0 = h0;
+      dn.row = pc.row;
+      dn.slot = pc.slot;
+      dn.idx = it.pieces - 1;
+      dn.orow = orow;
+      dn.whole = pc.whole;
+      pend_done = true;
       pend = false;
       ++k;
-
-      // ---- piece epilogue: denominators, output row or partial slot
-      float L[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float v = l_part[g];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        L[g] = v;
-      }
-      float* lb = lsum;
-      if (lane == 0) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) lb[warp * kN + g] = L[g];
-        mbar_arrive(l_full);
-      }
-      if (!mbar_wait(l_full, (uint32_t)(it.pieces - 1) & 1u, p.err)) {
-        ok = false;
-        break;
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float Lg = lb[g] + lb[kN + g] + lb[2 * kN + g] + lb[3 * kN + g];
-        const float lse_nat = (m_run[g] + log2f(Lg)) * kLn2;
-        const int h = h0 + g;
-        const float val = acc[g] / Lg;
-        if (pc.whole) {
-          store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + r, p.out_dtype, val);
-          if (r == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)pc.row * p.lse_sn] = lse_nat;
-        } else {
-          const int64_t pidx = ((int64_t)blockIdx.x * 2 + pc.slot) * G + g;
-          p.part_o[pidx * kD + r] = val;
-          if (r == 0) p.part_lse[pidx] = lse_nat;
-        }
-      }
     }
+    if (ok && pend_done && !finish()) ok = false;
     if (!ok) atomicExch(&abort_flag, 1);
   }
 
