@@ -245,7 +245,7 @@ def run_ours(args, ws, rank, device):
 
     dist = ws > 1
     if args.workload == "c3":
-        batch = workloads.config3(world=ws, rank=rank)
+        batch = workloads.config3(world=ws, rank=rank, ctx=args.ctx)
     else:
         batch = workloads.CONFIGS[args.workload]()
     if args.layout and batch.num_hbm_blocks > 0:
@@ -361,8 +361,9 @@ def run_ours(args, ws, rank, device):
     hbm_b, host_b = batch.kv_bytes()
     step_b = batch.step_bytes()
     achieved = step_b / kern_t / 1e9
-    roof = {"unit": "GB/s", "achieved": round(achieved, 1), "traffic": _traffic("fd_decode_kernel", args.workload),
-            "kernel": "fd_decode_kernel", "algorithmic_bytes_per_launch": step_b,
+    kname = gpu_ops.decode_kernel_name(batch.dtype, batch.D, batch.H, batch.KVH, batch.BS, batch.n, tps)
+    roof = {"unit": "GB/s", "achieved": round(achieved, 1), "traffic": _traffic(kname, args.workload),
+            "kernel": kname, "algorithmic_bytes_per_launch": step_b,
             "kernel_ms": round(kern_t * 1e3, 4)}
     if host_b > 0:
         pcie = pcie_h2d_gbs(device)
@@ -494,6 +495,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3"], default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
+    ap.add_argument("--ctx", type=int, default=131072,
+                    help="c3 context length per row (a smaller one for profiling captures)")
     ap.add_argument("--layout", choices=["nhd", "hnd"], default=None,
                     help="HBM-tier layout: nhd = vLLM [B, BS, KVH, 2D]; hnd = [2, B, KVH, BS, D] "
                          "(default: the workload's own)")

@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -166,6 +167,20 @@ def choose_tiles_per_split(total_tokens: int, n_ctas_per_row: int, block_size: i
     tiles = max(1, math.ceil(total_tokens / tt)) * max(1, n_ctas_per_row)
     tps = max(8, math.ceil(tiles / (num_sms * 2 * 8)))
     return (tps + 3) // 4 * 4
+
+
+def decode_kernel_name(dtype: torch.dtype, head_size: int, num_heads: int, num_kv_heads: int, block_size: int,
+                       n: int, tiles_per_split: int = 0) -> str:
+    """Name of the kernel fd_decode_attn launches for this shape, mirroring
+    the library's dispatch (fd_decode.cu geometry(), fd_decode_mma.cu
+    mma_eligible()): the tcgen05 kernel for 16-bit KV, head size 128, query
+    group 2/4/8, block size a multiple of 16 and the persistent schedule
+    (<= 1024 rows, no explicit split), unless FASTDECODE_B200_MMA=0."""
+    G = num_heads // max(1, num_kv_heads)
+    persistent = tiles_per_split <= 0 and 0 < n <= 1024
+    mma = (persistent and dtype in (torch.float16, torch.bfloat16) and head_size == 128 and G in (2, 4, 8)
+           and block_size % 16 == 0 and not os.environ.get("FASTDECODE_B200_MMA", "").startswith("0"))
+    return "fd_decode_mma_kernel" if mma else "fd_decode_kernel"
 
 
 def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tier_split: int,
