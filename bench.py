@@ -1,7 +1,7 @@
 """Benchmark of the paged decode-attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c0|c2|c3]
+                    [--workload c1|c0|c2|c3|c4]
 
 Under torchrun (N > 1) there is one process per GPU.
 
@@ -14,6 +14,10 @@ vllm_fastdecoder_b200/workloads.py):
   c2            GQA 32/8 bf16, 256 rows, lognormal lengths, all HBM
   c3            8 rows x 131072 tokens, GQA bf16, KV sharded over the N GPUs,
                 partials all-gathered over NCCL and LSE-merged (strong scaling)
+  c4            a continuous-batching decode trace over 32 layers (about 128
+                running requests, most of their KV in the host tier); a step
+                is one decode step of every running request through all 32
+                layers (KV write + decode per layer); N > 1: replicas
 
 Reported: `value` = rows/s with inputs resident (device-timed, CUDA events,
 max over ranks); `e2e` = the same through the public API with the step's q /
@@ -403,6 +407,214 @@ def run_ours(args, ws, rank, device):
     return line
 
 
+# ---------------------------------------------------------------- config 4: the trace
+
+
+def _trace_caches(tr, device):
+    """The trace's KV tiers: vLLM's NHD HBM cache [G, BS, KVH, 2D] (logical
+    [G, KVH, BS, 2D]) and the pinned host tier [blocks, KVH, BS, D] x 2,
+    filled with N(0,1).  One physical cache serves every layer: a layer reads
+    the same bytes as with per-layer caches, and each tier is larger than L2,
+    so nothing is reused across layers."""
+    from vllm_fastdecoder_b200.gpu_ops import KVTier
+
+    dt, KVH, BS, D = tr.dtype, tr.KVH, tr.BS, tr.D
+    gen = torch.Generator(device=device).manual_seed(tr.seed + 1)
+    phys = torch.empty(tr.G, BS, KVH, 2 * D, dtype=dt, device=device)
+    phys.normal_(generator=gen)
+    kv_cache = phys.permute(0, 2, 1, 3)
+    shape = (tr.host_blocks, KVH, BS, D)
+    hk = torch.empty(shape, dtype=dt, pin_memory=True)
+    hv = torch.empty(shape, dtype=dt, pin_memory=True)
+    chunk = max(1, (256 << 20) // (KVH * BS * D * hk.element_size()))
+    tmp = torch.empty((chunk,) + shape[1:], dtype=dt, device=device)
+    for dst in (hk, hv):
+        for s0 in range(0, shape[0], chunk):
+            e = min(shape[0], s0 + chunk)
+            tmp[:e - s0].normal_(generator=gen)
+            dst[s0:e].copy_(tmp[:e - s0])
+    del tmp
+    torch.cuda.synchronize(device)
+    return kv_cache, (KVTier(kv_cache[..., :D], kv_cache[..., D:]), KVTier(hk, hv))
+
+
+def run_trace(args, ws, rank, device):
+    """Config 4 on this GPU (replicas for N > 1): per step, for each of the 32
+    layers, the tier-aware KV write of every running request's new token and
+    the decode over both tiers.  `value` is device time with the step's tables
+    resident; `e2e` runs the plugin's own path per step (host planner,
+    to_device, q/k/v for every layer copied in from pinned memory, 32 x
+    FastDecodeImpl._forward_split, the last layer's output read back)."""
+    from types import SimpleNamespace
+
+    from vllm_fastdecoder_b200 import backend, gpu_ops, plan, state, workloads
+
+    dist = ws > 1
+    W0, K = args.warmup, args.steps
+    tr = workloads.trace4(seed=rank, steps=2 * (W0 + K))
+    L, H, KVH, D, BS, G, dt = tr.layers, tr.H, tr.KVH, tr.D, tr.BS, tr.G, tr.dtype
+    kv_cache, tiers = _trace_caches(tr, device)
+    Rmax = max(st.rows for st in tr.steps)
+    gen = torch.Generator(device=device).manual_seed(tr.seed + 2)
+    q_all = torch.empty(L, Rmax, H, D, dtype=dt, device=device).normal_(generator=gen)
+    k_all = torch.empty(L, Rmax, KVH, D, dtype=dt, device=device).normal_(generator=gen)
+    v_all = torch.empty(L, Rmax, KVH, D, dtype=dt, device=device).normal_(generator=gen)
+    out = torch.empty(Rmax, H, D, dtype=dt, device=device)
+    lse = torch.empty(H, Rmax, dtype=torch.float32, device=device)
+    dev_steps = [(st.block_table.to(device), st.lens.to(device), st.slots.to(device), st.rows,
+                  int(st.lens.max())) for st in tr.steps[:W0 + K]]
+
+    def dev_step(k, evs=None):
+        bt, lens, slots, R, mx = dev_steps[k]
+        for l in range(L):
+            gpu_ops.store_kv_tiered(k_all[l, :R], v_all[l, :R], slots, tiers, G)
+            if evs is not None:
+                evs[l][0].record()
+            gpu_ops.decode_tiered(q_all[l, :R], tiers, G, bt, lens, tr.scale, out[:R], lse[:, :R], max_len=mx)
+            if evs is not None:
+                evs[l][1].record()
+
+    for k in range(W0):
+        dev_step(k)
+    torch.cuda.synchronize(device)
+    gpu_ops.check_device_errors(device)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+           for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(device)
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    clocks.start()
+    time.sleep(0.25)
+    t0.record()
+    for k in range(K):
+        dev_step(W0 + k, evs[k])
+    t1.record()
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    gpu_ops.check_device_errors(device)
+    elapsed = t0.elapsed_time(t1) * 1e-3
+    kern = [sum(a.elapsed_time(b) for a, b in evs[k]) * 1e-3 / L for k in range(K)]  # per decode launch
+    kern_t = sum(kern) / len(kern)
+    rows = sum(dev_steps[W0 + k][3] for k in range(K))
+    if dist:
+        t = torch.tensor([elapsed, kern_t], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed, kern_t = float(t[0]), float(t[1])
+    value = rows * ws / elapsed
+
+    # ---- end to end through the plugin's split path
+    names = [f"model.layers.{l}.self_attn.attn" for l in range(L)]
+    hk, hv = tiers[1].k, tiers[1].v
+    state.STORE = state.CpuKVStore(num_gpu_blocks=G, num_cpu_blocks=tr.host_blocks, block_size=BS,
+                                   num_kv_heads=KVH, head_size=D, dtype=dt, k={nm: hk for nm in names},
+                                   v={nm: hv for nm in names})
+    impl = backend.FastDecodeImpl.__new__(backend.FastDecodeImpl)
+    impl.num_heads, impl.num_kv_heads, impl.head_size = H, KVH, D
+    impl.scale, impl.logits_soft_cap = tr.scale, 0.0
+    impl.vllm_flash_attn_version = 2
+    impl.kv_cache_dtype = "auto"
+    impl.kv_sharing_target_layer_name = None
+    layers = [SimpleNamespace(layer_name=nm, _k_scale=None, _v_scale=None) for nm in names]
+    h_qkv = torch.empty(L, Rmax, H + 2 * KVH, D, dtype=dt, pin_memory=True)
+    h_qkv.normal_()
+    d_qkv = torch.empty(L, Rmax, H + 2 * KVH, D, dtype=dt, device=device)
+    h_out = torch.empty(Rmax, H, D, dtype=dt, pin_memory=True)
+    e_out = torch.empty(Rmax, H, D, dtype=dt, device=device)
+    h2d_bytes = []
+
+    def e2e_step(k):
+        st = tr.steps[W0 + K + k]
+        R = st.rows
+        qsl = torch.arange(R + 1, dtype=torch.int32)
+        width = int(st.block_table.shape[1])
+        hp = plan.build_host_plan(qsl, st.lens, st.block_table, st.slots, G, tr.host_blocks, BS)
+        bt_d = st.block_table.to(device)
+        dp = plan.to_device(hp, bt_d, device)
+        d_qkv[:, :R].copy_(h_qkv[:, :R], non_blocking=True)
+        for l in range(L):
+            q, kk, vv = d_qkv[l, :R].split([H, KVH, KVH], dim=1)
+            impl._forward_split(layers[l], q, kk, vv, kv_cache, dp, e_out[:R])
+        h_out[:R].copy_(e_out[:R], non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        h2d_bytes.append(R * width * 4 + (2 * R + 1) * 4 + R * 8 + L * R * (H + 2 * KVH) * D * 2)
+
+    for k in range(W0):
+        e2e_step(k)
+    h2d_bytes.clear()
+    if dist:
+        torch.distributed.barrier()
+    e2e_rows = 0
+    tt = time.perf_counter()
+    for k in range(K):
+        e2e_step(W0 + k)
+        e2e_rows += tr.steps[W0 + K + W0 + k].rows
+    e2e_t = time.perf_counter() - tt
+    gpu_ops.check_device_errors(device)
+    if dist:
+        t = torch.tensor([e2e_t], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_t = float(t[0])
+
+    # ---- roofline of the decode launches (per launch, averaged over the timed steps)
+    peaks = _peaks()
+    pcie = pcie_h2d_gbs(device)
+    step_b = hbm_b = host_b = 0
+    for k in range(K):
+        b = tr.batch(W0 + k)
+        step_b += b.step_bytes()
+        hb, xb = b.kv_bytes()
+        hbm_b += hb
+        host_b += xb
+    step_b, hbm_b, host_b = step_b / K, hbm_b / K, host_b / K  # one layer's decode launch
+    t_ideal = (step_b - host_b) / (peaks["hbm_gbs"] * 1e9) + host_b / (pcie * 1e9)
+    kname = gpu_ops.decode_kernel_name(dt, D, H, KVH, BS, Rmax)
+    roof = {"unit": "GB/s", "achieved": round(step_b / kern_t / 1e9, 1), "traffic": _traffic(kname, "c4"),
+            "kernel": kname, "algorithmic_bytes_per_launch": int(step_b), "kernel_ms": round(kern_t * 1e3, 4),
+            "bound": "hbm+pcie", "peak": round(step_b / t_ideal / 1e9, 1), "frac": round(t_ideal / kern_t, 4),
+            "peak_note": f"bytes at their tier's rate: HBM {peaks['hbm_gbs']} GB/s ({peaks['source']}), host tier "
+                         f"{pcie:.1f} GB/s (pinned H2D copy measured in this run)",
+            "hbm_bytes": int(step_b - host_b), "host_bytes": int(host_b)}
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W0,
+        "ms_per_step": round(elapsed / K * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) q/K/V; simulated continuous-batching trace)",
+        "config": {
+            "workload": "continuous-batching decode trace (config 4): 32 layers, 32/32 heads, D128, fp16, BS16, "
+                        "HBM tier 2048 blocks, host tier HBM-first up to 32768 blocks, <= 128 running, Poisson "
+                        "arrivals, prompt U[128,1024], output U[64,1024], LIFO block reuse",
+            "unit_note": "a seq is one running request advanced one token through all 32 layers",
+            "rows_per_step": round(rows / K, 1), "layers": L, "host_blocks_touched": tr.host_blocks,
+            "layer_storage": "one physical cache serves the 32 layers (same bytes per layer; each tier > L2)",
+            "hbm_kv_bytes_per_layer": int(hbm_b), "host_kv_bytes_per_layer": int(host_b),
+            "l2": "no flush: each layer streams more KV than the 126 MB L2",
+            "parallelism": f"replicas x{ws}",
+        },
+        "kv_gbs": round((hbm_b + host_b) * L * K * ws / elapsed / 1e9, 1),
+        "e2e": {"value": round(e2e_rows * ws / e2e_t, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(sum(h2d_bytes) / max(1, len(h2d_bytes))),
+                "d2h_bytes_per_step": Rmax * H * D * 2,
+                "api": "FastDecodeImpl._forward_split x 32 layers per step (planner + C ABI fd_store_kv / "
+                       "fd_decode_attn), wall clock with a host sync per step"},
+        "roofline": roof,
+        "clocks": clk,
+        "gpu_launches": K * L * (2 + 1),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        b = tr.batch(W0)
+        res = SimpleNamespace(tiers=tiers, q=q_all[0, :b.n])
+        t, th, r, kind = time_reference(b, res, steps=10, warmup=2, budget_s=15.0)
+        line["cpu_baseline"] = {
+            "value": round(r / (t * L), 2), "unit": UNIT, "cores": th, "kind": kind,
+            "sample": f"the reference's CPU leg of one layer of one step (decode_attn over the host-tier blocks of "
+                      f"{r} rows, {host_b / 1e9:.3f} GB), median of up to 10 calls, times 32 layers",
+            "cpu": _cpu_model(),
+        }
+    return line
+
+
 def _dtype_name(dt) -> str:
     return {torch.float16: "fp16", torch.bfloat16: "bf16", torch.float32: "fp32"}[dt]
 
@@ -440,7 +652,8 @@ def _config(batch, args, ws, tps, has_combine) -> dict:
         }[args.workload],
         "rows": batch.n, "heads": batch.H, "kv_heads": batch.KVH, "head_size": batch.D, "block_size": batch.BS,
         "hbm_kv_bytes": hbm_b, "host_kv_bytes": host_b, "hbm_layout": batch.hbm_layout,
-        "schedule": "split grid" if tps else "persistent (one CTA pair per SM, equal tile ranges)",
+        "schedule": "split grid" if tps else "persistent (all CTAs resident, equal ranges of tiles plus "
+                                             "per-segment weight positions)",
         "tiles_per_split": tps, "split_combine": has_combine,
         "l2": "no flush: each step streams more KV than the 126 MB L2" if hbm_b + host_b > (126 << 20)
               else "KV smaller than L2",
@@ -454,6 +667,8 @@ def _config(batch, args, ws, tps, has_combine) -> dict:
 def run_reference(args, ws, rank, device):
     from vllm_fastdecoder_b200 import workloads
 
+    if args.workload == "c4":
+        return run_reference_trace(args, ws, device)
     if args.workload == "c3":
         batch = workloads.config3(world=1, rank=0)
     else:
@@ -476,6 +691,42 @@ def run_reference(args, ws, rank, device):
     }
 
 
+def run_reference_trace(args, ws, device):
+    """Config 4 on the reference's CPU leg: its decode_attn over the host-tier
+    blocks of one layer of each step (the layers are alike), times 32."""
+    from types import SimpleNamespace
+
+    from vllm_fastdecoder_b200 import workloads
+
+    tr = workloads.trace4(seed=0, steps=args.warmup + args.steps)
+    _, tiers = _trace_caches(tr, device)
+    gen = torch.Generator(device=device).manual_seed(tr.seed + 2)
+    q = torch.empty(max(st.rows for st in tr.steps), tr.H, tr.D, dtype=tr.dtype, device=device).normal_(
+        generator=gen)
+    per_layer, rows, th, kind = [], 0, 1, "reference"
+    for k in range(args.warmup, args.warmup + args.steps):
+        b = tr.batch(k)
+        t, th, r, kind = time_reference(b, SimpleNamespace(tiers=tiers, q=q[:b.n]), steps=3, warmup=1)
+        per_layer.append(t)
+        rows += r
+    t_step = statistics.mean(per_layer) * tr.layers
+    v = round(rows / len(per_layer) / t_step, 2)
+    return {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t_step * 1e3, 4), "higher_is_better": True, "impl": "reference",
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) q/K/V; simulated continuous-batching trace)",
+        "config": {"workload": "continuous-batching decode trace (config 4), 32 layers; the reference's CPU leg"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": th, "kind": kind,
+                         "sample": "decode_attn over the host-tier blocks of one layer of each timed step "
+                                   "(median of 3 calls), times 32 layers", "cpu": _cpu_model()},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's AVX2 decode_attn (fastdecode/csrc/cpu_attn.cpp) compiled from its source, "
+                "timed on this host over the host-tier part of the trace; its GPU FlashAttention leg would "
+                "run concurrently",
+    }
+
+
 def _emit(fd: int, line: dict) -> None:
     os.write(fd, (json.dumps(line) + "\n").encode())
 
@@ -492,7 +743,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=0)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3"], default="c1")
+    ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3", "c4"], default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
     ap.add_argument("--ctx", type=int, default=131072,
@@ -504,7 +755,7 @@ def main() -> int:
     if args.impl == "reference":
         args.split_grid = False
     if args.steps <= 0:
-        args.steps = {"c1": 60, "c0": 400, "c2": 200, "c3": 100}[args.workload]
+        args.steps = {"c1": 60, "c0": 400, "c2": 200, "c3": 100, "c4": 5}[args.workload]
     args.warmup = max(3, args.warmup)
     ws, rank, local = _dist()
     if args.impl == "reference":
@@ -522,7 +773,7 @@ def main() -> int:
 
         torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
-        line = run_ours(args, ws, rank, device)
+        line = run_trace(args, ws, rank, device) if args.workload == "c4" else run_ours(args, ws, rank, device)
         if rank == 0:
             _emit(out_fd, line)
     finally:

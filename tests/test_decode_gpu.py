@@ -253,6 +253,34 @@ def test_decode_bad_block_id_sets_error(ops):
     ops.check_device_errors(dev)  # cleared
 
 
+@pytest.mark.parametrize("vtiles", ["0", "1", "12", "40"])
+@pytest.mark.parametrize("H,KVH,mma", [(8, 2, "1"), (8, 2, "0"), (8, 8, "1")])
+def test_decode_weighted_schedule(ops, monkeypatch, vtiles, H, KVH, mma):
+    """The persistent schedule with any per-segment weight (weight positions
+    carry no work; a CTA whose range opens or ends among them must still
+    write, and the combine read, the right partial slots), on both kernels
+    (query group 4 takes the tensor cores unless disabled; MHA the CUDA
+    cores), with ragged rows so ranges cut segments everywhere."""
+    import random
+
+    monkeypatch.setenv("FASTDECODE_B200_VTILES", vtiles)
+    monkeypatch.setenv("FASTDECODE_B200_MMA", mma)
+    rng = random.Random(int(vtiles) * 7 + H + KVH)
+    n, D, BS = 29, 128, 16
+    lens_l = [rng.choice([0, 1, 16, 17, 130, rng.randint(1, 2500)]) for _ in range(n)]
+    C = sum((x + BS - 1) // BS for x in lens_l) + 8
+    q, kc, vc, bt, lens = O.rand_case(n, H, KVH, D, BS, C, torch.bfloat16, max_len=max(lens_l), seed=n)
+    lens = torch.tensor(lens_l, dtype=torch.int32)
+    perm = torch.randperm(C, generator=torch.Generator().manual_seed(int(vtiles))).tolist()
+    bt = torch.zeros(n, bt.shape[1], dtype=torch.int32)
+    for i, L in enumerate(lens_l):
+        nb = (L + BS - 1) // BS
+        bt[i, :nb] = torch.tensor([perm.pop() for _ in range(nb)], dtype=torch.int32)
+    scale = D ** -0.5
+    out, lse = _run_paged(ops, q, kc, vc, bt, lens, scale)
+    _compare(q, kc, vc, bt, lens, scale, out, lse)
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("H,KVH", [(32, 8), (16, 8), (64, 8)])
 def test_decode_tensor_core_path_matches_cuda_core_path(ops, monkeypatch, dtype, H, KVH):

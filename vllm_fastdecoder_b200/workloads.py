@@ -17,6 +17,11 @@ with the configurations' shapes and value distributions (N(0,1) q/K/V,
       engine's choice), all HBM (NHD)
   c3  8 rows of 131072 tokens, 32/8 heads, bf16; each row's 8192 blocks are
       cut into P contiguous shards, rank r holding shard r in its HBM
+  c4  a continuous-batching decode trace (trace4): 32 layers, 32/32 heads,
+      D 128, fp16, BS 16, HBM tier 2048 blocks, host tier up to 32768
+      blocks, up to 128 running requests, Poisson arrivals, prompts
+      U[128, 1024], outputs U[64, 1024]; blocks are handed out HBM-first and
+      reused last-in-first-out after a request finishes
 
 A Batch holds the CPU-side description (lengths, unified block table, tier
 sizes); materialize() puts the KV tiers and queries in memory.
@@ -161,6 +166,123 @@ def config3(world: int = 1, rank: int = 0, seed: int = 0, ctx: int = 131072) -> 
 
 
 CONFIGS = {"c0": config0, "c1": config1, "c2": config2, "c3": config3}
+
+
+@dataclass
+class TraceStep:
+    """One decode step of the trace: every running request adds one token."""
+
+    block_table: torch.Tensor  # [R, W] int32, unified ids (junk-free past each row's end: zeros)
+    lens: torch.Tensor  # [R] int32, context including the new token
+    slots: torch.Tensor  # [R] int64, unified slot of the new token (id * BS + offset)
+
+    @property
+    def rows(self) -> int:
+        return int(self.lens.numel())
+
+
+@dataclass
+class Trace:
+    name: str
+    layers: int
+    H: int
+    KVH: int
+    D: int
+    BS: int
+    dtype: torch.dtype
+    G: int  # HBM tier blocks (ids < G)
+    host_blocks: int  # host-tier blocks the trace touches (ids G .. G + host_blocks - 1)
+    steps: list[TraceStep]
+    seed: int
+
+    @property
+    def scale(self) -> float:
+        return 1.0 / math.sqrt(self.D)
+
+    def batch(self, k: int) -> Batch:
+        """Step k as a Batch (for byte counts and the reference's CPU leg)."""
+        st = self.steps[k]
+        return Batch(f"{self.name}[{k}]", st.rows, self.H, self.KVH, self.D, self.BS, self.dtype, st.lens,
+                     st.block_table, G=self.G, num_hbm_blocks=self.G, num_host_blocks=self.host_blocks,
+                     hbm_layout="nhd", seed=self.seed)
+
+
+def trace4(seed: int = 0, steps: int = 16, layers: int = 32, max_running: int = 128, G: int = 2048,
+           C: int = 32768, prompt: tuple[int, int] = (128, 1024), output: tuple[int, int] = (64, 1024)) -> Trace:
+    """Config 4: a continuous-batching decode trace, simulated on the CPU.
+
+    The trace starts in steady state: max_running requests whose prompts
+    and output lengths are drawn from the configuration's distributions and
+    whose progress through their outputs is uniform.  Each step every running
+    request decodes one token (taking a new block at a block boundary);
+    requests that reach their output length finish and free their blocks;
+    Poisson arrivals at the rate that keeps max_running busy (max_running /
+    mean output length) join when there is room.  Blocks are handed out
+    HBM-first (ids 1 .. G-1; id 0 is vLLM's null block), then from the host
+    tier (ids >= G), and freed blocks of either tier are reused
+    last-in-first-out, so the host ids in use stay compact."""
+    rng = torch.Generator().manual_seed(seed)
+    BS = 16
+
+    def uni(lo, hi):
+        return int(torch.randint(lo, hi + 1, (1,), generator=rng))
+
+    free_hbm = list(range(1, G))
+    free_host = list(range(G, G + C))
+
+    def alloc():
+        if free_hbm:
+            return free_hbm.pop(0)
+        if free_host:
+            return free_host.pop(0)
+        raise RuntimeError("trace4: out of KV blocks")
+
+    def release(blocks):
+        free_hbm[:0] = [b for b in reversed(blocks) if b < G]
+        free_host[:0] = [b for b in reversed(blocks) if b >= G]
+
+    running = []
+
+    def admit(progress: bool):
+        P, out = uni(*prompt), uni(*output)
+        done = uni(0, out - 1) if progress else 0
+        ctx = P + done
+        blocks = [alloc() for _ in range((ctx + BS - 1) // BS)]
+        running.append({"ctx": ctx, "left": out - done, "blocks": blocks})
+
+    for _ in range(max_running):
+        admit(True)
+    rate = max_running / ((output[0] + output[1]) / 2)
+    queue = 0
+    out_steps = []
+    max_host = G - 1
+    for _ in range(steps):
+        queue += int(torch.poisson(torch.tensor([rate]), generator=rng))
+        while queue > 0 and len(running) < max_running:
+            admit(False)
+            queue -= 1
+        R = len(running)
+        W = max((r["ctx"] + BS) // BS + 1 for r in running)
+        bt = torch.zeros(R, W, dtype=torch.int32)
+        lens = torch.empty(R, dtype=torch.int32)
+        slots = torch.empty(R, dtype=torch.int64)
+        for i, r in enumerate(running):
+            pos = r["ctx"]  # the new token's position
+            if pos % BS == 0:
+                r["blocks"].append(alloc())
+            bl = r["blocks"]
+            bt[i, :len(bl)] = torch.tensor(bl, dtype=torch.int32)
+            lens[i] = pos + 1
+            slots[i] = bl[pos // BS] * BS + pos % BS
+            max_host = max(max_host, max(bl))
+        out_steps.append(TraceStep(bt, lens, slots))
+        for r in list(running):
+            r["ctx"] += 1
+            r["left"] -= 1
+            if r["left"] == 0:
+                running.remove(r)
+                release(r["blocks"])
+    return Trace("c4", layers, 32, 32, 128, BS, torch.float16, G, max(1, max_host - G + 1), out_steps, seed)
 
 
 @dataclass
