@@ -366,7 +366,10 @@ def run_ours(args, ws, rank, device):
     step_b = batch.step_bytes()
     achieved = step_b / kern_t / 1e9
     kname = gpu_ops.decode_kernel_name(batch.dtype, batch.D, batch.H, batch.KVH, batch.BS, batch.n, tps)
-    roof = {"unit": "GB/s", "achieved": round(achieved, 1), "traffic": _traffic(kname, args.workload),
+    traffic = _traffic(kname, args.workload)
+    if traffic is not None and args.workload == "c3":
+        traffic = int(traffic * (args.ctx / ws) / 131072)  # the table holds one GPU's full-context launch
+    roof = {"unit": "GB/s", "achieved": round(achieved, 1), "traffic": traffic,
             "kernel": kname, "algorithmic_bytes_per_launch": step_b,
             "kernel_ms": round(kern_t * 1e3, 4)}
     if host_b > 0:

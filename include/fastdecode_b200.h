@@ -63,7 +63,10 @@ enum fd_device_error {
   FD_DEVERR_LEN = 2,       /* lens[i] needs more blocks than the table row holds */
   FD_DEVERR_TIMEOUT = 3,   /* a bounded wait on an mbarrier gave up */
   FD_DEVERR_SLOT = 4,      /* KV-write slot outside both tiers */
-  FD_DEVERR_SPLITS = 5     /* lens[i] exceeds the max_len the grid was sized for */
+  FD_DEVERR_SPLITS = 5,    /* lens[i] exceeds the max_len the grid was sized for */
+  FD_DEVERR_PLAN = 6       /* fd_plan_step: bad query offsets, or a request that
+                              extends prior context by > 1 token while part of
+                              its KV is in the host tier (fastdecode/plan.py:142-149) */
 };
 
 /* ---------------------------------------------------------------- types */
@@ -114,8 +117,10 @@ typedef struct fd_decode_args {
   int32_t dtype; /* of q, K and V */
 
   /* output rows: out[orow, h, d], orow = out_rows ? out_rows[i] : i
-   * (out_rows fuses output.index_copy_ of backend.py:356); out_dtype is
-   * dtype or FD_DTYPE_F32 (fp32 partials for a later merge) */
+   * (out_rows fuses output.index_copy_ of backend.py:356); a negative
+   * out_rows[i] writes no output for row i (padding of a device-built row
+   * list); out_dtype is dtype or FD_DTYPE_F32 (fp32 partials for a later
+   * merge) */
   void *out;
   int32_t out_dtype;
   int32_t _pad0;
@@ -136,6 +141,12 @@ typedef struct fd_decode_args {
   void *workspace; /* scratch for split partials, fd_decode_workspace_size() bytes */
   size_t workspace_bytes;
   int32_t *error;  /* optional device error word */
+
+  /* optional: row i reads block-table row bt_rows[i] (else row i), so a
+   * device-built list of work rows (fd_plan_step) runs on the batch's own
+   * table without gathering it (replaces the index_select of table rows in
+   * fastdecode/plan.py:224-245) */
+  const int32_t *bt_rows;
 } fd_decode_args;
 
 /* ---------------------------------------------------------------- decode */
@@ -218,6 +229,114 @@ FD_API size_t fd_decode_attn_paged_workspace_size(int32_t n, int32_t num_heads,
 
 /* ---------------------------------------------------------------- merge */
 
+/* ---------------------------------------------------------------- plan */
+
+/* Slots of the plan header (int32[FD_PLAN_HEADER_LEN], device memory). */
+enum fd_plan_header {
+  FD_PLAN_FLAGS = 0,          /* FD_PLAN_* bits below */
+  FD_PLAN_N_TOK = 1,          /* tokens of the step (query_start_loc[R]) */
+  FD_PLAN_N_CPU_W = 2,        /* tokens whose KV goes to the host tier */
+  FD_PLAN_N_P = 3,            /* class P requests (all KV in HBM) */
+  FD_PLAN_N_P_TOK = 4,
+  FD_PLAN_P_MAX_Q = 5,
+  FD_PLAN_P_MAX_K = 6,
+  FD_PLAN_N_S = 7,            /* class S: decodes touching the host tier */
+  FD_PLAN_S_GPU_WIDTH = 8,    /* width of the compacted HBM table (multiple of 16) */
+  FD_PLAN_S_MAX_GPU_LEN = 9,
+  FD_PLAN_S_CPU_WIDTH = 10,   /* width of the compacted host table */
+  FD_PLAN_N_F = 11,           /* class F: fresh prefills touching the host tier */
+  FD_PLAN_N_F_TOK = 12,
+  FD_PLAN_F_MAX = 13,
+  FD_PLAN_S_MAX_LEN = 14,
+  FD_PLAN_N_PD = 15,          /* P requests that are decodes */
+  FD_PLAN_PD_MAX_LEN = 16,
+  FD_PLAN_N_PP = 17,          /* P requests that are prefills */
+  FD_PLAN_N_PP_TOK = 18,
+  FD_PLAN_PP_MAX_Q = 19,
+  FD_PLAN_PP_MAX_K = 20,
+  FD_PLAN_N_DECODE = 21,      /* rows of the decode list (S and P decodes) */
+  FD_PLAN_DECODE_MAX_LEN = 22,
+  FD_PLAN_HEADER_LEN = 32
+};
+enum fd_plan_flags {
+  FD_PLAN_TOUCHES_HOST = 1, /* some request or new token uses the host tier (the
+                               reference planner returns None otherwise) */
+  FD_PLAN_BAD_BLOCK_ID = 2, /* a block id >= G + C (reference: RuntimeError) */
+  FD_PLAN_HOST_EXTEND = 4,  /* reference: NotImplementedError (FD_DEVERR_PLAN) */
+  FD_PLAN_BAD_OFFSETS = 8   /* query_start_loc not 0-based, decreasing, or past
+                               max_tokens: nothing else was written */
+};
+
+/* The per-step plan computed on the device (fastdecode/plan.py:103-245).
+ * Inputs are device tensors of the step; outputs are caller-allocated
+ * device buffers of the given capacities (R = num_reqs rows, T =
+ * max_tokens tokens); the header says how many entries of each are valid.
+ * Each output matches the reference HostPlan / DevicePlan field of the same
+ * name bit for bit. */
+typedef struct fd_plan_args {
+  const int32_t *query_start_loc; /* [R + 1] */
+  const int32_t *seq_lens;        /* [R] tokens including this step's */
+  const int32_t *block_table;     /* [R, bt_stride], unified ids */
+  int64_t bt_stride;
+  int32_t bt_width;
+  int32_t num_reqs;
+  const int64_t *slot_mapping;    /* [>= T] unified slots (-1: padding) */
+  int32_t max_tokens;             /* T */
+  int32_t block_size;
+  int64_t num_gpu_blocks;         /* G */
+  int64_t num_cpu_blocks;         /* C */
+
+  int32_t *header;                /* [FD_PLAN_HEADER_LEN] */
+  /* KV writes */
+  int64_t *gpu_slot_mapping;      /* [T] host slots replaced by -1 */
+  int64_t *cpu_w_tok;             /* [T] */
+  int64_t *cpu_w_slot;            /* [T] host-relative */
+  /* P */
+  int64_t *p_tok;                 /* [T] */
+  int32_t *p_cu;                  /* [R + 1] */
+  int32_t *p_seqlens;             /* [R] */
+  int64_t *p_req;                 /* [R] */
+  /* S */
+  int64_t *s_tok;                 /* [R] */
+  int32_t *s_gpu_bt;              /* [R, s_gpu_bt_stride], width in the header */
+  int64_t s_gpu_bt_stride;        /* >= bt_width rounded up to 16 */
+  int32_t *s_gpu_lens;            /* [R] */
+  int32_t *s_cpu_bt;              /* [R, s_cpu_bt_stride] host-relative ids */
+  int64_t s_cpu_bt_stride;        /* >= bt_width */
+  int32_t *s_cpu_lens;            /* [R] */
+  /* F */
+  int64_t *f_tok;                 /* [T] */
+  int32_t *f_cu;                  /* [R + 1] */
+  /* this engine's additions (plan.py of this repository) */
+  int64_t *s_req;                 /* [R] */
+  int32_t *s_seq_lens;            /* [R] */
+  int64_t *pd_req;                /* [R] */
+  int64_t *pd_tok;                /* [R] */
+  int32_t *pd_seq_lens;           /* [R] */
+  int64_t *pp_req;                /* [R] */
+  int64_t *pp_tok;                /* [T] */
+  int32_t *pp_cu;                 /* [R + 1] */
+  int32_t *pp_seqlens;            /* [R] */
+  /* decode list for fd_decode_attn: q_rows = out_rows = d_tok, bt_rows =
+   * d_row, lens = d_lens, n = R; entries past the header's N_DECODE have
+   * d_tok = -1 and d_lens = 0 (no work, no output) */
+  int64_t *d_tok;                 /* [R] */
+  int32_t *d_row;                 /* [R] */
+  int32_t *d_lens;                /* [R] */
+  int32_t *error;                 /* optional device error word */
+} fd_plan_args;
+
+/* Replaces the reference's host planner build_host_plan + to_device
+ * (fastdecode/plan.py:103-245, called per step at fastdecode/backend.py:
+ * 140-178): one single-CTA launch on the caller's stream, no host
+ * synchronisation, no host copies.  Capacities are checked on the host;
+ * query offsets past max_tokens are caught on the device
+ * (FD_PLAN_BAD_OFFSETS, FD_DEVERR_PLAN). */
+FD_API int fd_plan_step(const fd_plan_args *a, void *stream);
+
+/* sizeof(fd_plan_args) as compiled into the library (binding check). */
+FD_API size_t fd_plan_args_bytes(void);
+
 /* Two-way log-sum-exp merge, the rule of vLLM merge_attn_states as restated
  * in fastdecode/cpu_ops.py:93-113 and called at fastdecode/backend.py:54-55,
  * 354-356: an lse of +inf (FlashAttention's empty row) counts as -inf, and a
@@ -280,7 +399,7 @@ FD_API int fd_host_device_pointer(void *host, void **device_ptr);
 FD_API int fd_host_register(void *host, size_t bytes);
 FD_API int fd_host_unregister(void *host);
 
-/* Library version, e.g. 100 for 0.1.0. */
+/* Library version, e.g. 101 for 0.1.1 (101: fd_plan_step, bt_rows). */
 FD_API int fd_version(void);
 
 /* sizeof(fd_decode_args) and sizeof(fd_kv_tier) as compiled into the

@@ -65,12 +65,17 @@ class GpuOpsTorchPrefill(backend._GpuOps):
     fa = staticmethod(torch_fa)
 
 
-@pytest.mark.parametrize("dtype,H,KVH,two_pass", [
-    (torch.float16, 8, 8, False),
-    (torch.bfloat16, 16, 4, False),
-    (torch.float16, 8, 2, True),
+@pytest.mark.parametrize("dtype,H,KVH,two_pass,device_plan", [
+    (torch.float16, 8, 8, False, False),
+    (torch.bfloat16, 16, 4, False, False),
+    (torch.float16, 8, 2, True, False),
+    (torch.float16, 8, 8, False, True),
+    (torch.bfloat16, 16, 4, False, True),
 ])
-def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass):
+def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass, device_plan):
+    """device_plan: decode-only steps are planned on the GPU (fd_plan_step)
+    and run through FastDecodeImpl._forward_device, as the metadata builder
+    does for them; steps with prefills take the host planner."""
     if two_pass:
         monkeypatch.setenv(config.ENV_TWO_PASS, "1")
     monkeypatch.setattr(backend, "OPS", GpuOpsTorchPrefill)
@@ -113,7 +118,7 @@ def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass):
         free_gpu[:0] = [b for b in blocks if b < G]
         free_cpu.extend(b for b in blocks if b >= G)
 
-    running, n_split, n_rows = [], 0, 0
+    running, n_split, n_rows, n_dev = [], 0, 0, 0
     for step in range(steps):
         rows = []
         for r in list(running):
@@ -160,13 +165,21 @@ def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass):
         v = v.reshape(Tp, KVH, D)
 
         width = max(1, min((max(seqs) + BS - 1) // BS, W))
-        hp = plan.build_host_plan(qsl, seq, bt[:, :width], slots, G, C, BS)
+        decode_only = all(ql == 1 for ql in qlens)
+        hp = None if (device_plan and decode_only) else plan.build_host_plan(qsl, seq, bt[:, :width], slots, G, C, BS)
         # the unified pool gets this step's K/V (the reference cache)
         sl = slots.to(dev)
         uk[sl // BS, :, sl % BS] = k[:T]
         uv[sl // BS, :, sl % BS] = v[:T]
         out = torch.full((Tp, H, D), float("nan"), dtype=dtype, device=dev)
-        if hp is None:
+        if device_plan and decode_only:
+            dp = plan.plan_on_device(qsl.to(dev), seq.to(dev), bt[:, :width].to(dev).contiguous(), sl, G, C, BS)
+            ds = plan.DeviceDecodeStep(dp, R, T, max(seqs))
+            impl._forward_device(layer, q, k, v, kv_cache, ds, sl, out)
+            gpu_ops.check_device_errors(dev)
+            n_dev += 1
+            continue_check = True
+        elif hp is None:
             # an all-HBM step takes vLLM's stock path; only mirror its KV write
             kv_cache[sl // BS, :, sl % BS, :D] = k[:T]
             kv_cache[sl // BS, :, sl % BS, D:] = v[:T]
@@ -214,5 +227,8 @@ def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass):
             if r["left"] <= 0:
                 running.remove(r)
                 release(r["blocks"])
-    assert n_split >= steps // 2 and n_rows > 100
+    if device_plan:
+        assert n_dev >= 5 and n_split + n_dev >= steps // 2 and n_rows > 100, (n_dev, n_split, n_rows)
+    else:
+        assert n_split >= steps // 2 and n_rows > 100
     state.STORE = None

@@ -41,6 +41,19 @@ def test_struct_mirrors_match_the_library():
     assert lib.fd_abi_sizes(ctypes.byref(a), ctypes.byref(b)) == 0
     assert a.value == ctypes.sizeof(nat.FdDecodeArgs)
     assert b.value == ctypes.sizeof(nat.FdKvTier)
+    assert lib.fd_plan_args_bytes() == ctypes.sizeof(nat.FdPlanArgs)
+
+
+def test_plan_step_host_checks_need_no_gpu():
+    """fd_plan_step rejects bad sizes and missing buffers before any launch."""
+    lib = nat.load()
+    a = nat.FdPlanArgs()
+    a.num_reqs, a.bt_width, a.block_size, a.bt_stride = 4, 8, 16, 4  # stride < width
+    assert lib.fd_plan_step(ctypes.byref(a), None) == 1
+    assert b"bt_stride" in lib.fd_last_error_message()
+    a.bt_stride, a.s_gpu_bt_stride, a.s_cpu_bt_stride = 8, 16, 8
+    assert lib.fd_plan_step(ctypes.byref(a), None) == 1  # buffers missing
+    assert b"null" in lib.fd_last_error_message()
 
 
 def test_host_side_argument_checks_need_no_gpu():

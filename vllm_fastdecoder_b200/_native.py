@@ -49,6 +49,38 @@ class FdDecodeArgs(ctypes.Structure):
         ("lse", c_void_p), ("lse_stride_h", c_int64), ("lse_stride_n", c_int64),
         ("max_len", c_int32), ("tiles_per_split", c_int32),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("error", c_void_p),
+        ("bt_rows", c_void_p),
+    ]
+
+
+# fd_plan_header slots and fd_plan_flags bits
+PLAN_HEADER_LEN = 32
+PLAN_FIELDS = {
+    "flags": 0, "n_tok": 1, "n_cpu_w": 2, "n_p": 3, "n_p_tok": 4, "p_max_q": 5, "p_max_k": 6, "n_s": 7,
+    "s_gpu_width": 8, "s_max_gpu_len": 9, "s_cpu_width": 10, "n_f": 11, "n_f_tok": 12, "f_max": 13,
+    "s_max_len": 14, "n_pd": 15, "pd_max_len": 16, "n_pp": 17, "n_pp_tok": 18, "pp_max_q": 19,
+    "pp_max_k": 20, "n_decode": 21, "decode_max_len": 22,
+}
+PLAN_TOUCHES_HOST, PLAN_BAD_BLOCK_ID, PLAN_HOST_EXTEND, PLAN_BAD_OFFSETS = 1, 2, 4, 8
+
+
+class FdPlanArgs(ctypes.Structure):
+    _fields_ = [
+        ("query_start_loc", c_void_p), ("seq_lens", c_void_p), ("block_table", c_void_p),
+        ("bt_stride", c_int64), ("bt_width", c_int32), ("num_reqs", c_int32),
+        ("slot_mapping", c_void_p), ("max_tokens", c_int32), ("block_size", c_int32),
+        ("num_gpu_blocks", c_int64), ("num_cpu_blocks", c_int64),
+        ("header", c_void_p),
+        ("gpu_slot_mapping", c_void_p), ("cpu_w_tok", c_void_p), ("cpu_w_slot", c_void_p),
+        ("p_tok", c_void_p), ("p_cu", c_void_p), ("p_seqlens", c_void_p), ("p_req", c_void_p),
+        ("s_tok", c_void_p), ("s_gpu_bt", c_void_p), ("s_gpu_bt_stride", c_int64), ("s_gpu_lens", c_void_p),
+        ("s_cpu_bt", c_void_p), ("s_cpu_bt_stride", c_int64), ("s_cpu_lens", c_void_p),
+        ("f_tok", c_void_p), ("f_cu", c_void_p),
+        ("s_req", c_void_p), ("s_seq_lens", c_void_p),
+        ("pd_req", c_void_p), ("pd_tok", c_void_p), ("pd_seq_lens", c_void_p),
+        ("pp_req", c_void_p), ("pp_tok", c_void_p), ("pp_cu", c_void_p), ("pp_seqlens", c_void_p),
+        ("d_tok", c_void_p), ("d_row", c_void_p), ("d_lens", c_void_p),
+        ("error", c_void_p),
     ]
 
 
@@ -80,6 +112,8 @@ SIGNATURES = {
     "fd_host_device_pointer": (c_int32, [c_void_p, POINTER(c_void_p)]),
     "fd_host_register": (c_int32, [c_void_p, c_size_t]),
     "fd_host_unregister": (c_int32, [c_void_p]),
+    "fd_plan_step": (c_int32, [POINTER(FdPlanArgs), c_void_p]),
+    "fd_plan_args_bytes": (c_size_t, []),
     "fd_version": (c_int32, []),
     "fd_abi_sizes": (c_int32, [POINTER(c_size_t), POINTER(c_size_t)]),
 }

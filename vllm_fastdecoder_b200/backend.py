@@ -35,7 +35,7 @@ import os
 import torch
 
 from vllm_fastdecoder_b200 import config, state
-from vllm_fastdecoder_b200.plan import DevicePlan, build_host_plan, to_device
+from vllm_fastdecoder_b200.plan import DeviceDecodeStep, DevicePlan, build_host_plan, plan_on_device, to_device
 
 logger = logging.getLogger("fastdecode")
 
@@ -186,6 +186,7 @@ class FastDecodeMetadataBuilder(FlashAttentionMetadataBuilder):
         cm = common_attn_metadata
         md = super().build(0, cm, fast_build)
         md.fd_plan = None
+        md.fd_dplan = None
         md.fd_num_reqs = cm.num_reqs
         md.fd_seq_cpu = None
         store = state.STORE
@@ -201,6 +202,12 @@ class FastDecodeMetadataBuilder(FlashAttentionMetadataBuilder):
             return md
         qsl = cm.query_start_loc_cpu[: R + 1]
         upper = getattr(cm, "seq_lens_cpu_upper_bound", None)
+        if (config.device_plan() and upper is not None and cm.block_table_tensor.is_cuda
+                and bool(((qsl[1:] - qsl[:-1]) <= 1).all())):
+            # a decode-only step: planned on the GPU from the device tensors,
+            # no block-table or slot copy to the host (fd_plan_step)
+            md.fd_dplan = self._device_plan(cm, R, int(qsl[-1]), int(upper[:R].max()), store)
+            return md
         seq = upper[:R] if upper is not None else cm.seq_lens[:R].cpu()
         width = max(1, min(int((int(seq.max()) + bs - 1) // bs), cm.block_table_tensor.shape[1]))
         bt_dev = cm.block_table_tensor[:R]
@@ -214,6 +221,24 @@ class FastDecodeMetadataBuilder(FlashAttentionMetadataBuilder):
         if config.stats_enabled():
             self._log_stats(hp, R)
         return md
+
+    def _device_plan(self, cm, R: int, n_tok: int, max_seq: int, store):
+        """fd_plan_step over the step's device tensors; the plan buffers are
+        kept and reused while they fit."""
+        bt = cm.block_table_tensor[:R]
+        if bt.stride(1) != 1:
+            bt = bt.contiguous()
+        qsl = cm.query_start_loc[: R + 1]
+        seq = cm.seq_lens[:R]
+        if qsl.dtype != torch.int32:
+            qsl = qsl.to(torch.int32)
+        if seq.dtype != torch.int32:
+            seq = seq.to(torch.int32)
+        buf = getattr(self, "_dplan_buf", None)
+        dp = plan_on_device(qsl, seq, bt, cm.slot_mapping, store.num_gpu_blocks, store.num_cpu_blocks,
+                            store.block_size, out=buf, max_tokens=n_tok)
+        self._dplan_buf = dp
+        return DeviceDecodeStep(dp, R, n_tok, max_seq)
 
     def _log_stats(self, hp, num_reqs) -> None:
         a = self._acc
@@ -257,6 +282,9 @@ class FastDecodeImpl(FlashAttentionImpl):
             raise NotImplementedError("FastDecode: fused output quantization")
         if attn_metadata is None:  # profiling run
             return output.fill_(0)
+        dstep = getattr(attn_metadata, "fd_dplan", None)
+        if dstep is not None:
+            return self._forward_device(layer, query, key, value, kv_cache, dstep, attn_metadata.slot_mapping, output)
         plan = getattr(attn_metadata, "fd_plan", None)
         if plan is None:
             if self.kv_sharing_target_layer_name is None and key is not None:
@@ -264,6 +292,26 @@ class FastDecodeImpl(FlashAttentionImpl):
                                                       attn_metadata.slot_mapping)
             return super().forward(layer, query, key, value, kv_cache, attn_metadata, output)
         return self._forward_split(layer, query, key, value, kv_cache, plan, output)
+
+    def _forward_device(self, layer, query, key, value, kv_cache, ds: "DeviceDecodeStep", slot_mapping, output):
+        """A decode-only step planned on the GPU: one tier-aware KV write of
+        the step's tokens and one decode launch over the planner's decode
+        list (every request, whichever tiers its blocks are in), all inputs
+        on the device.  Replaces the reference's split path for such steps
+        (fastdecode/backend.py:257-357)."""
+        store = state.STORE
+        assert store is not None
+        D = self.head_size
+        G = store.num_gpu_blocks
+        hbm = OPS.tier(kv_cache[..., :D], kv_cache[..., D:])
+        host = OPS.tier(store.k[layer.layer_name], store.v[layer.layer_name])
+        tiers = (hbm, host)
+        if self.kv_sharing_target_layer_name is None and ds.n_tok:
+            OPS.store_kv(key[: ds.n_tok], value[: ds.n_tok], slot_mapping[: ds.n_tok], tiers, G)
+        dp = ds.plan
+        OPS.decode(query, tiers, G, dp.block_table, dp.d_lens, self.scale, output, q_rows=dp.d_tok,
+                   out_rows=dp.d_tok, bt_rows=dp.d_row, n=ds.num_reqs, max_len=ds.max_seq)
+        return output
 
     def _forward_split(self, layer, query, key, value, kv_cache, dp: DevicePlan, output):
         hp = dp.host

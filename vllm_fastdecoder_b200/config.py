@@ -19,6 +19,8 @@ ENV_CPU_BLOCKS = "FASTDECODE_CPU_BLOCKS"
 ENV_CPU_KV_GB = "FASTDECODE_CPU_KV_GB"
 ENV_STATS = "FASTDECODE_STATS"
 ENV_TWO_PASS = "FASTDECODE_B200_TWO_PASS"
+# decode-only steps are planned on the GPU (fd_plan_step) unless set to 0
+ENV_DEVICE_PLAN = "FASTDECODE_B200_DEVICE_PLAN"
 
 
 def enabled() -> bool:
@@ -35,6 +37,10 @@ def stats_enabled() -> bool:
 
 def two_pass() -> bool:
     return _flag(ENV_TWO_PASS)
+
+
+def device_plan() -> bool:
+    return os.environ.get(ENV_DEVICE_PLAN, "1") not in ("", "0", "false", "False") and not two_pass()
 
 
 def kv_bytes_per_block(kv_cache_config) -> int:

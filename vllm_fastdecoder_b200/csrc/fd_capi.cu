@@ -50,6 +50,9 @@ extern "C" const char* fd_device_error_string(int32_t code) {
       return "KV-write slot outside both KV tiers";
     case FD_DEVERR_SPLITS:
       return "sequence length exceeds the max_len the launch was sized for";
+    case FD_DEVERR_PLAN:
+      return "step planner: query offsets not 0-based, decreasing or past the token capacity, or a request "
+             "extending prior context by more than one token while part of its KV is in the host tier";
     default:
       return "unknown device error";
   }
@@ -101,7 +104,7 @@ extern "C" int fd_host_unregister(void* host) {
   return fdh::cuda_status(cudaHostUnregister(host), "cudaHostUnregister");
 }
 
-extern "C" int fd_version(void) { return 100; }
+extern "C" int fd_version(void) { return 101; }
 
 extern "C" int fd_abi_sizes(size_t* decode_args_bytes, size_t* kv_tier_bytes) {
   if (decode_args_bytes != nullptr) *decode_args_bytes = sizeof(fd_decode_args);

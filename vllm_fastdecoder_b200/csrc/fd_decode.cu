@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         continue;
       }
       const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-      for (int o = threadIdx.x; o < p.H * D; o += blockDim.x) {
+      for (int o = threadIdx.x; orow >= 0 && o < p.H * D; o += blockDim.x) {
         const int h = o / D, d = o - h * D;
         store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
       }
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         const int kh = blockIdx.y / p.gcs, gc = blockIdx.y - kh * p.gcs;
         const int h0 = kh * p.G + gc * GQ;
         const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-        for (int o = threadIdx.x; o < GQ * D; o += blockDim.x) {
+        for (int o = threadIdx.x; orow >= 0 && o < GQ * D; o += blockDim.x) {
           const int g = o / D, d = o - g * D;
           store_out(p.out, orow * p.out_sn + (int64_t)(h0 + g) * p.out_sh + d, p.out_dtype, 0.f);
         }
@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   StageIter pieces;
   if (p.persistent) {
     pieces.init(g_cur, g_end, row_cur, prefix, p.lens, p.n, Y, C::kNW, p.vtiles);
+    pieces.trows = p.bt_rows;
   } else {
     const int i = blockIdx.z;
     const int len = p.lens[i];
@@ -213,6 +214,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     sp.t0 = blockIdx.x * p.tiles_per_split;
     sp.t1 = min(ntiles, sp.t0 + p.tiles_per_split);
     sp.len = len;
+    sp.trow = p.bt_rows != nullptr ? p.bt_rows[i] : i;
     sp.whole = (nsplits == 1);
     sp.slot = blockIdx.x;
     pieces.init_single(sp, C::kNW);
@@ -569,7 +571,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
       const float lse_nat = (M + log2f(L)) * kLn2;
       const int h = h0 + g;
       if (pc.whole) {
-        store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
+        if (orow >= 0) store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
         if (d == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)pc.row * p.lse_sn] = lse_nat;
       } else {
         const int64_t pidx = p.persistent ? ((int64_t)blockIdx.x * 2 + pc.slot) * GQ + g
@@ -609,7 +611,7 @@ __global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, in
   for (int s = 0; s < ns; ++s) L += wsm[s];
   const float inv = 1.f / L;
   const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  for (int d = threadIdx.x; orow >= 0 && d < D; d += blockDim.x) {
     float O = 0.f;
     for (int s = 0; s < ns; ++s) O = fmaf(wsm[s], p.part_o[(base + s) * D + d], O);
     store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O * inv);
@@ -664,7 +666,7 @@ __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParam
       O = fmaf(w, p.part_o[s * D + d], O);
     }
     const int h = h0 + g;
-    store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O / L);
+    if (orow >= 0) store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, O / L);
     if (d == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = M + logf(L);
   }
 }
@@ -985,6 +987,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
   p.out_sn = a->out_stride_n;
   p.out_sh = a->out_stride_h;
   p.out_rows = a->out_rows;
+  p.bt_rows = a->bt_rows;
   p.lse = a->lse;
   p.lse_sh = a->lse_stride_h;
   p.lse_sn = a->lse_stride_n;

@@ -29,6 +29,7 @@ struct alignas(64) DecodeParams {
   int contig[2];
   int64_t split;
   const int32_t* bt;
+  const int32_t* bt_rows;  // optional: work row i reads table row bt_rows[i]
   int64_t bt_stride;
   int bt_width;
   const int32_t* lens;
@@ -67,6 +68,7 @@ constexpr int kMaxPersistentCtas = 320;
 // it writes an fp32 partial into `slot`.
 struct Piece {
   int row, y, t0, t1, len, slot;
+  int trow;  // block-table row of `row` (bt_rows indirection)
   bool whole;
 };
 
@@ -84,6 +86,7 @@ struct StageIter {
   int64_t g_cur, g_end;
   const int* prefix;
   const int* lens;
+  const int32_t* trows;  // block-table row of each work row (null: the row itself)
   int n, Y, tps, vt;
   int row_cur;
   bool first, have, single;
@@ -94,6 +97,7 @@ struct StageIter {
   __device__ void init(int64_t g0, int64_t g1, int row, const int* prefix_s, const int* lens_s, int n_rows, int y,
                        int tiles_per_stage, int vtiles) {
     vt = vtiles;
+    trows = nullptr;
     g_cur = g0;
     g_end = g1;
     prefix = prefix_s;
@@ -111,6 +115,7 @@ struct StageIter {
 
   __device__ void init_single(const Piece& piece, int tiles_per_stage) {
     pc = piece;
+    trows = nullptr;
     g_cur = 0;
     g_end = 1;
     tps = tiles_per_stage;
@@ -147,6 +152,7 @@ struct StageIter {
       pc.t0 = t0;
       pc.t1 = min(t1, nt);
       pc.len = lens != nullptr ? lens[row] : 0;
+      pc.trow = trows != nullptr ? trows[row] : row;
       pc.whole = (t0 == 0 && t1 >= nt);
       pc.slot = first ? 0 : 1;
       first = false;
@@ -204,7 +210,7 @@ struct IdPrefetch {
       const int tile = a0 + first_tile + lane;
       if (lane < nlanes && tile < a1)
         cp_async4(ring + (issued % kIdRing) * kIdLanes + lane,
-                  p.bt + (int64_t)it.pc.row * p.bt_stride + tile / p.tiles_per_block);
+                  p.bt + (int64_t)it.pc.trow * p.bt_stride + tile / p.tiles_per_block);
       if (apf && heads_per_piece > 0) {
         if (p.q_rows != nullptr) {
           if (lane == 0) prefetch_l2(p.q_rows + it.pc.row);

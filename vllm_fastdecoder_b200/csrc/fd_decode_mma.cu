@@ -69,9 +69,10 @@ constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kOffIds = (kOffTmem + 16 + 127) / 128 * 128;  // producer's block-id ring
 constexpr int kOffPrefix = kOffIds + kProd * kIdRingBytes;
 constexpr int kSmemFixed = kOffPrefix + 1024;  // + 1024 for aligning the base
-// the tile prefix [n + 1] and the lengths [n] follow, 16-byte aligned each
+// the tile prefix [n + 1], the lengths [n] and the block-table rows [n]
+// follow, 16-byte aligned each
 constexpr int kRowsBytes = (kMaxPersistentRows + 1 + 3) / 4 * 16;
-static_assert(kSmemFixed + 2 * kRowsBytes <= 227 * 1024, "smem budget");
+static_assert(kSmemFixed + 3 * kRowsBytes <= 227 * 1024, "smem budget");
 
 // UMMA shared-memory descriptor, 128-byte swizzle, sm_100 version bits.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);  // [n + 1] tile prefix
   int* lens_s = prefix + ((p.n + 4) & ~3);                   // [n] lengths
+  int* trow_s = lens_s + ((p.n + 4) & ~3);                   // [n] block-table rows (bt_rows)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -189,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       if (i < p.n) {
         const int len = p.lens[i];
         lens_s[i] = len;
+        trow_s[i] = p.bt_rows != nullptr ? p.bt_rows[i] : i;
         if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + kTT - 1) / kTT + p.vtiles;
       }
       int v = nt;
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
       continue;
     }
     const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-    for (int o = threadIdx.x; o < p.H * kD; o += blockDim.x) {
+    for (int o = threadIdx.x; orow >= 0 && o < p.H * kD; o += blockDim.x) {
       const int h = o / kD, d = o - h * kD;
       store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
     }
@@ -283,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage, p.vtiles);
     IdPrefetch ids;
     ids.it.init(g0, g1, row0, prefix, nullptr, p.n, Y, kTilesPerStage, p.vtiles);
+    ids.it.trows = trow_s;
     ids.ring = reinterpret_cast<int*>(smem + kOffIds + pw * kIdRingBytes);
     ids.issued = 0;
     const int q_heads = q_owner ? G : 0;
@@ -552,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
         const int h = dn.h0 + g;
         const float val = dn.acc[g] / Lg;
         if (dn.whole) {
-          store_out(p.out, dn.orow * p.out_sn + (int64_t)h * p.out_sh + r, p.out_dtype, val);
+          if (dn.orow >= 0) store_out(p.out, dn.orow * p.out_sn + (int64_t)h * p.out_sh + r, p.out_dtype, val);
           if (r == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)dn.row * p.lse_sn] = lse_nat;
         } else {
           const int64_t pidx = ((int64_t)blockIdx.x * 2 + dn.slot) * G + g;
@@ -716,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
 template <int GM>
 int launch_mma_g(const DecodeParams& q, int dtype, size_t smem, int n, cudaStream_t s) {
   static unsigned long long done_h = 0, done_b = 0;
-  const int budget = mma::kSmemFixed + 2 * mma::kRowsBytes;
+  const int budget = mma::kSmemFixed + 3 * mma::kRowsBytes;
   int st;
   if (dtype == FD_DTYPE_BF16) {
     st = fdh::ensure_smem(reinterpret_cast<const void*>(mma::fd_decode_mma_kernel<__nv_bfloat16, GM>), budget, &done_b);
@@ -741,7 +745,7 @@ int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem
   if (!mma_eligible(dtype, D, p.G, p.BS) || p.gcs != 1 || p.TT != mma::kTT || !p.persistent) return FD_OK;
   for (int t = 0; t < 2; ++t)
     if (p.nblk[t] > 0 && !p.host[t] && !p.use_tmap[t]) return FD_OK;
-  const size_t smem = (size_t)mma::kSmemFixed + 2 * extra_smem;  // prefix + lengths
+  const size_t smem = (size_t)mma::kSmemFixed + 3 * extra_smem;  // prefix, lengths, table rows
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -187,15 +187,22 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
                 block_table: torch.Tensor, lens: torch.Tensor, scale: float, out: torch.Tensor,
                 lse: torch.Tensor | None = None, *, q_rows: torch.Tensor | None = None,
                 out_rows: torch.Tensor | None = None, max_len: int = 0,
-                tiles_per_split: int = 0, n: int | None = None) -> nat.FdDecodeArgs:
+                tiles_per_split: int = 0, n: int | None = None,
+                bt_rows: torch.Tensor | None = None) -> nat.FdDecodeArgs:
     """Validate and pack the arguments of fd_decode_attn (workspace included).
-    The tensors must stay alive, unmoved, while the returned args are used."""
+    The tensors must stay alive, unmoved, while the returned args are used.
+    With bt_rows (int32 [n]) work row i reads table row bt_rows[i]; a
+    negative out_rows[i] writes nothing for row i (a device-built decode
+    list, plan.plan_on_device)."""
     lib = nat.load()
     dev = q.device
     _check(dev.type == "cuda", "q must be a CUDA tensor")
     H, D = q.shape[-2], q.shape[-1]
     _check(q.stride(-1) == 1 and out.stride(-1) == 1, "q and out need a contiguous head dim")
-    n = block_table.shape[0] if n is None else n
+    n = (block_table.shape[0] if bt_rows is None else bt_rows.shape[0]) if n is None else n
+    if bt_rows is not None:
+        _check(bt_rows.dtype == torch.int32 and bt_rows.device == dev and bt_rows.numel() >= n,
+               "bt_rows must be int32 on q's device with n entries")
     _check(block_table.dtype == torch.int32 and lens.dtype == torch.int32, "block_table and lens must be int32")
     _check(block_table.stride(-1) == 1, "block_table rows must be contiguous")
     _check(block_table.device == dev and lens.device == dev, "block_table and lens must be on q's device")
@@ -238,6 +245,7 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
         a.lse = lse.data_ptr()
         a.lse_stride_h = lse.stride(0)
         a.lse_stride_n = lse.stride(1)
+    a.bt_rows = _ptr(bt_rows)
     a.max_len = int(max_len)
     a.tiles_per_split = int(tiles_per_split)
     a.error = error_word(dev).data_ptr()

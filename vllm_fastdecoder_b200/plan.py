@@ -16,6 +16,9 @@ this engine's additions for the single-pass two-tier kernel (the S rows'
 full block-table rows and lengths, and the P requests that are decodes).
 
 All of build_host_plan runs on CPU tensors, so it is testable without a GPU.
+plan_on_device computes the same plan on the GPU from the step's device
+tensors (fd_plan_step, one launch, no host copies); device_plan_to_host
+reads it back for tests and statistics.
 """
 
 from __future__ import annotations
@@ -321,4 +324,166 @@ def to_device(hp: HostPlan, block_table_dev: torch.Tensor, device) -> DevicePlan
         pp_cu=put(hp.pp_cu),
         pp_seqlens=put(hp.pp_seqlens),
         pp_bt=rows(hp.pp_req),
+    )
+
+
+# ------------------------------------------------------------------ on the GPU
+
+
+class DeviceStepPlan:
+    """Device buffers of the plan computed by fd_plan_step (the reference
+    planner, fastdecode/plan.py:103-245, run on the GPU): capacities R
+    requests, T tokens, table width W; the int32 header (device) says how many
+    entries are valid.  Reusable across steps of the same capacities."""
+
+    def __init__(self, R: int, T: int, W: int, device):
+        R, T, W = max(1, int(R)), max(1, int(T)), max(1, int(W))
+        self.R, self.T, self.W = R, T, W
+        self.gw_cap = -(-W // 16) * 16
+
+        def i32(*shape):
+            return torch.zeros(shape, dtype=_I32, device=device)
+
+        def i64(*shape):
+            return torch.zeros(shape, dtype=_I64, device=device)
+
+        self.header = i32(32)
+        self.gpu_slot_mapping, self.cpu_w_tok, self.cpu_w_slot = i64(T), i64(T), i64(T)
+        self.p_tok, self.p_cu, self.p_seqlens, self.p_req = i64(T), i32(R + 1), i32(R), i64(R)
+        self.s_tok, self.s_gpu_bt, self.s_gpu_lens = i64(R), i32(R, self.gw_cap), i32(R)
+        self.s_cpu_bt, self.s_cpu_lens = i32(R, W), i32(R)
+        self.f_tok, self.f_cu = i64(T), i32(R + 1)
+        self.s_req, self.s_seq_lens = i64(R), i32(R)
+        self.pd_req, self.pd_tok, self.pd_seq_lens = i64(R), i64(R), i32(R)
+        self.pp_req, self.pp_tok, self.pp_cu, self.pp_seqlens = i64(R), i64(T), i32(R + 1), i32(R)
+        self.d_tok, self.d_row, self.d_lens = i64(R), i32(R), i32(R)
+        # set by plan_on_device for the step
+        self.num_reqs = 0
+        self.num_gpu_blocks = 0
+        self.block_size = 0
+        self.block_table: torch.Tensor | None = None
+
+    def fits(self, R: int, T: int, W: int) -> bool:
+        return R <= self.R and T <= self.T and W <= self.W
+
+
+@dataclass
+class DeviceDecodeStep:
+    """A decode-only step planned on the GPU, as the backend's attention
+    metadata carries it: the device plan and the host-side sizes the
+    launches need (all known without reading the device)."""
+
+    plan: DeviceStepPlan
+    num_reqs: int
+    n_tok: int
+    max_seq: int
+
+
+def plan_on_device(query_start_loc: torch.Tensor, seq_lens: torch.Tensor, block_table: torch.Tensor,
+                   slot_mapping: torch.Tensor, num_gpu_blocks: int, num_cpu_blocks: int, block_size: int,
+                   out: DeviceStepPlan | None = None, max_tokens: int | None = None) -> DeviceStepPlan:
+    """Launch fd_plan_step on the current stream: the step's plan from its
+    device tensors (query_start_loc [R+1] int32, seq_lens [R] int32,
+    block_table [R, W] int32 with contiguous rows, slot_mapping [>= T] int64),
+    no host synchronisation.  `out` is reused when its capacities fit."""
+    import ctypes
+
+    from vllm_fastdecoder_b200 import _native as nat
+    from vllm_fastdecoder_b200 import gpu_ops
+
+    dev = block_table.device
+    R = int(query_start_loc.numel()) - 1
+    W = int(block_table.shape[1])
+    T = int(slot_mapping.numel()) if max_tokens is None else int(max_tokens)
+    if query_start_loc.dtype != _I32 or seq_lens.dtype != _I32 or block_table.dtype != _I32:
+        raise RuntimeError("plan_on_device: query_start_loc, seq_lens and block_table must be int32")
+    if slot_mapping.dtype != _I64 or int(slot_mapping.numel()) < T:
+        raise RuntimeError("plan_on_device: slot_mapping must be int64 with at least max_tokens entries")
+    if block_table.stride(1) != 1 or int(block_table.shape[0]) < R or int(seq_lens.numel()) < R:
+        raise RuntimeError("plan_on_device: block_table rows must be contiguous and cover every request")
+    if out is None or not out.fits(R, T, W):
+        out = DeviceStepPlan(R, T, W, dev)
+    p = lambda t: t.data_ptr()  # noqa: E731
+    a = nat.FdPlanArgs()
+    a.query_start_loc, a.seq_lens, a.block_table = p(query_start_loc), p(seq_lens), p(block_table)
+    a.bt_stride, a.bt_width, a.num_reqs = block_table.stride(0), W, R
+    a.slot_mapping, a.max_tokens, a.block_size = p(slot_mapping), T, int(block_size)
+    a.num_gpu_blocks, a.num_cpu_blocks = int(num_gpu_blocks), int(num_cpu_blocks)
+    a.header = p(out.header)
+    for name in ("gpu_slot_mapping", "cpu_w_tok", "cpu_w_slot", "p_tok", "p_cu", "p_seqlens", "p_req", "s_tok",
+                 "s_gpu_bt", "s_gpu_lens", "s_cpu_bt", "s_cpu_lens", "f_tok", "f_cu", "s_req", "s_seq_lens",
+                 "pd_req", "pd_tok", "pd_seq_lens", "pp_req", "pp_tok", "pp_cu", "pp_seqlens", "d_tok", "d_row",
+                 "d_lens"):
+        setattr(a, name, p(getattr(out, name)))
+    a.s_gpu_bt_stride, a.s_cpu_bt_stride = out.s_gpu_bt.stride(0), out.s_cpu_bt.stride(0)
+    a.error = gpu_ops.error_word(dev).data_ptr()
+    lib = nat.load()
+    nat.check(lib.fd_plan_step(ctypes.byref(a), gpu_ops._stream(dev)), "fd_plan_step")
+    out.num_reqs, out.num_gpu_blocks, out.block_size, out.block_table = R, int(num_gpu_blocks), int(block_size), \
+        block_table
+    return out
+
+
+def device_plan_to_host(dp: DeviceStepPlan, num_cpu_blocks: int) -> HostPlan | None:
+    """The device plan as a HostPlan (synchronises; for tests and statistics),
+    raising exactly where the reference planner raises."""
+    from vllm_fastdecoder_b200 import _native as nat
+
+    h = dp.header.cpu().tolist()
+    F = nat.PLAN_FIELDS
+    flags = h[F["flags"]]
+    if flags & nat.PLAN_BAD_OFFSETS:
+        raise RuntimeError("FastDecode: query_start_loc is not a 0-based, non-decreasing offset array within "
+                           "the token capacity")
+    if not flags & nat.PLAN_TOUCHES_HOST:
+        return None
+    if flags & nat.PLAN_BAD_BLOCK_ID:
+        raise RuntimeError("FastDecode: block id beyond GPU+CPU capacity; engine and worker disagree on "
+                           "FASTDECODE_CPU_BLOCKS / FASTDECODE_CPU_KV_GB")
+    if flags & nat.PLAN_HOST_EXTEND:
+        raise NotImplementedError(
+            "FastDecode: a request with prior context is being extended by >1 token while part of its KV is on "
+            "the CPU (chunked prefill or prefix-cache hit). Run with enable_prefix_caching=False and "
+            "max_num_batched_tokens >= max_model_len.")
+    n = {k: h[v] for k, v in F.items()}
+
+    def cut(t, k):
+        return t[:k].cpu().contiguous()
+
+    nS = n["n_s"]
+    return HostPlan(
+        n_tok=n["n_tok"],
+        gpu_slot_mapping=cut(dp.gpu_slot_mapping, n["n_tok"]),
+        cpu_w_tok=cut(dp.cpu_w_tok, n["n_cpu_w"]),
+        cpu_w_slot=cut(dp.cpu_w_slot, n["n_cpu_w"]),
+        p_tok=cut(dp.p_tok, n["n_p_tok"]),
+        p_cu=cut(dp.p_cu, n["n_p"] + 1),
+        p_seqlens=cut(dp.p_seqlens, n["n_p"]),
+        p_req=cut(dp.p_req, n["n_p"]),
+        p_max_q=n["p_max_q"],
+        p_max_k=n["p_max_k"],
+        s_tok=cut(dp.s_tok, nS),
+        s_gpu_bt=dp.s_gpu_bt[:nS, :n["s_gpu_width"]].cpu().contiguous(),
+        s_gpu_lens=cut(dp.s_gpu_lens, nS),
+        s_max_gpu_len=n["s_max_gpu_len"],
+        s_cpu_bt=dp.s_cpu_bt[:nS, :n["s_cpu_width"]].cpu().contiguous(),
+        s_cpu_lens=cut(dp.s_cpu_lens, nS),
+        f_tok=cut(dp.f_tok, n["n_f_tok"]),
+        f_cu=cut(dp.f_cu, n["n_f"] + 1),
+        f_max=n["f_max"],
+        s_req=cut(dp.s_req, nS),
+        s_seq_lens=cut(dp.s_seq_lens, nS),
+        s_max_len=n["s_max_len"],
+        pd_req=cut(dp.pd_req, n["n_pd"]),
+        pd_tok=cut(dp.pd_tok, n["n_pd"]),
+        pd_seq_lens=cut(dp.pd_seq_lens, n["n_pd"]),
+        pd_max_len=n["pd_max_len"],
+        pp_req=cut(dp.pp_req, n["n_pp"]),
+        pp_tok=cut(dp.pp_tok, n["n_pp_tok"]),
+        pp_cu=cut(dp.pp_cu, n["n_pp"] + 1),
+        pp_seqlens=cut(dp.pp_seqlens, n["n_pp"]),
+        pp_max_q=n["pp_max_q"],
+        pp_max_k=n["pp_max_k"],
+        num_gpu_blocks=dp.num_gpu_blocks,
+        block_size=dp.block_size,
     )
