@@ -290,19 +290,57 @@ def run_ours(args, ws, rank, device):
     torch.cuda.synchronize(device)
     gpu_ops.check_device_errors(device)
 
+    # the step as one CUDA graph (both launches; the sharded exchange stays
+    # eager), with its own workspace so no later call can move it
+    graph = None
+    if not args.no_graph and gather is None:
+        ws_g = torch.empty(max(256, a.workspace_bytes), dtype=torch.uint8, device=device)
+        a_g = gpu_ops.decode_args(res.q, res.tiers, batch.G, res.block_table, res.lens, batch.scale, out, lse,
+                                  max_len=max_len, tiles_per_split=tps, workspace_buf=ws_g)
+
+        def gstep():
+            gpu_ops.launch_decode(a_g, device, "partials")
+            if has_combine:
+                gpu_ops.launch_decode(a_g, device, "combine")
+
+        gstep()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            gstep()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        gpu_ops.check_device_errors(device)
+
+    # kernel time of the decode launch: eager steps with events around it
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(device)
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize(device)
-    clocks.start()
-    time.sleep(0.25)  # let nvidia-smi take its first sample before the region
+    if graph is None:
+        clocks.start()
+        time.sleep(0.25)  # let nvidia-smi take its first sample before the region
     t_start.record()
     for k in range(args.steps):
         step(evs[k])
     t_end.record()
     torch.cuda.synchronize(device)
+    elapsed_eager = t_start.elapsed_time(t_end) * 1e-3
+    # the timed region of `value`: K graph replays (or the eager steps above)
+    if graph is not None:
+        if dist:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        clocks.start()
+        time.sleep(0.25)
+        t_start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        t_end.record()
+        torch.cuda.synchronize(device)
     clk = clocks.stop()
     if dist:
         torch.distributed.barrier()
@@ -390,7 +428,10 @@ def run_ours(args, ws, rank, device):
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "strong" if args.workload == "c3" else "weak", "vs_baseline": None, "dtype": _dtype_name(batch.dtype),
         "data": "synthetic (seeded N(0,1) q/K/V, configuration shapes)",
-        "config": _config(batch, args, ws, tps, has_combine),
+        "config": dict(_config(batch, args, ws, tps, has_combine), timing=(
+            "value: one CUDA graph of the step (decode + combine launches) replayed K times; roofline: eager "
+            f"steps with CUDA events around the decode launch (eager step {elapsed_eager / args.steps * 1e3:.4f} ms)"
+            if graph is not None else "value and roofline: eager steps, CUDA events")),
         "kv_gbs": round((hbm_b + host_b) * (1 if args.workload == "c3" else ws) * args.steps / elapsed / 1e9, 1),
         "e2e": {"value": round(rows_per_step * args.steps / e2e_t, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -749,6 +790,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3", "c4"], default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time eager launches instead of a captured CUDA graph of the step")
     ap.add_argument("--ctx", type=int, default=131072,
                     help="c3 context length per row (a smaller one for profiling captures)")
     ap.add_argument("--layout", choices=["nhd", "hnd"], default=None,

@@ -188,12 +188,15 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
                 lse: torch.Tensor | None = None, *, q_rows: torch.Tensor | None = None,
                 out_rows: torch.Tensor | None = None, max_len: int = 0,
                 tiles_per_split: int = 0, n: int | None = None,
-                bt_rows: torch.Tensor | None = None) -> nat.FdDecodeArgs:
+                bt_rows: torch.Tensor | None = None,
+                workspace_buf: torch.Tensor | None = None) -> nat.FdDecodeArgs:
     """Validate and pack the arguments of fd_decode_attn (workspace included).
     The tensors must stay alive, unmoved, while the returned args are used.
     With bt_rows (int32 [n]) work row i reads table row bt_rows[i]; a
     negative out_rows[i] writes nothing for row i (a device-built decode
-    list, plan.plan_on_device)."""
+    list, plan.plan_on_device).  workspace_buf (uint8, on q's device) replaces
+    the shared grow-only workspace, e.g. for launches captured in a CUDA graph,
+    whose pointers must stay valid for the graph's lifetime."""
     lib = nat.load()
     dev = q.device
     _check(dev.type == "cuda", "q must be a CUDA tensor")
@@ -251,7 +254,12 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
     a.error = error_word(dev).data_ptr()
     need = lib.fd_decode_workspace_size(ctypes.byref(a))
     if need:
-        ws = workspace(dev, need)
+        if workspace_buf is not None:
+            _check(workspace_buf.device == dev and workspace_buf.dtype == torch.uint8 and workspace_buf.numel() >= need,
+                   f"workspace_buf must be uint8 on q's device with >= {need} bytes")
+            ws = workspace_buf
+        else:
+            ws = workspace(dev, need)
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
     return a
