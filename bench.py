@@ -261,7 +261,8 @@ def run_ours(args, ws, rank, device):
     if sharded:
         from vllm_fastdecoder_b200 import sharded as sh
 
-        gather = sh.PartialExchange(n, H, D, ws, device)
+        gather = (sh.PeerExchange(n, H, D, ws, device) if args.exchange == "peer"
+                  else sh.PartialExchange(n, H, D, ws, device))
         final = torch.empty(n, H, D, dtype=batch.dtype, device=device)
         out, lse = gather.o_view, gather.lse_view
     else:
@@ -448,6 +449,12 @@ def run_ours(args, ws, rank, device):
             "sample": _sample_text(batch, r),
             "cpu": _cpu_model(),
         }
+    if gather is not None:
+        line["config"]["exchange"] = ("peer memory: one fd_exchange_merge launch per step (CUDA IPC buffers, "
+                                      "NVLink stores)" if args.exchange == "peer"
+                                      else "NCCL all_gather_into_tensor + fd_merge_partials")
+        if hasattr(gather, "close"):
+            gather.close()  # collective: every rank reaches it
     return line
 
 
@@ -790,6 +797,9 @@ def main() -> int:
     ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3", "c4"], default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
+                    help="c3 on N > 1 GPUs: partials exchanged over peer memory in one kernel (fd_exchange_merge) "
+                         "or with an NCCL all-gather and a merge kernel")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of a captured CUDA graph of the step")
     ap.add_argument("--ctx", type=int, default=131072,

@@ -337,6 +337,44 @@ FD_API int fd_plan_step(const fd_plan_args *a, void *stream);
 /* sizeof(fd_plan_args) as compiled into the library (binding check). */
 FD_API size_t fd_plan_args_bytes(void);
 
+/* ------------------------------------------------------- peer exchange */
+
+/* The sharded long-context path (no reference counterpart: the reference
+ * has no multi-GPU path) exchanges each rank's fp32 partial over peer
+ * memory instead of an NCCL all-gather: fd_exchange_merge pushes the
+ * rank's packed [o (n*H*D) | lse (H*n)] into every rank's receive buffer
+ * over NVLink, waits (bounded) for every rank's, and merges with the rule
+ * of fd_merge_partials, in one launch per step.  Buffers are plain device
+ * memory shared with CUDA IPC (no multicast object). */
+#define FD_MAX_PEERS 8
+#define FD_IPC_HANDLE_BYTES 64
+
+typedef struct fd_peer_exchange {
+  void *base[FD_MAX_PEERS]; /* rank q's allocation as mapped in this process:
+                               the own one from fd_peer_alloc, the others
+                               from fd_peer_open */
+  int32_t rank;
+  int32_t world;
+  int64_t slot_floats;      /* floats per rank slot: >= n*H*D + H*n, multiple of 4 */
+} fd_peer_exchange;
+
+/* Bytes of one rank's allocation (counters + 2 x world slots). */
+FD_API size_t fd_peer_buffer_bytes(int32_t world, int64_t slot_floats);
+/* cudaMalloc + zero + IPC handle (FD_IPC_HANDLE_BYTES written to ipc_handle). */
+FD_API int fd_peer_alloc(size_t bytes, void **ptr, void *ipc_handle);
+/* Map another rank's allocation (cudaIpcOpenMemHandle) / unmap it. */
+FD_API int fd_peer_open(const void *ipc_handle, void **ptr);
+FD_API int fd_peer_close(void *ptr);
+FD_API int fd_peer_free(void *ptr);
+/* One step: every rank calls it once per step, in the same order, with the
+ * same n / heads / head size / num_ctas (0: 32, at most 64).  send: this rank's packed
+ * partial (16-byte aligned); out [n, H, D] in out_dtype; out_lse [H, n] or
+ * NULL.  A wait longer than timeout_ns (0: 2 s) records FD_DEVERR_TIMEOUT
+ * in *error and returns; the exchange must then be rebuilt. */
+FD_API int fd_exchange_merge(const fd_peer_exchange *x, const float *send, int32_t n, int32_t num_heads,
+                             int32_t head_size, void *out, int32_t out_dtype, float *out_lse, int32_t num_ctas,
+                             int64_t timeout_ns, int32_t *error, void *stream);
+
 /* Two-way log-sum-exp merge, the rule of vLLM merge_attn_states as restated
  * in fastdecode/cpu_ops.py:93-113 and called at fastdecode/backend.py:54-55,
  * 354-356: an lse of +inf (FlashAttention's empty row) counts as -inf, and a

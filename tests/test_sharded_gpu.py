@@ -1,8 +1,11 @@
-"""KV-sharded decode on 2 GPUs over NCCL: each rank decodes its contiguous
-shard of every row with the split-KV kernel into the packed exchange buffer,
-the partials are all-gathered and merged with fd_merge_partials; the result
-must match the oracle over the unsharded rows (tolerances of the decode
-tests: bf16 output 1.6e-2, lse 1e-4).  Skipped with fewer than 2 GPUs."""
+"""KV-sharded decode on 2 GPUs: each rank decodes its contiguous shard of
+every row with the split-KV kernel into the packed exchange buffer; the
+partials are exchanged and merged either with NCCL (all-gather, then
+fd_merge_partials) or over peer memory (fd_exchange_merge: one kernel,
+CUDA-IPC buffers, no multicast).  Both must match the oracle over the
+unsharded rows (bf16 output 1.6e-2, lse 1e-4) and each other bit for bit,
+over three consecutive steps (both parities of the peer buffers).  NVLS is
+off.  Skipped with fewer than 2 GPUs."""
 
 from __future__ import annotations
 
@@ -56,14 +59,23 @@ def _rank(rank, world, port, path):
         n, H, D = q.shape
         BS = kc.shape[2]
         lbt, llens = sharded.shard_rows(bt, lens, BS, world, rank)
-        ex = sharded.PartialExchange(n, H, D, world, dev)
-        final = torch.empty(n, H, D, dtype=q.dtype, device=dev)
-        sharded.sharded_decode(q.to(dev), (KVTier(kc.to(dev), vc.to(dev)), None), 1 << 40, lbt.to(dev),
-                               llens.to(dev), 1.0 / math.sqrt(D), ex, final)
-        torch.cuda.synchronize(dev)
-        gpu_ops.check_device_errors(dev)
+        tiers = (KVTier(kc.to(dev), vc.to(dev)), None)
+        res = {}
+        for name, ex in (("nccl", sharded.PartialExchange(n, H, D, world, dev)),
+                         ("peer", sharded.PeerExchange(n, H, D, world, dev))):
+            outs = []
+            for _ in range(3):
+                final = torch.full((n, H, D), float("nan"), dtype=q.dtype, device=dev)
+                sharded.sharded_decode(q.to(dev), tiers, 1 << 40, lbt.to(dev), llens.to(dev), 1.0 / math.sqrt(D),
+                                       ex, final)
+                torch.cuda.synchronize(dev)
+                gpu_ops.check_device_errors(dev)
+                outs.append((final.cpu(), ex.lse_out.cpu()))
+            res[name] = outs
+            if isinstance(ex, sharded.PeerExchange):
+                ex.close()
         if rank == 0:
-            torch.save({"out": final.cpu(), "lse": ex.lse_out.cpu()}, path)
+            torch.save(res, path)
     finally:
         dist.destroy_process_group()
 
@@ -78,6 +90,10 @@ def test_sharded_decode_two_gpus(tmp_path):
     D = q.shape[2]
     ref_o, ref_l = O.ref_decode_attn_f64(q, kc, vc, bt, lens, 1.0 / math.sqrt(D))
     nz = lens > 0
-    torch.testing.assert_close(res["out"][nz].double(), ref_o[nz], atol=1.6e-2, rtol=1.6e-2)
-    torch.testing.assert_close(res["lse"][:, nz].double(), ref_l[:, nz], atol=1e-4, rtol=1e-5)
-    assert torch.all(res["out"][~nz] == 0) and torch.all(torch.isneginf(res["lse"][:, ~nz]))
+    for k in range(3):
+        for name in ("nccl", "peer"):
+            out, lse = res[name][k]
+            torch.testing.assert_close(out[nz].double(), ref_o[nz], atol=1.6e-2, rtol=1.6e-2)
+            torch.testing.assert_close(lse[:, nz].double(), ref_l[:, nz], atol=1e-4, rtol=1e-5)
+            assert torch.all(out[~nz] == 0) and torch.all(torch.isneginf(lse[:, ~nz]))
+        assert torch.equal(res["nccl"][k][0], res["peer"][k][0]) and torch.equal(res["nccl"][k][1], res["peer"][k][1])

@@ -84,6 +84,14 @@ class FdPlanArgs(ctypes.Structure):
     ]
 
 
+MAX_PEERS = 8  # FD_MAX_PEERS
+IPC_HANDLE_BYTES = 64  # FD_IPC_HANDLE_BYTES
+
+
+class FdPeerExchange(ctypes.Structure):
+    _fields_ = [("base", c_void_p * MAX_PEERS), ("rank", c_int32), ("world", c_int32), ("slot_floats", c_int64)]
+
+
 # name -> (restype, argtypes); mirrors include/fastdecode_b200.h
 SIGNATURES = {
     "fd_decode_workspace_size": (c_size_t, [POINTER(FdDecodeArgs)]),
@@ -113,6 +121,14 @@ SIGNATURES = {
     "fd_host_register": (c_int32, [c_void_p, c_size_t]),
     "fd_host_unregister": (c_int32, [c_void_p]),
     "fd_plan_step": (c_int32, [POINTER(FdPlanArgs), c_void_p]),
+    "fd_peer_buffer_bytes": (c_size_t, [c_int32, c_int64]),
+    "fd_peer_alloc": (c_int32, [c_size_t, POINTER(c_void_p), c_void_p]),
+    "fd_peer_open": (c_int32, [c_void_p, POINTER(c_void_p)]),
+    "fd_peer_close": (c_int32, [c_void_p]),
+    "fd_peer_free": (c_int32, [c_void_p]),
+    "fd_exchange_merge": (c_int32, [
+        POINTER(FdPeerExchange), c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_int32,
+        c_int64, c_void_p, c_void_p]),
     "fd_plan_args_bytes": (c_size_t, []),
     "fd_version": (c_int32, []),
     "fd_abi_sizes": (c_int32, [POINTER(c_size_t), POINTER(c_size_t)]),

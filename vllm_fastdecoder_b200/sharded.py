@@ -8,6 +8,11 @@ of all ranks are all-gathered with NCCL over NVLink, and every rank merges the
 reference's two-tier rule (fastdecode/cpu_ops.py:93-113) applied to P parts;
 the reference itself has no multi-GPU path.
 
+Two exchanges with the same interface: PartialExchange (NCCL all-gather,
+then the merge kernel) and PeerExchange (fd_exchange_merge: one kernel per
+step pushes the partial into every rank's buffer over NVLink, waits for
+every rank's and merges; buffers shared with CUDA IPC, no multicast).
+
 One process per GPU (torchrun); the process group is the caller's.
 """
 
@@ -85,6 +90,85 @@ class PartialExchange:
         del o_local_unused, lse_local_unused
         self.gather()
         self.merge_fn(self.recv, self.world, self.n, self.H, self.D, final, self.lse_out)
+
+
+class PeerExchange:
+    """The exchange and merge over peer memory (C ABI fd_exchange_merge):
+    o_view / lse_view are views of the packed send buffer the decode kernel
+    writes; exchange_and_merge(final) runs one launch that needs every rank
+    to call it for the same step.  Build it collectively (every rank of the
+    group) after torch.cuda.set_device; close() collectively too."""
+
+    def __init__(self, n: int, H: int, D: int, world: int, device: torch.device, group=None, num_ctas: int = 32,
+                 timeout_s: float = 2.0):
+        import ctypes
+
+        from vllm_fastdecoder_b200 import _native as nat
+
+        self._nat, self._lib = nat, nat.load()
+        self.n, self.H, self.D, self.world = n, H, D, world
+        self.group, self.device = group, device
+        self.rank = dist.get_rank(group) if world > 1 else 0
+        self.num_ctas, self.timeout_ns = int(num_ctas), int(timeout_s * 1e9)
+        self.slot = (n * H * D + H * n + 3) // 4 * 4
+        self.send = torch.zeros(self.slot, dtype=torch.float32, device=device)
+        self.o_view = self.send[: n * H * D].view(n, H, D)
+        self.lse_view = self.send[n * H * D: n * H * D + H * n].view(H, n)
+        self.lse_out = torch.empty(H, n, dtype=torch.float32, device=device)
+        lib = self._lib
+        nbytes = lib.fd_peer_buffer_bytes(world, self.slot)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * nat.IPC_HANDLE_BYTES)()
+        nat.check(lib.fd_peer_alloc(nbytes, ctypes.byref(own), handle), "fd_peer_alloc")
+        self._own, self._opened = own.value, []
+        handles = [bytes(handle)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        x = nat.FdPeerExchange()
+        x.rank, x.world, x.slot_floats = self.rank, world, self.slot
+        for q in range(world):
+            if q == self.rank:
+                x.base[q] = self._own
+                continue
+            p = ctypes.c_void_p()
+            buf = ctypes.create_string_buffer(handles[q], nat.IPC_HANDLE_BYTES)
+            nat.check(lib.fd_peer_open(buf, ctypes.byref(p)), "fd_peer_open")
+            x.base[q] = p.value
+            self._opened.append(p.value)
+        self.x = x
+        if world > 1:
+            dist.barrier(group=group)  # every rank mapped before the first step
+
+    def gather(self) -> None:
+        raise NotImplementedError("PeerExchange exchanges and merges in one launch: use exchange_and_merge")
+
+    def exchange_and_merge(self, o_local_unused, lse_local_unused, final: torch.Tensor) -> None:
+        import ctypes
+
+        from vllm_fastdecoder_b200 import gpu_ops
+
+        del o_local_unused, lse_local_unused
+        nat = self._nat
+        if not (final.is_contiguous() and tuple(final.shape) == (self.n, self.H, self.D)):
+            raise RuntimeError("PeerExchange: final must be a contiguous [n, H, D] tensor")
+        nat.check(self._lib.fd_exchange_merge(
+            ctypes.byref(self.x), self.send.data_ptr(), self.n, self.H, self.D, final.data_ptr(),
+            gpu_ops.dtype_code(final.dtype), self.lse_out.data_ptr(), self.num_ctas, self.timeout_ns,
+            gpu_ops.error_word(self.device).data_ptr(), gpu_ops._stream(self.device)), "fd_exchange_merge")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            self._lib.fd_peer_close(p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        self._lib.fd_peer_free(self._own)
+        self._own = None
 
 
 def sharded_decode(q: torch.Tensor, tiers, tier_split: int, local_bt: torch.Tensor, local_lens: torch.Tensor,
