@@ -4,20 +4,24 @@
 //
 // Each rank owns one device allocation, mapped into every other rank's
 // process with CUDA IPC (plain device memory: no multicast object, no NVLS):
-//   [0]   arrival counter   u64, incremented by every CTA of every rank once
-//                            per step (red.release.sys)
+//   [0]   arrival counter   u64, incremented once per step by every rank
+//                            (red.release.sys)
 //   [8]   step counter      u64, this rank's completed steps
 //   [16]  CTA counter       u64, this rank's finished CTAs
+//   [24]  push counter      u64, this rank's CTAs done pushing
 //   [256] receive buffer    fp32 [2 parities][world][slot], slot = the packed
 //                            partial [o (n*H*D) | lse (H*n)] rounded to 4
 // One launch per step of at most 32 small CTAs, which the SMs hold at once
 // (every wait is bounded in any case):
 //   1. every CTA stores its share of the rank's packed partial into slot
 //      [parity][rank] of every rank's receive buffer (16-byte stores over
-//      NVLink; the own copy is local), fences at system scope, then adds 1
-//      to every rank's arrival counter;
+//      NVLink; the own copy is local), fences at system scope and counts
+//      itself on the rank's push counter; the last CTA of the rank fences
+//      again and adds 1 to every rank's arrival counter (world remote
+//      atomics per rank and step: one signal per CTA and rank made 256
+//      contending atomics per counter at 8 ranks, slower than NCCL);
 //   2. it waits (bounded, %globaltimer) until its own counter reaches
-//      step * world * CTAs: every share of every rank has landed;
+//      step * world: every rank's slot has landed;
 //   3. it merges its (row, head) pairs from the receive buffer with the
 //      log-sum-exp rule of fd_merge_partials, same operations in the same
 //      order (so the result equals the NCCL path bit for bit);
@@ -42,6 +46,7 @@ struct ExchangeParams {
   unsigned long long* arrive[FD_MAX_PEERS];  // rank q's arrival counter (mapped)
   unsigned long long* step;               // this rank's step counter
   unsigned long long* done;               // this rank's finished-CTA counter
+  unsigned long long* pushed;             // this rank's CTAs done pushing
   int rank, world, n, H, D;
   int64_t slot;                           // floats per rank slot (multiple of 4)
   void* out;
@@ -84,11 +89,16 @@ __global__ void fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams 
   }
   __syncthreads();  // the CTA's stores happen before thread 0's fence and release
 
-  // 2. announce, then wait for every CTA of every rank
+  // 2. the rank's last CTA to finish pushing announces the rank to every
+  // rank; then every CTA waits for every rank
   if (threadIdx.x == 0) {
     __threadfence_system();
-    for (int q = 0; q < p.world; ++q) red_add_release_sys(p.arrive[q], 1ull);
-    const unsigned long long want = step * (unsigned long long)p.world * gridDim.x;
+    const unsigned long long prev = atomicAdd(p.pushed, 1ull);
+    if (prev + 1 == step * gridDim.x) {
+      __threadfence_system();  // the other CTAs' fenced stores happen before the signal
+      for (int q = 0; q < p.world; ++q) red_add_release_sys(p.arrive[q], 1ull);
+    }
+    const unsigned long long want = step * (unsigned long long)p.world;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1; ld_acquire_sys(p.arrive[p.rank]) < want; ++it) {
       if ((it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
@@ -234,6 +244,7 @@ extern "C" int fd_exchange_merge(const fd_peer_exchange* x, const float* send, i
   unsigned char* own = static_cast<unsigned char*>(x->base[x->rank]);
   p.step = reinterpret_cast<unsigned long long*>(own + 8);
   p.done = reinterpret_cast<unsigned long long*>(own + 16);
+  p.pushed = reinterpret_cast<unsigned long long*>(own + 24);
   p.rank = x->rank;
   p.world = x->world;
   p.n = n;
