@@ -139,7 +139,12 @@ _LOCK = threading.Lock()
 
 
 def lib_path() -> Path:
-    return library_path()
+    """The library to load: FASTDECODE_B200_LIB if set (e.g. a build with
+    other compile-time options), else the in-tree build."""
+    import os
+
+    env = os.environ.get("FASTDECODE_B200_LIB")
+    return Path(env) if env else library_path()
 
 
 def load() -> ctypes.CDLL:

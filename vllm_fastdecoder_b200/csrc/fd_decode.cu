@@ -817,12 +817,12 @@ int geometry(const fd_decode_args* a, Geometry* g) {
   // round trip, the epilogue, and a last stage that is on average half
   // empty).  Measured on B200 (lognormal lengths for the tensor-core kernel,
   // uniform ones for the CUDA-core kernel), the balance is best at a weight
-  // of 12 tiles per segment for the tensor-core kernel (8-tile stages) and
-  // 5 for the CUDA-core kernel (4-tile stages); FASTDECODE_B200_VTILES
-  // overrides it.
+  // of 16 tiles per segment for the tensor-core kernel (8-tile stages, four
+  // producer warps) and 5 for the CUDA-core kernel (4-tile stages);
+  // FASTDECODE_B200_VTILES overrides it.
   g->vtiles = 0;
   if (g->persistent) {
-    g->vtiles = g->mma ? 12 : 5;
+    g->vtiles = g->mma ? 16 : 5;
     const char* vt_env = getenv("FASTDECODE_B200_VTILES");
     if (vt_env != nullptr && vt_env[0] >= '0' && vt_env[0] <= '9') g->vtiles = std::min(atoi(vt_env), 64);
   }

@@ -4,11 +4,13 @@
 // decode attention are small matrix products per 128-token stage:
 //   S^T [128 tokens x 8] = K [128 x 128] . q^T [128 x 8]       (q.K^T)
 //   O^T [128 dims  x 8] = V^T [128 x 128] . P^T [128 x 8]      (P.V)
-// (the group padded to the MMA's N = 16).  One CTA per SM, seven warps:
-//   warps 4, 6  TMA producers: K and V tiles (16 tokens, one kv head) into
+// (the group padded to the MMA's N = 16).  One CTA per SM, nine warps:
+//   warps 4, 6-8  TMA producers: K and V tiles (16 tokens, one kv head) into
 //            a 3-stage ring in the 128-byte-swizzled layout the MMA reads
-//            (tiled TMA, box {64 dims, 1, 16, 1}), four tiles of a stage
-//            each; host-tier tiles by 16-byte loads stored with the same
+//            (tiled TMA, box {64 dims, 1, 16, 1}), two tiles of a stage
+//            each (a warp issues its TMA boxes one after another, ~45 ns
+//            apiece, so the 32 boxes of a 64 KB stage are spread over four
+//            warps); host-tier tiles by 16-byte loads stored with the same
 //            swizzle; warp 4 also stages q of each piece.  Block ids are
 //            fetched six stages ahead (cp.async ring).
 //   warp 5   MMA issuer: one thread polls the barriers and issues
@@ -39,6 +41,10 @@
 #include "fd_decode.cuh"
 #include "fd_internal.h"
 
+#ifndef FD_MMA_PRODUCERS
+#define FD_MMA_PRODUCERS 4  // producer warps of the tcgen05 kernel
+#endif
+
 namespace fdk {
 namespace mma {
 
@@ -51,10 +57,10 @@ constexpr int kNST = 3;             // stages in the ring
 constexpr int kPanel = kTok * 128;  // 128 token rows x 128 B (64 dims)
 constexpr int kKV = 2 * kPanel;     // K or V of one stage (32 KB)
 constexpr int kStage = 2 * kKV;     // K + V (64 KB)
-static_assert(kTilesPerStage % 2 == 0, "tiles split between two producer warps");
+static_assert(kTilesPerStage % FD_MMA_PRODUCERS == 0, "tiles split evenly between the producer warps");
 constexpr int kQB = 2 * kN * 128;   // q: two panels of 16 rows x 128 B
 constexpr int kPB = 2 * kN * 128;   // P: two panels (tokens 0-63, 64-127) x 16 rows
-constexpr int kProd = 2;                         // producer warps (4 and 6), 4 tiles of a stage each
+constexpr int kProd = FD_MMA_PRODUCERS;          // producer warps (4, then 6, 7, ...), kTilesPerProd tiles each
 constexpr int kTilesPerProd = kTilesPerStage / kProd;
 constexpr int kThreads = (4 + 1 + kProd) * 32;
 constexpr int kTmemCols = 4 * kN;  // S0 S1 O0 O1, kN columns each
@@ -273,13 +279,14 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
 
   if (warp == 4 || warp >= 6) {
     // ------------------------------------------------------------ producers
-    // Warp 4 fills tiles 0-3 of every stage, warp 6 tiles 4-7: one warp
-    // issues its TMA boxes one after another (~45 ns each), so two warps
-    // halve a stage's issue time.  Block ids come kIdAhead stages ahead
+    // Producer pw (warp 4, then warps 6, 7, ...) fills tiles
+    // [pw * kTilesPerProd, (pw + 1) * kTilesPerProd) of every stage: one
+    // warp issues its TMA boxes one after another (~45 ns each), so the
+    // warps share a stage's issue time.  Block ids come kIdAhead stages ahead
     // through a cp.async ring per warp (q of the coming pieces is prefetched
     // into L2 there); warp 4 also loads q into registers one stage ahead of
     // its piece and stores it for the MMA.
-    const int pw = warp == 4 ? 0 : 1;
+    const int pw = warp == 4 ? 0 : warp - 5;
     const bool q_owner = pw == 0;
     const uint64_t pol = l2_evict_first_policy();
     StageIter it;
