@@ -253,6 +253,43 @@ def test_decode_bad_block_id_sets_error(ops):
     ops.check_device_errors(dev)  # cleared
 
 
+@pytest.mark.parametrize("H,KVH", [(8, 8), (16, 4)])
+def test_staged_host_tier_equals_mapped(ops, H, KVH):
+    """The host tier staged into device memory by the copy engine
+    (host_range) gives the same result as reading it in place: same kernel,
+    same data (CUDA-core kernel for MHA, tcgen05 kernel for the group of 4)."""
+    from vllm_fastdecoder_b200.gpu_ops import KVTier
+
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(H)
+    D, BS, G, C, n = 128, 16, 30, 50, 7
+    dt = torch.bfloat16
+    hk = torch.randn(G, KVH, BS, D, generator=g).to(dt).to(dev)
+    hv = torch.randn(G, KVH, BS, D, generator=g).to(dt).to(dev)
+    ck = torch.randn(C, KVH, BS, D, generator=g).to(dt).pin_memory()
+    cv = torch.randn(C, KVH, BS, D, generator=g).to(dt).pin_memory()
+    lens = torch.tensor([1, 90, 0, 300, 17, 64, 200], dtype=torch.int32)
+    W = 20
+    bt = torch.zeros(n, W, dtype=torch.int32)
+    ids = torch.randperm(G - 1, generator=g).tolist()
+    host = (torch.randperm(C - 10, generator=g) + 5).tolist()  # host ids 5..44: the range starts above 0
+    for i in range(n):
+        nb = (int(lens[i]) + BS - 1) // BS
+        for j in range(nb):
+            bt[i, j] = (host.pop() + G) if j % 3 else ids.pop()
+    q = torch.randn(n, H, D, generator=g).to(dt).to(dev)
+    tiers = (KVTier(hk, hv), KVTier(ck, cv))
+    outs = []
+    for hr in (None, ops.host_block_range(bt, lens, BS, G)):
+        out = torch.full((n, H, D), float("nan"), dtype=dt, device=dev)
+        lse = torch.empty(H, n, dtype=torch.float32, device=dev)
+        ops.decode_tiered(q, tiers, G, bt.to(dev), lens.to(dev), D ** -0.5, out, lse, host_range=hr)
+        ops.check_device_errors(dev)
+        outs.append((out.cpu(), lse.cpu()))
+    assert ops.host_block_range(bt, lens, BS, G)[0] >= 5
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
 @pytest.mark.parametrize("vtiles", ["0", "1", "12", "40"])
 @pytest.mark.parametrize("H,KVH,mma", [(8, 2, "1"), (8, 2, "0"), (8, 8, "1")])
 def test_decode_weighted_schedule(ops, monkeypatch, vtiles, H, KVH, mma):

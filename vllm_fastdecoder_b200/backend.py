@@ -334,8 +334,13 @@ class FastDecodeImpl(FlashAttentionImpl):
             if config.two_pass():
                 self._split_two_pass(query, tiers, G, dp, output)
             else:
+                # a dense range of host blocks is staged into HBM by the copy
+                # engine (faster than SM loads over PCIe), a sparse one read in place
+                span = hp.host_hi - hp.host_lo
+                hr = ((hp.host_lo, hp.host_hi)
+                      if config.stage_host() and span > 0 and hp.host_used >= 0.6 * span else None)
                 OPS.decode(query, tiers, G, dp.s_bt, dp.s_seq_lens, self.scale, output,
-                           q_rows=dp.s_tok, out_rows=dp.s_tok, max_len=hp.s_max_len)
+                           q_rows=dp.s_tok, out_rows=dp.s_tok, max_len=hp.s_max_len, host_range=hr)
 
         # 3) all-HBM decodes
         if hp.pd_req.numel():

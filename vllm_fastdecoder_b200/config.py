@@ -21,6 +21,9 @@ ENV_STATS = "FASTDECODE_STATS"
 ENV_TWO_PASS = "FASTDECODE_B200_TWO_PASS"
 # decode-only steps are planned on the GPU (fd_plan_step) unless set to 0
 ENV_DEVICE_PLAN = "FASTDECODE_B200_DEVICE_PLAN"
+# host-planned steps copy their host-tier blocks to HBM with the copy engine
+# (when the range they span is dense) unless set to 0
+ENV_STAGE_HOST = "FASTDECODE_B200_STAGE_HOST"
 
 
 def enabled() -> bool:
@@ -37,6 +40,10 @@ def stats_enabled() -> bool:
 
 def two_pass() -> bool:
     return _flag(ENV_TWO_PASS)
+
+
+def stage_host() -> bool:
+    return os.environ.get(ENV_STAGE_HOST, "1") not in ("", "0", "false", "False")
 
 
 def device_plan() -> bool:

@@ -156,6 +156,52 @@ def _tier_device(t: KVTier | None) -> torch.device | None:
     return t.k.device
 
 
+# ------------------------------------------------------------- host-tier staging
+
+_STAGE: dict[int, torch.Tensor] = {}
+
+
+def stage_host_blocks(tier: KVTier, lo: int, hi: int, device: torch.device) -> KVTier:
+    """Copy host-tier blocks [lo, hi) into device memory with the copy engine
+    (two cudaMemcpyAsync on the current stream: K, then V) and return the
+    device tier over the copy.  The copy engine reads pinned memory faster
+    than SM loads over PCIe (B200: 55.6 vs ~51 GB/s), so a step that reads
+    most of a compact range of host blocks gains by staging it; decode with
+    tier_split + lo as the split so that host id h maps to staged block
+    h - lo.  The staging buffer is shared and grow-only (per device): it
+    is overwritten by the next staging call on the same device."""
+    _check(tier.host, "stage_host_blocks: the tier must be the pinned host tier")
+    _check(0 <= lo <= hi <= tier.k.shape[0], f"stage_host_blocks: range [{lo}, {hi}) outside the tier")
+    _check(tier.k.is_contiguous() and tier.v.is_contiguous(), "stage_host_blocks: host tier must be contiguous")
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    per = tier.k[0].numel()
+    need = 2 * max(1, hi - lo) * per
+    buf = _STAGE.get(idx)
+    if buf is None or buf.numel() < need or buf.dtype != tier.k.dtype:
+        buf = torch.empty(need, dtype=tier.k.dtype, device=torch.device("cuda", idx))
+        _STAGE[idx] = buf
+    shape = (max(1, hi - lo),) + tuple(tier.k.shape[1:])
+    k = buf[: need // 2].view(shape)
+    v = buf[need // 2: need].view(shape)
+    if hi > lo:
+        k[: hi - lo].copy_(tier.k[lo:hi], non_blocking=True)
+        v[: hi - lo].copy_(tier.v[lo:hi], non_blocking=True)
+    return KVTier(k[: max(1, hi - lo)], v[: max(1, hi - lo)])
+
+
+def host_block_range(block_table: torch.Tensor, lens: torch.Tensor, block_size: int, tier_split: int) -> tuple[int, int]:
+    """[lo, hi) of the host-tier blocks (ids >= tier_split, host-relative)
+    a step reads, from CPU copies of its block table and lengths."""
+    W = block_table.shape[1]
+    nb = ((lens.to(torch.int64) + block_size - 1) // block_size).clamp(max=W)
+    used = torch.arange(W).unsqueeze(0) < nb.unsqueeze(1)
+    ids = block_table.to(torch.int64)[used]
+    ids = ids[ids >= tier_split]
+    if ids.numel() == 0:
+        return 0, 0
+    return int(ids.min()) - tier_split, int(ids.max()) - tier_split + 1
+
+
 # ------------------------------------------------------------- decode
 
 
@@ -283,7 +329,15 @@ def decode_tiered(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], t
     tiers (ids < tier_split and >= tier_split), block_table [n, W] int32,
     lens [n] int32, out [*, H, D] (rows out_rows[i] or i; q dtype or fp32),
     lse [H, n] fp32 or None.  Keywords: q_rows, out_rows, max_len,
-    tiles_per_split, n (see decode_args)."""
+    tiles_per_split, n (see decode_args), and host_range = (lo, hi): stage
+    host-tier blocks [lo, hi) (every host block the step reads) into device
+    memory with the copy engine first (stage_host_blocks) and decode from
+    there."""
+    host_range = kw.pop("host_range", None)
+    if host_range is not None and tiers[1] is not None and tiers[1].host:
+        lo, hi = host_range
+        tiers = (tiers[0], stage_host_blocks(tiers[1], lo, hi, q.device))
+        tier_split = tier_split + lo
     a = decode_args(q, tiers, tier_split, block_table, lens, scale, out, lse, **kw)
     launch_decode(a, q.device)
 

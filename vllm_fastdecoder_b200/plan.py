@@ -72,6 +72,11 @@ class HostPlan:
     pp_max_k: int = 0
     num_gpu_blocks: int = 0
     block_size: int = 0
+    # host-relative range [host_lo, host_hi) of the host blocks the step
+    # reads, and how many of them it reads (for staging them in one copy)
+    host_lo: int = 0
+    host_hi: int = 0
+    host_used: int = 0
 
     @property
     def n_s(self) -> int:
@@ -159,7 +164,8 @@ def build_host_plan(
     if not bool(touches_host.any()) and not bool(host_slot.any()):
         return None
 
-    if bool(host_blk.any()) and int(ids[host_blk].max()) >= G + num_cpu_blocks:
+    host_ids = ids[host_blk]
+    if host_ids.numel() and int(host_ids.max()) >= G + num_cpu_blocks:
         raise RuntimeError(
             "FastDecode: block id beyond GPU+CPU capacity; engine and worker "
             "disagree on FASTDECODE_CPU_BLOCKS / FASTDECODE_CPU_KV_GB"
@@ -240,6 +246,9 @@ def build_host_plan(
         pp_max_k=int(pp_seq.max()) if pp_seq.numel() else 0,
         num_gpu_blocks=G,
         block_size=bs,
+        host_lo=int(host_ids.min()) - G if host_ids.numel() else 0,
+        host_hi=int(host_ids.max()) - G + 1 if host_ids.numel() else 0,
+        host_used=int(host_ids.numel()),
     )
 
 
