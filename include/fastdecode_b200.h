@@ -145,7 +145,9 @@ typedef struct fd_decode_args {
   /* optional: row i reads block-table row bt_rows[i] (else row i), so a
    * device-built list of work rows (fd_plan_step) runs on the batch's own
    * table without gathering it (replaces the index_select of table rows in
-   * fastdecode/plan.py:224-245) */
+   * fastdecode/plan.py:224-245).  Like q_rows and out_rows, its entries must
+   * address rows of their tensors: row indices are the caller's contract
+   * and are not range-checked (block ids and lengths are). */
   const int32_t *bt_rows;
 } fd_decode_args;
 
