@@ -4,9 +4,10 @@
 // Grid: x = split of the row's token range, y = (kv head, query-head chunk),
 // z = row.  Each CTA streams its split's K/V tiles (tile = min(block_size,16)
 // tokens of one block and one kv head) through an NST-deep shared-memory ring:
-//   * warp 4 (producer) fills a stage: device-memory tiles with TMA bulk
-//     copies (cp.async.bulk, completion counted in bytes on the stage's
-//     mbarrier), host-tier tiles (pinned, mapped) with 16-byte loads;
+//   * warps 4-5 (producers) fill a stage, two tiles each (a warp issues its
+//     copies one after another): device-memory tiles with TMA bulk copies
+//     (cp.async.bulk, completion counted in bytes on the stage's mbarrier),
+//     host-tier tiles (pinned, mapped) with 16-byte loads;
 //   * warps 0-3 (consumers) each own one tile per stage: q.K^T with fp32 FMAs
 //     and shuffle reductions, an fp32 online softmax in the exp2 domain, then
 //     P.V into per-lane fp32 accumulators, and release the stage.
@@ -48,7 +49,11 @@ struct Cfg {
   static constexpr int kNCH = kRB / 16;
   static constexpr int kEPC = 16 / kE;
   static constexpr int kNW = 4;  // consumer warps
-  static constexpr int kThreads = (kNW + 1) * 32;
+  // producer warps: a warp issues its copies one after another, so the
+  // tiles of a stage are split between two of them
+  static constexpr int kNP = 2;
+  static constexpr int kTilesPerProd = kNW / kNP;  // tiles of a stage per producer warp
+  static constexpr int kThreads = (kNW + kNP) * 32;
   static constexpr int kMaxTT = 16;
   // q.K: kTPT lanes per token, each holding kCPL 16-byte chunks of q per head
   static constexpr int kTPT = cmin(p2div(kNCH, 1), ceil_pow2(cmax(2, GQ * D / 64), 1));
@@ -70,7 +75,7 @@ struct Cfg {
   static constexpr int kBarBytes = 128;
   static constexpr int kPsBytes = round128(kNW * kMaxTT * GQ * 4);
   static constexpr int kRedBytes = round128((2 * kNW * GQ + kNW * kRedRows * GQ * D) * 4);
-  static constexpr int kSmem = kBarBytes + kIdRingBytes + kPsBytes + kRedBytes + kNST * kStageBytes;
+  static constexpr int kSmem = kBarBytes + kNP * kIdRingBytes + kPsBytes + kRedBytes + kNST * kStageBytes;
   static constexpr int kPrefixMax = round128((kMaxPersistentRows + 1) * 4);
   static constexpr bool kValid = (kRB % 16 == 0) && kNCH <= 32 && (GQ * kCPL * kEPC <= 64 || GQ == 1) &&
                                  (2 * kNST + 2) * 8 <= kBarBytes && kSmem + kPrefixMax <= 227 * 1024;
@@ -88,12 +93,12 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   uint64_t* empty = full + C::kNST;
   uint64_t* comb_full = empty + C::kNST;  // 4 consumer warps wrote their piece state
   uint64_t* comb_done = comb_full + 1;    // 4 consumer warps finished the piece outputs
-  int* id_ring = reinterpret_cast<int*>(smem + C::kBarBytes);
-  float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes + kIdRingBytes);
-  float* red_m = reinterpret_cast<float*>(smem + C::kBarBytes + kIdRingBytes + C::kPsBytes);
+  int* id_ring = reinterpret_cast<int*>(smem + C::kBarBytes);  // [kNP] rings
+  float* ps_all = reinterpret_cast<float*>(smem + C::kBarBytes + C::kNP * kIdRingBytes);
+  float* red_m = reinterpret_cast<float*>(smem + C::kBarBytes + C::kNP * kIdRingBytes + C::kPsBytes);
   float* red_l = red_m + C::kNW * GQ;
   float* red_acc = red_l + C::kNW * GQ;
-  unsigned char* stages = smem + C::kBarBytes + kIdRingBytes + C::kPsBytes + C::kRedBytes;
+  unsigned char* stages = smem + C::kBarBytes + C::kNP * kIdRingBytes + C::kPsBytes + C::kRedBytes;
   int* prefix = reinterpret_cast<int*>(stages + C::kNST * C::kStageBytes);
   __shared__ int abort_flag;
 
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     abort_flag = 0;
 #pragma unroll
     for (int s = 0; s < C::kNST; ++s) {
-      mbar_init(&full[s], 32);
+      mbar_init(&full[s], 32 * C::kNP);
       mbar_init(&empty[s], C::kNW);
     }
     mbar_init(comb_full, C::kNW);
@@ -227,22 +232,27 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
 
   const uint32_t tile_bytes = (uint32_t)p.TT * C::kRB;
 
-  if (warp == C::kNW) {
-    // ------------------------------------------------------------ producer
+  if (warp >= C::kNW) {
+    // ------------------------------------------------------------ producers
+    // producer pw fills tiles [pw * kTilesPerProd, (pw + 1) * kTilesPerProd)
+    // of every stage;
+    // block ids kIdAhead stages ahead (a cp.async ring per producer), q of
+    // coming pieces prefetched into L2 for the consumers (producer 0)
+    const int pw = warp - C::kNW;
+    const int slot0 = pw * C::kTilesPerProd;  // first tile slot of this producer in a stage
+    const int q_heads = pw == 0 ? GQ : 0;
     const uint64_t pol = l2_evict_first_policy();
-    // block ids kIdAhead stages ahead (cp.async ring), q of coming pieces
-    // prefetched into L2 for the consumers
     IdPrefetch ids;
     ids.it = pieces;  // a copy, before any piece was taken: the same sequence
-    ids.ring = id_ring;
+    ids.ring = id_ring + pw * (kIdRingBytes / 4);
     ids.issued = 0;
-    for (int i = 0; i < kIdAhead; ++i) ids.push(p, lane, GQ, C::kRB);
+    for (int i = 0; i < kIdAhead; ++i) ids.push(p, lane, q_heads, C::kRB, slot0, C::kTilesPerProd);
     int k = 0;
     Piece pc;
     while (next_piece(pc)) {
       const int kh = pc.y / p.gcs;
       for (int t = pc.t0; t < pc.t1; t += C::kNW, ++k) {
-        ids.push(p, lane, GQ, C::kRB);  // stage k + kIdAhead
+        ids.push(p, lane, q_heads, C::kRB, slot0, C::kTilesPerProd);  // stage k + kIdAhead
         const int64_t id_k = ids.take(k, lane);
         const int st = k % C::kNST;
         const uint32_t use = (uint32_t)(k / C::kNST);
@@ -251,13 +261,13 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
           return;
         }
         unsigned char* sbase = stages + st * C::kStageBytes;
-        const int tile = t + lane;
+        const int tile = t + slot0 + lane;
         int tier = 0;
         bool valid = false;
         const unsigned char* ks = nullptr;
         const unsigned char* vs = nullptr;
         int blk_id = 0, r0 = 0;
-        if (lane < C::kNW && tile < pc.t1) {
+        if (lane < C::kTilesPerProd && tile < pc.t1) {
           const int b = tile / p.tiles_per_block;
           r0 = (tile - b * p.tiles_per_block) * p.TT;
           int64_t id = id_k;
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
         // tile's two copies (no cross-lane traffic on the issue path)
         const bool own = bulk && (p.contig[tier] || p.use_tmap[tier]);
         if (own) {
-          unsigned char* kd = sbase + (2 * lane) * C::kTileSlot;
+          unsigned char* kd = sbase + (2 * (slot0 + lane)) * C::kTileSlot;
           unsigned char* vd = kd + C::kTileSlot;
           if (p.contig[tier]) {
             bulk_g2s(kd, ks, tile_bytes, &full[st], pol);
@@ -303,7 +313,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
           const unsigned char* vw = reinterpret_cast<const unsigned char*>(
               __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
           const int tr = __shfl_sync(0xffffffffu, tier, w);
-          unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
+          unsigned char* kd = sbase + (2 * (slot0 + w)) * C::kTileSlot;
           unsigned char* vd = kd + C::kTileSlot;
           for (int r = lane; r < p.TT; r += 32) {
             bulk_g2s(kd + r * C::kRB, kw + r * p.tok_sb[tr], C::kRB, &full[st], pol);
@@ -318,7 +328,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
               __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vs), w));
           const int tr = __shfl_sync(0xffffffffu, tier, w);
           const int64_t tsb = p.tok_sb[tr];
-          unsigned char* kd = sbase + (2 * w) * C::kTileSlot;
+          unsigned char* kd = sbase + (2 * (slot0 + w)) * C::kTileSlot;
           unsigned char* vd = kd + C::kTileSlot;
           const int nch = p.TT * C::kNCH;
           constexpr int U = 4;
@@ -619,28 +629,39 @@ __global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, in
   if (threadIdx.x == 0 && p.lse != nullptr) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = M + logf(L);
 }
 
-// Persistent schedule: a (row, kv-head chunk) segment cut by CTA range
-// boundaries has one partial per CTA that touched it; CTA c's range is
-// [c*T/N, (c+1)*T/N) of the T flattened tiles, so those CTAs are
-// cta(g0) .. cta(g1-1) with cta(t) = ((t+1)*N - 1) / T.  The first of them
-// holds the partial in its slot 0 if its range starts at the segment, else in
-// slot 1; every later one in slot 0 (CTAs with an empty range, possible when
-// T < N, wrote nothing and are skipped).  One CTA per (chunk, row).
+// Persistent schedule: merge the segments that CTA ranges cut.  One CTA per
+// decode CTA c: it merges the segment containing its range start when that
+// segment began in an earlier CTA and its last real tile lies in c's range,
+// so every cut segment is merged exactly once (by the CTA holding its last
+// tile) and the grid stays at the decode kernel's CTA count instead of one
+// CTA per (row, kv-head chunk) segment.  Slot rule: the first contributing
+// CTA wrote into slot 0 if the segment was its first real piece, else slot
+// 1; every later one into slot 0.
 __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
-  const int y = blockIdx.x;
-  const int i = blockIdx.y;
   const int* P = p.ws_prefix;
-  const int nv = P[i + 1] - P[i];
-  if (nv == 0) return;
-  const int nt = nv - p.vtiles;  // real tiles of the segment; the rest only weigh the split
   const int Y = p.KVH * p.gcs;
   const int64_t N = p.ncta;
   const int64_t T = (int64_t)P[p.n] * Y;
+  const int64_t c = blockIdx.x;
+  const int64_t ga = c * T / N, gb = (c + 1) * T / N;
+  if (ga >= gb) return;
+  int lo = 0, hi = p.n - 1;  // last row whose first position is <= ga
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if ((int64_t)P[mid] * Y <= ga) lo = mid; else hi = mid - 1;
+  }
+  const int i = lo;
+  const int nv = P[i + 1] - P[i];
+  if (nv == 0) return;
+  const int nt = nv - p.vtiles;  // real tiles of the segment; the rest only weigh the split
+  const int64_t local = ga - (int64_t)P[i] * Y;
+  const int y = (int)(local / nv);
+  const int t0 = (int)(local - (int64_t)y * nv);
+  if (t0 == 0 || t0 >= nt) return;  // starts here, or only weight positions left
   const int64_t g0 = (int64_t)P[i] * Y + (int64_t)y * nv;
-  const int64_t g1 = g0 + nt;
+  if (g0 + nt - 1 >= gb) return;  // continues into a later CTA, which merges it
   const int64_t c0 = ((g0 + 1) * N - 1) / T;  // CTA owning position g0
-  const int64_t c1 = (g1 * N - 1) / T;        // CTA owning the last real tile
-  if (c0 == c1) return;
+  const int64_t c1 = c;
   // the segment is c0's first real piece (slot 0) unless c0's range holds
   // real tiles before g0, i.e. starts before the previous segment's weight
   // positions
@@ -652,15 +673,15 @@ __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParam
   for (int o = threadIdx.x; o < GQ * D; o += blockDim.x) {
     const int g = o / D, d = o - g * D;
     float M = -INFINITY;
-    for (int64_t c = c0; c <= c1; ++c) {
-      if ((c * T) / N == ((c + 1) * T) / N) continue;
-      const int64_t s = (c * 2 + (c == c0 ? first_slot : 0)) * GQ + g;
+    for (int64_t cc = c0; cc <= c1; ++cc) {
+      if ((cc * T) / N == ((cc + 1) * T) / N) continue;
+      const int64_t s = (cc * 2 + (cc == c0 ? first_slot : 0)) * GQ + g;
       M = fmaxf(M, p.part_lse[s]);
     }
     float L = 0.f, O = 0.f;
-    for (int64_t c = c0; c <= c1; ++c) {
-      if ((c * T) / N == ((c + 1) * T) / N) continue;
-      const int64_t s = (c * 2 + (c == c0 ? first_slot : 0)) * GQ + g;
+    for (int64_t cc = c0; cc <= c1; ++cc) {
+      if ((cc * T) / N == ((cc + 1) * T) / N) continue;
+      const int64_t s = (cc * 2 + (cc == c0 ? first_slot : 0)) * GQ + g;
       const float w = exp2f((p.part_lse[s] - M) * kLog2e);
       L += w;
       O = fmaf(w, p.part_o[s * D + d], O);
@@ -1060,7 +1081,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     }
     if (launch_combine && ncta > 1) {
       const int threads = g.GQ * D <= 128 ? 128 : 256;
-      fdk::fd_persistent_combine_kernel<<<dim3(a->num_kv_heads * g.gcs, a->n), threads, 0, s>>>(p, D);
+      fdk::fd_persistent_combine_kernel<<<(unsigned)ncta, threads, 0, s>>>(p, D);
       st = fdh::cuda_status(cudaGetLastError(), "fd_persistent_combine_kernel launch");
     }
     return st;
