@@ -429,7 +429,9 @@ def run_ours(args, ws, rank, device):
     step_b = batch.step_bytes()
     achieved = step_b / kern_t / 1e9
     kname = gpu_ops.decode_kernel_name(batch.dtype, batch.D, batch.H, batch.KVH, batch.BS, batch.n, tps)
-    traffic = _traffic(kname, args.workload)
+    # the captured traffic of the host-tier workloads is the staged path's
+    # (every byte from HBM); the mapped path reads the host tier over PCIe
+    traffic = _traffic(kname, args.workload) if staged or host_b == 0 else None
     if traffic is not None and args.workload == "c3":
         traffic = int(traffic * (args.ctx / ws) / 131072)  # the table holds one GPU's full-context launch
     roof = {"unit": "GB/s", "achieved": round(achieved, 1), "traffic": traffic,
@@ -657,7 +659,7 @@ def run_trace(args, ws, rank, device):
     step_b, hbm_b, host_b = step_b / K, hbm_b / K, host_b / K  # one layer's decode launch
     t_ideal = (step_b - host_b) / (peaks["hbm_gbs"] * 1e9) + host_b / (pcie * 1e9)
     kname = gpu_ops.decode_kernel_name(dt, D, H, KVH, BS, Rmax)
-    roof = {"unit": "GB/s", "achieved": round(step_b / kern_t / 1e9, 1), "traffic": _traffic(kname, "c4"),
+    roof = {"unit": "GB/s", "achieved": round(step_b / kern_t / 1e9, 1), "traffic": _traffic(kname, "c4") if staged else None,
             "kernel": kname, "algorithmic_bytes_per_launch": int(step_b), "kernel_ms": round(kern_t * 1e3, 4),
             "bound": "hbm+pcie", "peak": round(step_b / t_ideal / 1e9, 1), "frac": round(t_ideal / kern_t, 4),
             "peak_note": f"bytes at their tier's rate: HBM {peaks['hbm_gbs']} GB/s ({peaks['source']}), host tier "
