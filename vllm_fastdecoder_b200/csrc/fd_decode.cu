@@ -107,27 +107,15 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   const int Y = p.KVH * p.gcs;
 
   // ---------------------------------------------------------------- setup
-  if (p.persistent && warp == 0) {
-    // prefix[i] = positions of rows < i: tiles + vtiles per row (0 for empty
-    // rows and rows whose length overruns their table row)
-    int carry = 0;
-    for (int base = 0; base < p.n; base += 32) {
-      const int i = base + lane;
-      int nt = 0;
-      if (i < p.n) {
-        const int len = p.lens[i];
-        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + p.TT - 1) / p.TT + p.vtiles;
-      }
-      int v = nt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, v, off);
-        if (lane >= off) v += u;
-      }
-      if (i < p.n) prefix[i + 1] = carry + v;
-      carry += __shfl_sync(0xffffffffu, v, 31);
+  // prefix[i] = positions of rows < i: tiles + vtiles per row (0 for empty
+  // rows and rows whose length overruns their table row).  Every thread
+  // loads lengths (independent loads: one memory round trip) and leaves
+  // row i's count in prefix[i + 1]; warp 0 then scans in place.
+  if (p.persistent) {
+    for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
+      const int len = p.lens[i];
+      prefix[i + 1] = (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) ? (len + p.TT - 1) / p.TT + p.vtiles : 0;
     }
-    if (lane == 0) prefix[0] = 0;
   }
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -141,6 +129,22 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     fence_barrier_init();
   }
   __syncthreads();
+  if (p.persistent && warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < p.n; base += 32) {
+      const int i = base + lane;
+      int v = i < p.n ? prefix[i + 1] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += u;
+      }
+      if (i < p.n) prefix[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) prefix[0] = 0;
+  }
+  if (p.persistent) __syncthreads();
 
   int64_t g_cur = 0, g_end = 0;
   int row_cur = 0;

@@ -189,27 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   const int Y = p.KVH;
 
   // ---------------------------------------------------------------- setup
-  if (warp == 0) {
-    int carry = 0;
-    for (int base = 0; base < p.n; base += 32) {
-      const int i = base + lane;
-      int nt = 0;
-      if (i < p.n) {
-        const int len = p.lens[i];
-        lens_s[i] = len;
-        trow_s[i] = p.bt_rows != nullptr ? p.bt_rows[i] : i;
-        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + kTT - 1) / kTT + p.vtiles;
-      }
-      int v = nt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, v, off);
-        if (lane >= off) v += u;
-      }
-      if (i < p.n) prefix[i + 1] = carry + v;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-    if (lane == 0) prefix[0] = 0;
+  // lengths and table rows into shared memory by every thread (independent
+  // loads: one memory round trip), then warp 0 scans them
+  for (int i = threadIdx.x; i < p.n; i += kThreads) {
+    lens_s[i] = p.lens[i];
+    trow_s[i] = p.bt_rows != nullptr ? p.bt_rows[i] : i;
   }
   // q and P buffers start zeroed: the padding rows stay zero
   for (int o = threadIdx.x * 16; o < 2 * kQB + 2 * kPB; o += kThreads * 16)
@@ -241,6 +225,27 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < p.n; base += 32) {
+      const int i = base + lane;
+      int nt = 0;
+      if (i < p.n) {
+        const int len = lens_s[i];
+        if (len > 0 && (len + p.BS - 1) / p.BS <= p.bt_width) nt = (len + kTT - 1) / kTT + p.vtiles;
+      }
+      int v = nt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += u;
+      }
+      if (i < p.n) prefix[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) prefix[0] = 0;
   }
   tc_fence_before();
   __syncthreads();
