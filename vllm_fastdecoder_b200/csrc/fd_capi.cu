@@ -32,6 +32,23 @@ int ensure_smem(const void* kernel, int bytes, unsigned long long* done_mask) {
   return FD_OK;
 }
 
+int device_sms(int* dev, int* sms) {
+  static int cached[64] = {0};
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (*dev >= 0 && *dev < 64) {
+    const int c = __atomic_load_n(&cached[*dev], __ATOMIC_RELAXED);
+    if (c > 0) {
+      *sms = c;
+      return FD_OK;
+    }
+  }
+  e = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, *dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+  if (*dev >= 0 && *dev < 64) __atomic_store_n(&cached[*dev], *sms, __ATOMIC_RELAXED);
+  return FD_OK;
+}
+
 }  // namespace fdh
 
 extern "C" const char* fd_last_error_message(void) { return g_msg; }

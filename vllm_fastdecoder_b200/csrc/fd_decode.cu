@@ -24,6 +24,7 @@
 #include <math.h>
 
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <mutex>
@@ -732,16 +733,30 @@ int launch_impl(const DecodeParams& p, dim3 grid, size_t extra, cudaStream_t s) 
   return fdh::cuda_status(cudaGetLastError(), "fd_decode_kernel launch");
 }
 
+// resident CTAs per SM of this kernel (queried once per device)
 template <typename T, int D, int GQ>
 int occupancy_impl(int* per_sm) {
   using C = Cfg<T, D, GQ>;
   static unsigned long long done = 0;
+  static int cached[64] = {0};
   auto kern = fdk::fd_decode_kernel<T, D, GQ>;
   int st = fdh::ensure_smem(reinterpret_cast<const void*>(kern), C::kSmem + C::kPrefixMax, &done);
   if (st != FD_OK) return st;
-  return fdh::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, C::kThreads,
-                                                                        C::kSmem + C::kPrefixMax),
-                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fdh::cuda_status(e, "cudaGetDevice");
+  if (dev >= 0 && dev < 64) {
+    const int c = __atomic_load_n(&cached[dev], __ATOMIC_RELAXED);
+    if (c > 0) {
+      *per_sm = c;
+      return FD_OK;
+    }
+  }
+  st = fdh::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, C::kThreads,
+                                                                      C::kSmem + C::kPrefixMax),
+                        "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (st == FD_OK && *per_sm > 0 && dev >= 0 && dev < 64) __atomic_store_n(&cached[dev], *per_sm, __ATOMIC_RELAXED);
+  return st;
 }
 
 struct KernelFns {
@@ -909,8 +924,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // blocks} with byte strides {head, token, block} and a box of one tile
 // {D, 1, TT, 1}.  Returns false when the driver rejects it (the caller then
 // copies tile rows one by one).
-bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
-                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128 = false) {
+bool encode_tier_map_uncached(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
+                              int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (enc == nullptr || nblk <= 0 || nblk > (int64_t)0xffffffff) return false;
   CUtensorMapDataType dt = dtype == FD_DTYPE_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -925,6 +940,58 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
                          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Tensor maps of the recently used K/V views (a KV cache lives for the whole
+// run, so the same few views come back every call): encoding one is a driver
+// call of about a microsecond.  The key is every input of the encoding.
+struct TmapKey {
+  const void* base;
+  int64_t nblk, head_sb, tok_sb, blk_sb;
+  int dtype, D, KVH, BS, TT, swizzle;
+};
+
+bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
+                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128 = false) {
+  constexpr int kSlots = 32;
+  struct Entry {
+    TmapKey key;
+    CUtensorMap map;
+    bool used;
+  };
+  static Entry cache[kSlots];
+  static int next = 0;
+  static std::mutex mu;
+  TmapKey key;
+  memset(&key, 0, sizeof(key));  // padding bytes take part in the comparison
+  key.base = base;
+  key.nblk = nblk;
+  key.head_sb = head_sb;
+  key.tok_sb = tok_sb;
+  key.blk_sb = blk_sb;
+  key.dtype = dtype;
+  key.D = D;
+  key.KVH = KVH;
+  key.BS = BS;
+  key.TT = TT;
+  key.swizzle = swizzle128 ? 1 : 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < kSlots; ++i)
+      if (cache[i].used && memcmp(&cache[i].key, &key, sizeof(key)) == 0) {
+        *m = cache[i].map;
+        return true;
+      }
+  }
+  if (!encode_tier_map_uncached(m, base, dtype, D, KVH, BS, nblk, head_sb, tok_sb, blk_sb, TT, swizzle128))
+    return false;
+  std::lock_guard<std::mutex> lock(mu);
+  Entry& e = cache[next];
+  next = (next + 1) % kSlots;
+  e.key = key;
+  e.map = *m;
+  e.used = true;
+  return true;
 }
 
 // Validate `a` and fill the kernel parameters; launch_main / launch_combine
@@ -1045,9 +1112,8 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     // as many CTAs as fit on the device at once (capped by the partial slots
     // and by the tile count, at least 16 tiles each)
     int dev = 0, sms = 0, per_sm = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return fdh::cuda_status(e, "device attributes");
+    st = fdh::device_sms(&dev, &sms);
+    if (st != FD_OK) return st;
     if (g.mma) {
       per_sm = 1;  // the tensor-core kernel takes most of an SM's shared memory
     } else {

@@ -759,9 +759,8 @@ int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem
     if (p.nblk[t] > 0 && !p.host[t] && !p.use_tmap[t]) return FD_OK;
   const size_t smem = (size_t)mma::kSmemFixed + 3 * extra_smem;  // prefix, lengths, table rows
   int dev = 0, sms = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return fdh::cuda_status(e, "device attributes");
+  int st0 = fdh::device_sms(&dev, &sms);
+  if (st0 != FD_OK) return st0;
   const int n = std::max(1, std::min(*ncta, std::min(sms, kMaxPersistentCtas)));
   DecodeParams q = p;
   q.ncta = n;

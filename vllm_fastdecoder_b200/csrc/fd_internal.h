@@ -34,4 +34,7 @@ inline int cuda_status(cudaError_t e, const char* what) {
 // Raise the dynamic shared-memory limit of `kernel` once per device.
 int ensure_smem(const void* kernel, int bytes, unsigned long long* done_mask);
 
+// The current device and its SM count (queried once per device).
+int device_sms(int* dev, int* sms);
+
 }  // namespace fdh
