@@ -82,6 +82,31 @@ struct Piece {
 // role of a kernel runs its own copy over the same sequence.  prefix/lens
 // may live in shared memory; lens may be null when the caller does not need
 // Piece::len.
+// Warm L2 with the block-table rows a CTA of a persistent launch is likely
+// to start in, while the row lengths load (the first block ids are then an L2
+// hit instead of a DRAM round trip): the whole table when it spans at most 64
+// lines, else the rows around the CTA's even share of rows.  A hint only:
+// the rows actually read come from the prefix.  Every address lies within a
+// row's first bt_width entries.  Measured on B200: config 2 (tensor-core
+// kernel) 0.2395 -> 0.2377 ms; the CUDA-core kernel on configs 0 and 1 lost
+// ~0.5 %, so only the tensor-core kernel calls it.
+__device__ __forceinline__ void warm_block_table(const DecodeParams& p) {
+  if (p.bt_rows != nullptr || p.n <= 0) return;  // table rows of a device-built list are not known yet
+  const int lpr = (p.bt_width * 4 + 127) / 128;  // 128-byte lines per row
+  int r0 = 0, r1 = p.n;
+  if ((int64_t)p.n * lpr > 64) {
+    const int est = (int)(((int64_t)blockIdx.x * p.n) / gridDim.x);
+    r0 = est > 0 ? est - 1 : 0;
+    r1 = est + 2 < p.n ? est + 2 : p.n;
+  }
+  const int total = (r1 - r0) * lpr;
+  for (int l = threadIdx.x; l < total; l += blockDim.x) {
+    const int r = r0 + l / lpr;
+    const int e = (l % lpr) * 32 < p.bt_width ? (l % lpr) * 32 : p.bt_width - 1;
+    prefetch_l2(p.bt + (int64_t)r * p.bt_stride + e);
+  }
+}
+
 struct StageIter {
   int64_t g_cur, g_end;
   const int* prefix;

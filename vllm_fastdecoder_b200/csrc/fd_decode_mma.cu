@@ -191,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   // ---------------------------------------------------------------- setup
   // lengths and table rows into shared memory by every thread (independent
   // loads: one memory round trip), then warp 0 scans them
+  warm_block_table(p);
   for (int i = threadIdx.x; i < p.n; i += kThreads) {
     lens_s[i] = p.lens[i];
     trow_s[i] = p.bt_rows != nullptr ? p.bt_rows[i] : i;
