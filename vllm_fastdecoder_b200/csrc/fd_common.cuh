@@ -117,6 +117,14 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before the kernel ahead of it in the stream ends;
+// griddep_wait() blocks until that kernel has completed and its memory
+// operations are visible, and griddep_launch_dependents() lets the
+// dependent kernel start launching once every CTA has called it or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // Fetch the 128-byte line holding p into L2 (no register result).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));

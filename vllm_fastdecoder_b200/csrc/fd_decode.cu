@@ -602,6 +602,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     ++npieces;
     if (abort_flag) return;
   }
+  griddep_launch_dependents();  // this CTA's writes are issued: the combine may launch
 }
 
 // Split-grid schedule: combine the split partials of rows that needed more
@@ -643,6 +644,7 @@ __global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, in
 // CTA wrote into slot 0 if the segment was its first real piece, else slot
 // 1; every later one into slot 0.
 __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
+  griddep_wait();  // launched early (programmatic dependent launch): the decode's partials first
   const int* P = p.ws_prefix;
   const int Y = p.KVH * p.gcs;
   const int64_t N = p.ncta;
@@ -1150,9 +1152,22 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
       if (st != FD_OK) return st;
     }
     if (launch_combine && ncta > 1) {
+      // programmatic dependent launch: the combine's launch overlaps the
+      // decode's last CTAs; the kernel waits for the decode grid before
+      // reading its partials
       const int threads = g.GQ * D <= 128 ? 128 : 256;
-      fdk::fd_persistent_combine_kernel<<<(unsigned)ncta, threads, 0, s>>>(p, D);
-      st = fdh::cuda_status(cudaGetLastError(), "fd_persistent_combine_kernel launch");
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)ncta);
+      cfg.blockDim = dim3((unsigned)threads);
+      cfg.dynamicSmemBytes = 0;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      st = fdh::cuda_status(cudaLaunchKernelEx(&cfg, fdk::fd_persistent_combine_kernel, p, D),
+                            "fd_persistent_combine_kernel launch");
     }
     return st;
   }

@@ -726,6 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   tc_fence_after();
   if (warp == 5)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  griddep_launch_dependents();  // this CTA's writes are issued: the combine may launch
 }
 
 }  // namespace mma
