@@ -309,10 +309,12 @@ def run_ours(args, ws, rank, device):
     torch.cuda.synchronize(device)
     gpu_ops.check_device_errors(device)
 
-    # the step as one CUDA graph (both launches; the sharded exchange stays
-    # eager), with its own workspace so no later call can move it
+    # the step as one CUDA graph (decode and combine launches, and on N > 1
+    # GPUs of config 3 the exchange: the NCCL all-gather and merge, or the
+    # peer-memory kernel, whose step counter lives on the device), with its
+    # own workspace so no later call can move it
     graph = None
-    if not args.no_graph and gather is None:
+    if not args.no_graph:
         ws_g = torch.empty(max(256, a.workspace_bytes), dtype=torch.uint8, device=device)
         a_g = gpu_ops.decode_args(res.q, dec_tiers, dec_split, res.block_table, res.lens, batch.scale, out, lse,
                                   max_len=max_len, tiles_per_split=tps, workspace_buf=ws_g)
@@ -322,6 +324,8 @@ def run_ours(args, ws, rank, device):
             gpu_ops.launch_decode(a_g, device, "partials")
             if has_combine:
                 gpu_ops.launch_decode(a_g, device, "combine")
+            if gather is not None:
+                gather.exchange_and_merge(out, lse, final)
 
         gstep()
         torch.cuda.synchronize(device)
@@ -463,7 +467,8 @@ def run_ours(args, ws, rank, device):
         "scaling": "strong" if args.workload == "c3" else "weak", "vs_baseline": None, "dtype": _dtype_name(batch.dtype),
         "data": "synthetic (seeded N(0,1) q/K/V, configuration shapes)",
         "config": dict(_config(batch, args, ws, tps, has_combine), timing=(
-            "value: one CUDA graph of the step (decode + combine launches) replayed K times; roofline: eager "
+            "value: one CUDA graph of the step (decode + combine launches"
+            + (", exchange and merge" if gather is not None else "") + ") replayed K times; roofline: eager "
             f"steps with CUDA events around the decode launch (eager step {elapsed_eager / args.steps * 1e3:.4f} ms)"
             if graph is not None else "value and roofline: eager steps, CUDA events")),
         "kv_gbs": round((hbm_b + host_b) * (1 if args.workload == "c3" else ws) * args.steps / elapsed / 1e9, 1),
@@ -482,6 +487,8 @@ def run_ours(args, ws, rank, device):
             "sample": _sample_text(batch, r),
             "cpu": _cpu_model(),
         }
+    if graph is not None:
+        graph.reset()  # a graph holding NCCL calls goes before the process group does
     if gather is not None:
         line["config"]["exchange"] = ("peer memory: one fd_exchange_merge launch per step (CUDA IPC buffers, "
                                       "NVLink stores)" if args.exchange == "peer"
