@@ -8,6 +8,8 @@ import ctypes
 import re
 from pathlib import Path
 
+import pytest
+
 from vllm_fastdecoder_b200 import _native as nat
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -83,3 +85,38 @@ def test_workspace_size_arithmetic():
     assert lib.fd_decode_workspace_size(ctypes.byref(a)) == 0
     a.bt_width = 64  # 64 tiles per row, 8 per split -> 8 splits of partials
     assert lib.fd_decode_workspace_size(ctypes.byref(a)) >= 4 * 8 * 8 * 64 * 4
+
+
+def _valid_args():
+    """Arguments that pass every host-side check (fp16, D 128, 8/8 heads,
+    block size 16); the pointers are placeholders, never dereferenced by the
+    checks these tests reach."""
+    a = nat.FdDecodeArgs()
+    a.q, a.out, a.block_table, a.lens = 4096, 8192, 12288, 16384
+    a.q_stride_n, a.q_stride_h = 8 * 128, 128
+    a.n, a.num_heads, a.num_kv_heads, a.head_size, a.block_size = 4, 8, 8, 128, 16
+    a.bt_width, a.bt_stride, a.dtype, a.out_dtype = 8, 8, 0, 0
+    a.scale = 0.088
+    return a
+
+
+@pytest.mark.parametrize("field,value,code,msg", [
+    ("n", -1, 1, b"n must be"),
+    ("out_dtype", 1, 2, b"out_dtype"),
+    ("q", None, 1, b"required"),
+    ("bt_width", 0, 1, b"bt_width"),
+    ("n", 70000, 2, b"65535"),
+    ("block_size", 24, 2, b"block_size"),
+    ("num_heads", 6, 1, b"multiple"),
+    ("head_size", 60, 2, b"head_size"),
+    ("q", 4104, 3, b"q pointer"),
+    ("q_stride_h", 132, 3, b"q pointer"),
+])
+def test_decode_rejects_bad_arguments_before_any_launch(field, value, code, msg):
+    """Each bad argument is reported with its status code and message before
+    the library touches the GPU (the checks of fd_decode_attn)."""
+    lib = nat.load()
+    a = _valid_args()
+    setattr(a, field, value)
+    assert lib.fd_decode_attn(ctypes.byref(a), None) == code
+    assert msg in lib.fd_last_error_message()
