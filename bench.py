@@ -1,19 +1,23 @@
 """Benchmark of the paged decode-attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c0|c2|c3|c4]
+                    [--workload c3|c0|c1|c2|c4] [--exchange nccl|peer]
 
 Under torchrun (N > 1) there is one process per GPU.
 
 A step is one decode-attention pass over one synthetic batch (see
 vllm_fastdecoder_b200/workloads.py):
-  c1 (default)  GPU/host split: 64 rows of U[256,4096] tokens, 32/32 heads,
+  c3 (default)  8 rows x 131072 tokens, GQA 32/8 bf16, each row's KV split
+                contiguously over the N GPUs; every rank decodes its shard
+                and the partials are exchanged and LSE-merged (strong
+                scaling); after the timed region the merged output of three
+                (row, kv head) pairs is checked against the C oracle over the
+                whole context (`parity`)
+  c0            16 rows, one 4096-block HBM pool (the reference's CPU case)
+  c1            GPU/host split: 64 rows of U[256,4096] tokens, 32/32 heads,
                 fp16, HBM tier of 2048 blocks, the rest in pinned host memory;
                 N > 1 runs N independent replicas (weak scaling)
-  c0            16 rows, one 4096-block HBM pool (the reference's CPU case)
   c2            GQA 32/8 bf16, 256 rows, lognormal lengths, all HBM
-  c3            8 rows x 131072 tokens, GQA bf16, KV sharded over the N GPUs,
-                partials all-gathered over NCCL and LSE-merged (strong scaling)
   c4            a continuous-batching decode trace over 32 layers (about 128
                 running requests, most of their KV in the host tier); a step
                 is one decode step of every running request through all 32
@@ -26,8 +30,9 @@ back every step; `roofline` = algorithmic bytes of the decode kernel per
 launch / its event-timed duration, against the measured HBM copy peak (and,
 for the host tier, the pinned host->device copy rate measured in the same
 run); `cpu_baseline` = the reference's own AVX2 kernel (compiled from its
-source into oracle/_ref) on this host's cores.
-`--impl reference` times only that reference CPU kernel on the same workload.
+source into oracle/_ref) on this host's cores, on the same values.
+`--impl reference` times only that reference CPU kernel on the same workload,
+by the same method (3 warm-ups, median of at least 10 calls).
 """
 
 from __future__ import annotations
@@ -180,65 +185,155 @@ def host_part(batch):
     return bt, torch.tensor(lens, dtype=torch.int32)
 
 
-def reference_inputs(batch, resident=None, rows: int | None = None):
-    """CPU tensors in the reference layout for its decode_attn: q [n,H,D],
-    caches [C,KVH,BS,D], table, lens.  For c1 the cache is the pinned host
-    tier itself and the table covers its host blocks only."""
+def reference_inputs(batch, resident, rows: int | None = None):
+    """CPU tensors in the reference layout for its decode_attn, holding the
+    same values the GPU arm decodes: q [n,H,D], caches [C,KVH,BS,D], table,
+    lens.  With a host tier (c1) the caches are the pinned host tier itself
+    and the table covers its host blocks only (the reference's CPU leg);
+    otherwise the HBM pool is copied to the host in the reference layout and
+    the table is the batch's own."""
     n = batch.n if rows is None else rows
     if batch.num_host_blocks > 0:
-        assert resident is not None
         hk, hv = resident.tiers[1].k, resident.tiers[1].v
         bt, lens = host_part(batch)
-        q = resident.q[:n].cpu()
-        return q, hk, hv, bt[:n].contiguous(), lens[:n].contiguous()
-    g = torch.Generator().manual_seed(batch.seed + 7)
-    bt = batch.block_table[:n].contiguous()
-    lens = batch.lens[:n].contiguous()
-    used = sorted({int(x) for i in range(n) for x in bt[i, :(int(lens[i]) + batch.BS - 1) // batch.BS]})
-    remap = {b: k for k, b in enumerate(used)}
-    bt2 = torch.zeros_like(bt)
-    for i in range(n):
-        nb = (int(lens[i]) + batch.BS - 1) // batch.BS
-        bt2[i, :nb] = torch.tensor([remap[int(x)] for x in bt[i, :nb]], dtype=torch.int32)
-    shape = (len(used), batch.KVH, batch.BS, batch.D)
-    kc = torch.empty(shape, dtype=batch.dtype)
-    vc = torch.empty(shape, dtype=batch.dtype)
-    kc.normal_(generator=g)
-    vc.normal_(generator=g)
-    q = torch.randn(n, batch.H, batch.D, generator=g).to(batch.dtype)
-    return q, kc, vc, bt2, lens
+        return resident.q[:n].cpu(), hk, hv, bt[:n].contiguous(), lens[:n].contiguous()
+    t = resident.tiers[0]
+    kc = t.k.contiguous().cpu()
+    vc = t.v.contiguous().cpu()
+    return (resident.q[:n].cpu(), kc, vc, batch.block_table[:n].contiguous(), batch.lens[:n].contiguous())
 
 
-def time_reference(batch, resident, steps: int, warmup: int, rows: int | None = None,
-                   budget_s: float | None = None):
-    """Median seconds per call of the reference AVX2 decode_attn with all host
-    threads.  Returns (seconds, threads, rows, kind)."""
+def time_reference(inputs, scale: float, steps: int, warmup: int) -> dict:
+    """The reference AVX2 decode_attn (oracle/_ref, all host threads) on
+    `inputs` = (q, k_cache, v_cache, block_table, lens): `warmup` untimed
+    calls, then `steps` timed calls (at least 10).  Falls back to the C
+    restatement, single-threaded, when the reference was not built.
+    Returns the median / min / max seconds per call, the thread count, the
+    kind ("reference" or "port") and the outputs of the last call."""
     from oracle import oracle as O
 
+    q, kc, vc, bt, lens = inputs
     ext = O.load_reference_ext()
-    kind = "reference"
-    q, kc, vc, bt, lens = reference_inputs(batch, resident, rows)
     H, n = q.shape[1], q.shape[0]
     out = torch.empty_like(q)
     lse = torch.empty(H, n, dtype=torch.float32)
     threads = os.cpu_count() or 1
     if ext is not None:
+        kind = "reference"
         ext.set_num_threads(threads)
-        fn = lambda: ext.decode_attn(q, kc, vc, bt, lens, batch.scale, out, lse)  # noqa: E731
-    else:  # the C restatement, single-threaded
+        fn = lambda: ext.decode_attn(q, kc, vc, bt, lens, scale, out, lse)  # noqa: E731
+    else:
         kind, threads = "port", 1
-        fn = lambda: O.decode_attn(q, kc, vc, bt, lens, batch.scale, out, lse)  # noqa: E731
-    for _ in range(warmup):
+        fn = lambda: O.decode_attn(q, kc, vc, bt, lens, scale, out, lse)  # noqa: E731
+    for _ in range(max(3, warmup)):
         fn()
     times = []
-    t_end = time.perf_counter() + (budget_s if budget_s else 1e9)
-    for _ in range(steps):
+    for _ in range(max(10, steps)):
         t0 = time.perf_counter()
         fn()
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end and len(times) >= 3:
-            break
-    return statistics.median(times), threads, n, kind
+    return {"median": statistics.median(times), "min": min(times), "max": max(times), "calls": len(times),
+            "threads": threads, "kind": kind, "rows": n, "out": out, "lse": lse,
+            "build": O.reference_ext_variant() if ext is not None else "oracle/libfd_oracle.so"}
+
+
+def _cpu_baseline_entry(r: dict, batch, unit_factor: float = 1.0, sample: str | None = None) -> dict:
+    """The cpu_baseline object of a timed reference leg: value from the
+    median, with the spread of the calls."""
+    per = lambda t: round(r["rows"] / (t * unit_factor), 2)  # noqa: E731
+    return {"value": per(r["median"]), "unit": UNIT, "cores": r["threads"], "kind": r["kind"],
+            "sample": sample or _sample_text(batch, r["rows"], r["calls"]),
+            "min_value": per(r["max"]), "max_value": per(r["min"]), "calls": r["calls"],
+            "method": "3 warm-up calls, then the median of the timed calls (min/max value from the slowest/fastest)",
+            "build": r["build"], "cpu": _cpu_model()}
+
+
+# ---------------------------------------------------------------- parity in the run
+
+
+def c3_slices(batch) -> list[tuple[int, int]]:
+    """(row, kv head) pairs whose full-context output the bench checks: the
+    first and the last, and one in between."""
+    return [(0, 0), (batch.n // 2, batch.KVH // 2), (batch.n - 1, batch.KVH - 1)]
+
+
+def c3_parity(batch, res, final: torch.Tensor, lse_out: torch.Tensor, ws: int, rank: int,
+              device: torch.device) -> dict | None:
+    """Check the sharded step's merged output against the C oracle over the
+    whole context.  For each checked (row, kv head) every rank gathers that
+    head's K and V over its shard in table order; an all-gather (every rank
+    takes part) brings the shards to rank 0 in rank order, i.e. sequence
+    order, and rank 0 runs the oracle's decode over the concatenated
+    131072 tokens (and a float64 evaluation) and compares the GPU's merged
+    o (bf16) and lse.  Returns the parity entry on rank 0, None elsewhere."""
+    import numpy as np
+
+    BS, D, G = batch.BS, batch.D, batch.H // batch.KVH
+    kt, vt = res.tiers[0].k, res.tiers[0].v  # [B, KVH, BS, D] views
+    worst = {"max_abs_o": 0.0, "max_abs_lse": 0.0, "max_abs_o_f64": 0.0, "max_abs_lse_f64": 0.0, "max_o": 0.0}
+    for (r, h) in c3_slices(batch):
+        L = int(batch.lens[r])
+        nb = (L + BS - 1) // BS
+        ids = res.block_table[r, :nb].long()
+        k = kt[ids, h].reshape(nb * BS, D)[:L].contiguous()
+        v = vt[ids, h].reshape(nb * BS, D)[:L].contiguous()
+        if ws > 1:
+            kk = torch.empty(ws * L, D, dtype=k.dtype, device=device)
+            vv = torch.empty(ws * L, D, dtype=v.dtype, device=device)
+            torch.distributed.all_gather_into_tensor(kk, k)
+            torch.distributed.all_gather_into_tensor(vv, v)
+            k, v = kk, vv
+        if rank != 0:
+            continue
+        from oracle import oracle as O
+
+        Lt = k.shape[0]
+        kc = k.cpu().view(Lt // BS, 1, BS, D)
+        vc = v.cpu().view(Lt // BS, 1, BS, D)
+        q = res.q[r, h * G:(h + 1) * G].cpu().view(1, G, D).contiguous()
+        bt = torch.arange(Lt // BS, dtype=torch.int32).view(1, -1)
+        ln = torch.tensor([Lt], dtype=torch.int32)
+        o_ref = torch.empty(1, G, D, dtype=batch.dtype)
+        lse_ref = torch.empty(G, 1, dtype=torch.float32)
+        O.decode_attn(q, kc, vc, bt, ln, batch.scale, o_ref, lse_ref)
+        o_gpu = final[r, h * G:(h + 1) * G].float().cpu()
+        l_gpu = lse_out[h * G:(h + 1) * G, r].cpu()
+        # float64 evaluation of the same head
+        kd = k.double().cpu().numpy()
+        vd = v.double().cpu().numpy()
+        qd = q[0].double().numpy()
+        sc = (qd @ kd.T) * batch.scale
+        m = sc.max(axis=1, keepdims=True)
+        e = np.exp(sc - m)
+        ssum = e.sum(axis=1, keepdims=True)
+        o64 = (e @ vd) / ssum
+        l64 = (m + np.log(ssum))[:, 0]
+        worst["max_abs_o"] = max(worst["max_abs_o"], float((o_gpu - o_ref[0].float()).abs().max()))
+        worst["max_abs_lse"] = max(worst["max_abs_lse"], float((l_gpu - lse_ref[:, 0]).abs().max()))
+        worst["max_abs_o_f64"] = max(worst["max_abs_o_f64"], float(np.abs(o_gpu.double().numpy() - o64).max()))
+        worst["max_abs_lse_f64"] = max(worst["max_abs_lse_f64"], float(np.abs(l_gpu.double().numpy() - l64).max()))
+        worst["max_o"] = max(worst["max_o"], float(np.abs(o64).max()))
+    if rank != 0:
+        return None
+    tol_o, tol_lse = 1.6e-2, 1e-4
+    return {k2: float(f"{v2:.3e}") for k2, v2 in worst.items()} | {
+        "checked": [f"row {r} kv-head {h}: {G} heads x {int(batch.lens[r]) * ws} tokens" for r, h in c3_slices(batch)],
+        "against": "C oracle (restatement of the reference decode_attn) over the whole context, and float64",
+        "tol": {"o_bf16": tol_o, "lse": tol_lse},
+        "ok": bool(worst["max_abs_o"] <= tol_o and worst["max_abs_lse"] <= tol_lse),
+    }
+
+
+def reference_parity(r: dict, out: torch.Tensor, lse: torch.Tensor, tol_o: float) -> dict:
+    """Our output against the reference kernel's on the same inputs (all rows)."""
+    o_gpu = out.float().cpu()
+    l_gpu = lse.cpu()
+    fin = torch.isfinite(r["lse"])
+    d_lse = float((l_gpu[fin] - r["lse"][fin]).abs().max()) if bool(fin.any()) else 0.0
+    d_o = float((o_gpu - r["out"].float()).abs().max())
+    return {"max_abs_o": float(f"{d_o:.3e}"), "max_abs_lse": float(f"{d_lse:.3e}"),
+            "against": f"the reference AVX2 decode_attn on the same inputs, all {r['rows']} rows",
+            "tol": {"o": tol_o, "lse": 1e-4}, "ok": bool(d_o <= tol_o and d_lse <= 1e-4)}
 
 
 # ---------------------------------------------------------------- our arm
@@ -355,13 +450,21 @@ def run_ours(args, ws, rank, device):
     torch.cuda.synchronize(device)
     elapsed_eager = t_start.elapsed_time(t_end) * 1e-3
     copy_t = (sum(c0.elapsed_time(c1) for c0, c1 in cevs) * 1e-3 / args.steps) if staged else 0.0
-    # the timed region of `value`: K graph replays (or the eager steps above)
+    # the timed region of `value`: K graph replays (or the eager steps above).
+    # A short step makes K steps shorter than nvidia-smi's sampling period,
+    # so the sampler starts under an untimed pre-roll of replays (~0.3 s of
+    # the same work) and its samples see the GPU under load.
     if graph is not None:
         if dist:
             torch.distributed.barrier()
         torch.cuda.synchronize(device)
         clocks.start()
-        time.sleep(0.25)
+        time.sleep(0.1)
+        pre = max(1, int(0.3 / max(elapsed_eager / args.steps, 1e-5)))
+        for _ in range(pre):
+            graph.replay()
+        if dist:
+            torch.distributed.barrier()  # NCCL barrier on the stream: after the pre-roll everywhere
         t_start.record()
         for _ in range(args.steps):
             graph.replay()
@@ -461,40 +564,56 @@ def run_ours(args, ws, rank, device):
         roof.update({"bound": "hbm", "peak": peaks["hbm_gbs"], "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_note": f"HBM copy bandwidth, {peaks['source']} (burst figure)"})
 
+    # ---- parity of this run's output (after the timed regions, outside them)
+    parity = None
+    if args.workload == "c3" and not args.no_parity:
+        parity = c3_parity(batch, res, final if sharded else out, gather.lse_out if sharded else lse, ws, rank,
+                           device)
+
+    run = {
+        "schedule": "split grid" if tps else "persistent (all CTAs resident, equal ranges of tiles plus "
+                                             "per-segment weight positions)",
+        "tiles_per_split": tps, "split_combine": has_combine, "kernel": kname,
+        "host_read": (args.host_read if res.tiers[1] is not None else "none (all HBM)"),
+        "timing": ("value: one CUDA graph of the step (decode + combine launches"
+                   + (", exchange and merge" if gather is not None else "") + ") replayed K times after an "
+                   "untimed pre-roll; roofline: eager steps with CUDA events around the decode launch (eager step "
+                   f"{elapsed_eager / args.steps * 1e3:.4f} ms)" if graph is not None
+                   else "value and roofline: eager steps, CUDA events"),
+    }
+    if gather is not None:
+        run["exchange"] = ("peer memory: one fd_exchange_merge launch per step (CUDA IPC buffers, NVLink stores)"
+                           if args.exchange == "peer" else "NCCL all_gather_into_tensor + fd_merge_partials")
+    full = workloads.config3(world=1, rank=0, ctx=args.ctx) if args.workload == "c3" else batch
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "strong" if args.workload == "c3" else "weak", "vs_baseline": None, "dtype": _dtype_name(batch.dtype),
         "data": "synthetic (seeded N(0,1) q/K/V, configuration shapes)",
-        "config": dict(_config(batch, args, ws, tps, has_combine), timing=(
-            "value: one CUDA graph of the step (decode + combine launches"
-            + (", exchange and merge" if gather is not None else "") + ") replayed K times; roofline: eager "
-            f"steps with CUDA events around the decode launch (eager step {elapsed_eager / args.steps * 1e3:.4f} ms)"
-            if graph is not None else "value and roofline: eager steps, CUDA events")),
-        "kv_gbs": round((hbm_b + host_b) * (1 if args.workload == "c3" else ws) * args.steps / elapsed / 1e9, 1),
+        "config": _config(full, args, ws),
+        "run": run,
+        "kv_gbs": round((hbm_b + host_b) * ws * args.steps / elapsed / 1e9, 1),
         "e2e": {"value": round(rows_per_step * args.steps / e2e_t, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "vllm_fastdecoder_b200.gpu_ops.decode_tiered (C ABI fd_decode_attn)"},
+                "api": "vllm_fastdecoder_b200.gpu_ops.decode_tiered (C ABI fd_decode_attn)"
+                       + (" + the exchange and merge" if gather is not None else "")},
         "roofline": roof,
         "clocks": clk,
         "gpu_launches": args.steps * (1 + int(has_combine) + (1 if gather is not None else 0)),
     }
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        rows = None if args.workload != "c3" else 1
-        t, th, r, kind = time_reference(batch, res, steps=30, warmup=3, rows=rows, budget_s=20.0)
-        line["cpu_baseline"] = {
-            "value": round(r / t, 2), "unit": UNIT, "cores": th, "kind": kind,
-            "sample": _sample_text(batch, r),
-            "cpu": _cpu_model(),
-        }
+    if parity is not None:
+        line["parity"] = parity
     if graph is not None:
         graph.reset()  # a graph holding NCCL calls goes before the process group does
-    if gather is not None:
-        line["config"]["exchange"] = ("peer memory: one fd_exchange_merge launch per step (CUDA IPC buffers, "
-                                      "NVLink stores)" if args.exchange == "peer"
-                                      else "NCCL all_gather_into_tensor + fd_merge_partials")
-        if hasattr(gather, "close"):
-            gather.close()  # collective: every rank reaches it
+    if gather is not None and hasattr(gather, "close"):
+        gather.close()  # collective: every rank reaches it
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        inputs = reference_inputs(batch, res)
+        r = time_reference(inputs, batch.scale, steps=10, warmup=3)
+        line["cpu_baseline"] = _cpu_baseline_entry(r, batch)
+        if batch.num_host_blocks == 0:
+            line["parity_vs_reference"] = reference_parity(
+                r, out, lse, 1.6e-2 if batch.dtype == torch.bfloat16 else 2e-3)
     return line
 
 
@@ -704,13 +823,11 @@ def run_trace(args, ws, rank, device):
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         b = tr.batch(W0)
         res = SimpleNamespace(tiers=tiers, q=q_all[0, :b.n])
-        t, th, r, kind = time_reference(b, res, steps=10, warmup=2, budget_s=15.0)
-        line["cpu_baseline"] = {
-            "value": round(r / (t * L), 2), "unit": UNIT, "cores": th, "kind": kind,
-            "sample": f"the reference's CPU leg of one layer of one step (decode_attn over the host-tier blocks of "
-                      f"{r} rows, {host_b / 1e9:.3f} GB), median of up to 10 calls, times 32 layers",
-            "cpu": _cpu_model(),
-        }
+        r = time_reference(reference_inputs(b, res), tr.scale, steps=10, warmup=3)
+        line["cpu_baseline"] = _cpu_baseline_entry(
+            r, b, unit_factor=L,
+            sample=f"the reference's CPU leg of one layer of one step (decode_attn over the host-tier blocks of "
+                   f"{r['rows']} rows, {host_b / 1e9:.3f} GB), median of {r['calls']} calls, times 32 layers")
     return line
 
 
@@ -728,32 +845,37 @@ def _cpu_model() -> str:
     return "unknown"
 
 
-def _sample_text(batch, rows) -> str:
+def _sample_text(batch, rows, calls: int) -> str:
     if batch.num_host_blocks > 0:
         _, host_b = batch.kv_bytes()
         return (f"the reference's CPU leg of one {batch.name} step: decode_attn over the host-tier blocks of "
-                f"all {batch.n} rows ({host_b / 1e9:.3f} GB of host KV), median of up to 30 calls")
-    return f"decode_attn over {rows} of the {batch.n} rows of one {batch.name} step, median of up to 30 calls"
+                f"all {batch.n} rows ({host_b / 1e9:.3f} GB of host KV), median of {calls} calls")
+    hbm_b, _ = batch.kv_bytes()
+    return (f"decode_attn over all {rows} rows of one {batch.name} step ({hbm_b / 1e9:.3f} GB of KV, whole "
+            f"contexts on one host), median of {calls} calls")
 
 
-def _config(batch, args, ws, tps, has_combine) -> dict:
+WORKLOADS = {
+    "c1": "GPU/host split with LSE merge (config 1): 64 rows, ctx U[256,4096], 32/32 heads, D128, fp16, "
+          "BS16, HBM tier 2048 blocks, per-row host fraction {0,.25,.5,.75,1}",
+    "c0": "single-layer paged decode (config 0): 16 rows, ctx U[64,2048], 32/32 heads, D128, fp16, "
+          "4096-block pool",
+    "c2": "GQA decode (config 2): 256 rows, ctx lognormal(median 1024, sigma 0.75) clip [32,8192], "
+          "32/8 heads, D128, bf16",
+    "c3": "long-context sharded decode (config 3): 8 rows x 131072 ctx, 32/8 heads, D128, bf16, BS16, "
+          "each row's blocks split contiguously over the GPUs, partials exchanged and LSE-merged",
+}
+
+
+def _config(batch, args, ws) -> dict:
+    """The workload's identity, the same in both arms: `batch` is the whole
+    workload (for c3 the unsharded batch, so byte counts are totals)."""
     hbm_b, host_b = batch.kv_bytes()
     return {
-        "workload": {
-            "c1": "GPU/host split with LSE merge (config 1): 64 rows, ctx U[256,4096], 32/32 heads, D128, fp16, "
-                  "BS16, HBM tier 2048 blocks, per-row host fraction {0,.25,.5,.75,1}",
-            "c0": "single-layer paged decode (config 0): 16 rows, ctx U[64,2048], 32/32 heads, D128, fp16, "
-                  "4096-block pool",
-            "c2": "GQA decode (config 2): 256 rows, ctx lognormal(median 1024, sigma 0.75) clip [32,8192], "
-                  "32/8 heads, D128, bf16",
-            "c3": f"long-context sharded decode (config 3): 8 rows x 131072 ctx, 32/8 heads, D128, bf16, "
-                  f"KV sharded over {ws} GPU(s), NCCL all-gather + LSE merge",
-        }[args.workload],
+        "workload": WORKLOADS[args.workload],
         "rows": batch.n, "heads": batch.H, "kv_heads": batch.KVH, "head_size": batch.D, "block_size": batch.BS,
+        "ctx_tokens": int(batch.lens.sum()),
         "hbm_kv_bytes": hbm_b, "host_kv_bytes": host_b, "hbm_layout": batch.hbm_layout,
-        "schedule": "split grid" if tps else "persistent (all CTAs resident, equal ranges of tiles plus "
-                                             "per-segment weight positions)",
-        "tiles_per_split": tps, "split_combine": has_combine,
         "l2": "no flush: each step streams more KV than the 126 MB L2" if hbm_b + host_b > (126 << 20)
               else "KV smaller than L2",
         "parallelism": f"replicas x{ws}" if args.workload != "c3" else f"kv-shard x{ws}",
@@ -764,29 +886,38 @@ def _config(batch, args, ws, tps, has_combine) -> dict:
 
 
 def run_reference(args, ws, rank, device):
+    """The reference arm: the reference's AVX2 decode_attn on this host's
+    cores over the same workload and the same values as the GPU arm (inputs
+    generated on the GPU with the same seeds, copied to the host in the
+    reference layout).  For c3 that is the whole 131072-token context of
+    every row on one host, whatever N is."""
     from vllm_fastdecoder_b200 import workloads
 
     if args.workload == "c4":
         return run_reference_trace(args, ws, device)
     if args.workload == "c3":
-        batch = workloads.config3(world=1, rank=0)
+        batch = workloads.config3(world=1, rank=0, ctx=args.ctx)
     else:
         batch = workloads.CONFIGS[args.workload]()
-    res = workloads.materialize(batch, device) if batch.num_host_blocks > 0 else None
-    t, th, r, kind = time_reference(batch, res, steps=args.steps, warmup=args.warmup)
-    v = round(r / t, 2)
+    res = workloads.materialize(batch, device)
+    inputs = reference_inputs(batch, res)
+    del res
+    torch.cuda.empty_cache()
+    r = time_reference(inputs, batch.scale, steps=args.steps, warmup=args.warmup)
+    entry = _cpu_baseline_entry(r, batch)
+    v = entry["value"]
     return {
         "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "impl": "reference",
-        "scaling": "weak", "vs_baseline": None, "dtype": _dtype_name(batch.dtype),
+        "ms_per_step": round(r["median"] * 1e3, 4), "higher_is_better": True, "impl": "reference",
+        "scaling": "strong" if args.workload == "c3" else "weak", "vs_baseline": None,
+        "dtype": _dtype_name(batch.dtype),
         "data": "synthetic (seeded N(0,1) q/K/V, configuration shapes)",
-        "config": _config(batch, args, 1, 0, False),
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": th, "kind": kind, "sample": _sample_text(batch, r),
-                         "cpu": _cpu_model()},
+        "config": _config(batch, args, ws),
+        "cpu_baseline": entry,
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's AVX2 decode_attn (fastdecode/csrc/cpu_attn.cpp) compiled from its source, "
-                "timed on this host; for c1 only its CPU leg (host-tier blocks) is timed, its GPU "
-                "FlashAttention leg would run concurrently",
+                "timed on this host with all its threads (rank 0 only; whole contexts, no sharding); for c1 "
+                "only its CPU leg (host-tier blocks) is timed, its GPU FlashAttention leg would run concurrently",
     }
 
 
@@ -805,9 +936,11 @@ def run_reference_trace(args, ws, device):
     per_layer, rows, th, kind = [], 0, 1, "reference"
     for k in range(args.warmup, args.warmup + args.steps):
         b = tr.batch(k)
-        t, th, r, kind = time_reference(b, SimpleNamespace(tiers=tiers, q=q[:b.n]), steps=3, warmup=1)
-        per_layer.append(t)
-        rows += r
+        r = time_reference(reference_inputs(b, SimpleNamespace(tiers=tiers, q=q[:b.n])), tr.scale, steps=10,
+                           warmup=3)
+        th, kind = r["threads"], r["kind"]
+        per_layer.append(r["median"])
+        rows += r["rows"]
     t_step = statistics.mean(per_layer) * tr.layers
     v = round(rows / len(per_layer) / t_step, 2)
     return {
@@ -818,7 +951,7 @@ def run_reference_trace(args, ws, device):
         "config": {"workload": "continuous-batching decode trace (config 4), 32 layers; the reference's CPU leg"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": th, "kind": kind,
                          "sample": "decode_attn over the host-tier blocks of one layer of each timed step "
-                                   "(median of 3 calls), times 32 layers", "cpu": _cpu_model()},
+                                   "(median of 10 calls after 3 warm-ups), times 32 layers", "cpu": _cpu_model()},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's AVX2 decode_attn (fastdecode/csrc/cpu_attn.cpp) compiled from its source, "
                 "timed on this host over the host-tier part of the trace; its GPU FlashAttention leg would "
@@ -842,7 +975,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=0)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1", "c0", "c2", "c3", "c4"], default="c1")
+    ap.add_argument("--workload", choices=["c3", "c0", "c1", "c2", "c4"], default="c3")
+    ap.add_argument("--no-parity", action="store_true", help="c3: skip the in-run oracle check of the output")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",

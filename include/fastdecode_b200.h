@@ -350,6 +350,13 @@ FD_API size_t fd_plan_args_bytes(void);
  * memory shared with CUDA IPC (no multicast object). */
 #define FD_MAX_PEERS 8
 #define FD_IPC_HANDLE_BYTES 64
+/* Layout of one rank's allocation (fd_peer_alloc): u64 counters of its own
+ * steps at byte 0, u64 arrival flags [FD_MAX_PEERS] at FD_PEER_FLAGS_OFFSET
+ * (flag q = the last step whose partial rank q delivered here, written only
+ * by rank q), the fp32 receive slots [2 parities][world][slot] from
+ * FD_PEER_RECV_OFFSET. */
+#define FD_PEER_FLAGS_OFFSET 64
+#define FD_PEER_RECV_OFFSET 256
 
 typedef struct fd_peer_exchange {
   void *base[FD_MAX_PEERS]; /* rank q's allocation as mapped in this process:
@@ -371,8 +378,14 @@ FD_API int fd_peer_free(void *ptr);
 /* One step: every rank calls it once per step, in the same order, with the
  * same n / heads / head size / num_ctas (0: 32, at most 64).  send: this rank's packed
  * partial (16-byte aligned); out [n, H, D] in out_dtype; out_lse [H, n] or
- * NULL.  A wait longer than timeout_ns (0: 2 s) records FD_DEVERR_TIMEOUT
- * in *error and returns; the exchange must then be rebuilt. */
+ * NULL.  The step waits until every rank's own arrival flag (not a count of
+ * arrivals) has reached the step, so a peer that is a step ahead cannot
+ * complete another rank's step.  Launched as a programmatic dependent of the
+ * kernel ahead of it on the stream (it waits for that kernel before reading
+ * send).  A wait longer than timeout_ns (0: 2 s) records FD_DEVERR_TIMEOUT
+ * in *error and returns with the outputs unwritten; the caller must read the
+ * error word (fd_read_error) after each step it cannot otherwise vouch for,
+ * and after a timeout the exchange must be freed and rebuilt on every rank. */
 FD_API int fd_exchange_merge(const fd_peer_exchange *x, const float *send, int32_t n, int32_t num_heads,
                              int32_t head_size, void *out, int32_t out_dtype, float *out_lse, int32_t num_ctas,
                              int64_t timeout_ns, int32_t *error, void *stream);

@@ -183,14 +183,40 @@ def ref_decode_attn_f64(q, k_cache, v_cache, block_table, lens, scale):
     return out, lse
 
 
+def _cpu_flags() -> set[str]:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("flags"):
+                return set(ln.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def reference_ext_variant() -> str | None:
+    """Which compiled reference module load_reference_ext() takes: the
+    -march=native build (the reference loader's default, fastdecode/
+    cpu_ops.py:32-34) when this host's CPU has every flag of the CPU it was
+    built on, else the portable x86-64-v3 build; None when neither exists."""
+    native = REF_DIR / "fd_ref_cpu_attn_native.so"
+    flags = REF_DIR / "native_flags.txt"
+    if native.exists() and flags.exists():
+        need = set(flags.read_text().split())
+        if need and need <= _cpu_flags():
+            return "fd_ref_cpu_attn_native"
+    if (REF_DIR / "fd_ref_cpu_attn.so").exists():
+        return "fd_ref_cpu_attn"
+    return None
+
+
 def load_reference_ext():
     """The reference's compiled AVX2 module from oracle/_ref, or None."""
-    so = REF_DIR / "fd_ref_cpu_attn.so"
-    if not so.exists():
+    name = reference_ext_variant()
+    if name is None:
         return None
     if str(REF_DIR) not in sys.path:
         sys.path.insert(0, str(REF_DIR))
-    return importlib.import_module("fd_ref_cpu_attn")
+    return importlib.import_module(name)
 
 
 def rand_case(n, H, KVH, D, BS, C, dtype, max_len, seed):

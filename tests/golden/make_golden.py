@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run where the reference checkout exists (default /root/reference, override
-with FD_REFERENCE_DIR) after `make -C oracle` has compiled the reference's CPU
-kernel into oracle/_ref:
+Run where the reference checkout exists (FD_REFERENCE_DIR, else a directory
+named `reference` beside this repository) after `make -C oracle` has compiled
+the reference's CPU kernel into oracle/_ref:
 
     python tests/golden/make_golden.py
 
@@ -38,7 +38,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("FD_REFERENCE_DIR", "/root/reference"))
+REF = Path(os.environ.get("FD_REFERENCE_DIR") or Path(__file__).resolve().parents[3] / "reference")
+if not (REF / "fastdecode").is_dir():
+    sys.exit(f"reference checkout not found at {REF}: set FD_REFERENCE_DIR")
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(REF))
 

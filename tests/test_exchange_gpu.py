@@ -105,3 +105,69 @@ def test_silent_peer_times_out_without_fault():
         torch.cuda.synchronize()
         for p in bufs:
             lib.fd_peer_free(p)
+
+
+def test_peer_a_step_ahead_does_not_complete_a_missing_rank():
+    """World 3 on one GPU with two stand-in peer buffers: "rank 1" has already
+    delivered the next step (its arrival flag is one step ahead) and "rank 2"
+    never signals.  A count of arrivals would reach step x world and merge
+    rank 2's stale slot; the per-source flags must make the wait run out
+    (FD_DEVERR_TIMEOUT) and leave the outputs unwritten."""
+    from vllm_fastdecoder_b200 import _native as nat
+    from vllm_fastdecoder_b200 import gpu_ops
+
+    dev = torch.device("cuda")
+    lib = nat.load()
+    n, H, D, world = 2, 4, 64, 3
+    slot = (n * H * D + H * n + 3) // 4 * 4
+    nbytes = lib.fd_peer_buffer_bytes(world, slot)
+    # plain device buffers stand in for the three ranks' allocations (zeroed:
+    # counters, flags and slots start at 0, as fd_peer_alloc leaves them)
+    bufs = [torch.zeros(nbytes // 8 + 1, dtype=torch.int64, device=dev) for _ in range(world)]
+    flags0 = bufs[0][nat.PEER_FLAGS_OFFSET // 8: nat.PEER_FLAGS_OFFSET // 8 + nat.MAX_PEERS]
+    flags0[1] = 2  # rank 1 is a step ahead of this rank's first step
+    x = nat.FdPeerExchange()
+    x.rank, x.world, x.slot_floats = 0, world, slot
+    for q in range(world):
+        x.base[q] = bufs[q].data_ptr()
+    send = torch.ones(slot, dtype=torch.float32, device=dev)
+    out = torch.full((n, H, D), 7.0, dtype=torch.float16, device=dev)
+    lse = torch.full((H, n), 7.0, dtype=torch.float32, device=dev)
+    err = gpu_ops.error_word(dev)
+    nat.check(lib.fd_exchange_merge(ctypes.byref(x), send.data_ptr(), n, H, D, out.data_ptr(),
+                                    gpu_ops.dtype_code(out.dtype), lse.data_ptr(), 4, 50_000_000,
+                                    err.data_ptr(), gpu_ops._stream(dev)), "fd_exchange_merge")
+    with pytest.raises(RuntimeError, match="device error 3"):
+        gpu_ops.check_device_errors(dev)
+    assert bool((out == 7.0).all()) and bool((lse == 7.0).all())
+    # this rank did deliver: its flag of step 1 is in every rank's buffer
+    for q in range(world):
+        assert int(bufs[q][nat.PEER_FLAGS_OFFSET // 8]) == 1
+    torch.cuda.synchronize()
+
+
+def test_check_marks_a_timed_out_exchange_unusable():
+    """PeerExchange.check() reads the error word after a step: a step that
+    timed out (here: a stand-in rank 1 that never delivers) makes check()
+    raise, and every later step is refused until the exchange is rebuilt."""
+    from vllm_fastdecoder_b200 import _native as nat
+    from vllm_fastdecoder_b200 import sharded
+
+    dev = torch.device("cuda")
+    n, H, D = 3, 8, 64
+    ex = sharded.PeerExchange(n, H, D, 1, dev, num_ctas=4, timeout_s=0.05)
+    fake = torch.zeros(ex._lib.fd_peer_buffer_bytes(2, ex.slot) // 8 + 1, dtype=torch.int64, device=dev)
+    try:
+        x = nat.FdPeerExchange()
+        x.rank, x.world, x.slot_floats = 0, 2, ex.slot
+        x.base[0], x.base[1] = ex.x.base[0], fake.data_ptr()
+        ex.x = x  # as if rank 1 had mapped its buffer and then stopped
+        final = torch.zeros(n, H, D, dtype=torch.bfloat16, device=dev)
+        ex.exchange_and_merge(None, None, final)
+        with pytest.raises(RuntimeError, match="device error 3"):
+            ex.check()
+        with pytest.raises(RuntimeError, match="unusable"):
+            ex.exchange_and_merge(None, None, final)
+    finally:
+        torch.cuda.synchronize()
+        ex.close()

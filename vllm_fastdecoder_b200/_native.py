@@ -86,6 +86,8 @@ class FdPlanArgs(ctypes.Structure):
 
 MAX_PEERS = 8  # FD_MAX_PEERS
 IPC_HANDLE_BYTES = 64  # FD_IPC_HANDLE_BYTES
+PEER_FLAGS_OFFSET = 64  # FD_PEER_FLAGS_OFFSET
+PEER_RECV_OFFSET = 256  # FD_PEER_RECV_OFFSET
 
 
 class FdPeerExchange(ctypes.Structure):

@@ -645,6 +645,7 @@ __global__ void fd_split_merge_kernel(const __grid_constant__ DecodeParams p, in
 // 1; every later one into slot 0.
 __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParams p, int D) {
   griddep_wait();  // launched early (programmatic dependent launch): the decode's partials first
+  griddep_launch_dependents();  // a dependent (the sharded exchange) may launch and wait for this grid
   const int* P = p.ws_prefix;
   const int Y = p.KVH * p.gcs;
   const int64_t N = p.ncta;

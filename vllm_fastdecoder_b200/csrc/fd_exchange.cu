@@ -4,32 +4,41 @@
 //
 // Each rank owns one device allocation, mapped into every other rank's
 // process with CUDA IPC (plain device memory: no multicast object, no NVLS):
-//   [0]   arrival counter   u64, incremented once per step by every rank
-//                            (red.release.sys)
-//   [8]   step counter      u64, this rank's completed steps
-//   [16]  CTA counter       u64, this rank's finished CTAs
-//   [24]  push counter      u64, this rank's CTAs done pushing
+//   [0]   step counter      u64, this rank's completed steps
+//   [8]   CTA counter       u64, this rank's finished CTAs
+//   [16]  push counter      u64, this rank's CTAs done pushing
+//   [64]  arrival flags     u64 [FD_MAX_PEERS]: flag q holds the last step
+//                            whose slot rank q has delivered into this
+//                            buffer (written only by rank q, st.release.sys)
 //   [256] receive buffer    fp32 [2 parities][world][slot], slot = the packed
 //                            partial [o (n*H*D) | lse (H*n)] rounded to 4
-// One launch per step of at most 32 small CTAs, which the SMs hold at once
+// One launch per step of at most 64 small CTAs, which the SMs hold at once
 // (every wait is bounded in any case):
 //   1. every CTA stores its share of the rank's packed partial into slot
 //      [parity][rank] of every rank's receive buffer (16-byte stores over
 //      NVLink; the own copy is local), fences at system scope and counts
 //      itself on the rank's push counter; the last CTA of the rank fences
-//      again and adds 1 to every rank's arrival counter (world remote
-//      atomics per rank and step: one signal per CTA and rank made 256
-//      contending atomics per counter at 8 ranks, slower than NCCL);
-//   2. it waits (bounded, %globaltimer) until its own counter reaches
-//      step * world: every rank's slot has landed;
+//      again and writes the step into flag [rank] of every rank's buffer
+//      (world remote release stores per rank and step);
+//   2. it waits (bounded, %globaltimer) until every flag of its own buffer
+//      holds at least the step: each rank's slot of this step has landed.
+//      Per-source flags, not one summed counter: a peer that is already a
+//      step ahead must not stand in for a rank whose signal of this step is
+//      still in flight;
 //   3. it merges its (row, head) pairs from the receive buffer with the
 //      log-sum-exp rule of fd_merge_partials, same operations in the same
 //      order (so the result equals the NCCL path bit for bit);
 //   4. the last CTA to finish advances the step counter, so the next launch
-//      (or graph replay) uses the other parity and the next target count.
+//      (or graph replay) uses the other parity and the next step number.
 // Double buffering by parity keeps a rank that is one step ahead from
 // overwriting a slot another rank is still merging; it cannot get two steps
-// ahead, because finishing a step needs every rank's shares of that step.
+// ahead, because finishing a step needs every rank's flag of that step, and
+// a rank raises its flag of step s + 1 only after its merge of step s ended.
+//
+// The kernel is launched as a programmatic dependent of the kernel before it
+// on the stream (the decode's combine): its launch overlaps that kernel's
+// tail, and griddepcontrol.wait holds every CTA until the partial it pushes
+// is complete.
 
 #include <math.h>
 #include <stdint.h>
@@ -43,7 +52,8 @@ namespace fdk {
 struct ExchangeParams {
   const float* send;                      // [slot] this rank's packed partial
   float* recv[FD_MAX_PEERS];              // rank q's receive buffer (mapped)
-  unsigned long long* arrive[FD_MAX_PEERS];  // rank q's arrival counter (mapped)
+  unsigned long long* flag_at[FD_MAX_PEERS];  // this rank's arrival flag in rank q's buffer (mapped)
+  const unsigned long long* flags;        // this rank's arrival flags [world]
   unsigned long long* step;               // this rank's step counter
   unsigned long long* done;               // this rank's finished-CTA counter
   unsigned long long* pushed;             // this rank's CTAs done pushing
@@ -62,8 +72,8 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-__device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ float lse_or_empty(float x) { return x == INFINITY ? -INFINITY : x; }
@@ -71,6 +81,7 @@ __device__ __forceinline__ float lse_or_empty(float x) { return x == INFINITY ? 
 __global__ void fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams p) {
   __shared__ unsigned long long s_step;
   __shared__ int s_ok;
+  griddep_wait();  // the partial in p.send is complete (programmatic dependent launch)
   if (threadIdx.x == 0) {
     s_step = *reinterpret_cast<volatile unsigned long long*>(p.step) + 1;
     s_ok = 1;
@@ -89,22 +100,24 @@ __global__ void fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams 
   }
   __syncthreads();  // the CTA's stores happen before thread 0's fence and release
 
-  // 2. the rank's last CTA to finish pushing announces the rank to every
-  // rank; then every CTA waits for every rank
+  // 2. the rank's last CTA to finish pushing raises the rank's flag in every
+  // rank's buffer; then every CTA waits for every rank's flag of this step
   if (threadIdx.x == 0) {
     __threadfence_system();
     const unsigned long long prev = atomicAdd(p.pushed, 1ull);
     if (prev + 1 == step * gridDim.x) {
-      __threadfence_system();  // the other CTAs' fenced stores happen before the signal
-      for (int q = 0; q < p.world; ++q) red_add_release_sys(p.arrive[q], 1ull);
+      __threadfence_system();  // the other CTAs' fenced stores happen before the flags
+      for (int q = 0; q < p.world; ++q) st_release_sys(p.flag_at[q], step);
     }
-    const unsigned long long want = step * (unsigned long long)p.world;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 1; ld_acquire_sys(p.arrive[p.rank]) < want; ++it) {
-      if ((it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
-        set_error(p.err, FD_DEVERR_TIMEOUT);
-        s_ok = 0;
-        break;
+    uint32_t it = 0;
+    for (int q = 0; q < p.world && s_ok; ++q) {
+      while (ld_acquire_sys(p.flags + q) < step) {
+        if ((++it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
+          set_error(p.err, FD_DEVERR_TIMEOUT);
+          s_ok = 0;
+          break;
+        }
       }
     }
   }
@@ -168,7 +181,12 @@ __global__ void fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams 
 }  // namespace fdk
 
 namespace {
+constexpr size_t kStepOffset = 0;
+constexpr size_t kDoneOffset = 8;
+constexpr size_t kPushedOffset = 16;
+constexpr size_t kFlagsOffset = 64;
 constexpr size_t kRecvOffset = 256;
+static_assert(kFlagsOffset + 8 * FD_MAX_PEERS <= kRecvOffset, "arrival flags overlap the receive buffer");
 }
 
 extern "C" size_t fd_peer_buffer_bytes(int32_t world, int64_t slot_floats) {
@@ -236,15 +254,16 @@ extern "C" int fd_exchange_merge(const fd_peer_exchange* x, const float* send, i
   if (ctas > 64) return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: at most 64 CTAs (%d)", ctas);
   fdk::ExchangeParams p{};
   p.send = send;
+  unsigned char* own = static_cast<unsigned char*>(x->base[x->rank]);
   for (int q = 0; q < x->world; ++q) {
     unsigned char* b = static_cast<unsigned char*>(x->base[q]);
     p.recv[q] = reinterpret_cast<float*>(b + kRecvOffset);
-    p.arrive[q] = reinterpret_cast<unsigned long long*>(b);
+    p.flag_at[q] = reinterpret_cast<unsigned long long*>(b + kFlagsOffset) + x->rank;
   }
-  unsigned char* own = static_cast<unsigned char*>(x->base[x->rank]);
-  p.step = reinterpret_cast<unsigned long long*>(own + 8);
-  p.done = reinterpret_cast<unsigned long long*>(own + 16);
-  p.pushed = reinterpret_cast<unsigned long long*>(own + 24);
+  p.flags = reinterpret_cast<const unsigned long long*>(own + kFlagsOffset);
+  p.step = reinterpret_cast<unsigned long long*>(own + kStepOffset);
+  p.done = reinterpret_cast<unsigned long long*>(own + kDoneOffset);
+  p.pushed = reinterpret_cast<unsigned long long*>(own + kPushedOffset);
   p.rank = x->rank;
   p.world = x->world;
   p.n = n;
@@ -260,7 +279,20 @@ extern "C" int fd_exchange_merge(const fd_peer_exchange* x, const float* send, i
   // co-residency but cost ~55 us per step on B200 (measured); at most 64
   // CTAs of 256 threads and no shared memory are resident together on an
   // otherwise idle stream, and the bounded wait turns any exception into
-  // FD_DEVERR_TIMEOUT rather than a hang.
-  fdk::fd_exchange_merge_kernel<<<ctas, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  // FD_DEVERR_TIMEOUT rather than a hang.  Programmatic dependent launch:
+  // the CTAs may start while the kernel ahead on the stream finishes and
+  // wait for it in griddepcontrol.wait.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3((unsigned)kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fdk::fd_exchange_merge_kernel, p);
+  if (e != cudaSuccess) return fdh::cuda_status(e, "fd_exchange_merge_kernel launch");
   return fdh::cuda_status(cudaGetLastError(), "fd_exchange_merge_kernel launch");
 }

@@ -107,6 +107,12 @@ def host_device_pointer(t: torch.Tensor) -> int:
     return _HOST_PTR[base] + (t.data_ptr() - base)
 
 
+def forget_host_pointer(t: torch.Tensor) -> None:
+    """Drop the cached device address of t's storage (its memory is about to
+    be unregistered)."""
+    _HOST_PTR.pop(t.untyped_storage().data_ptr(), None)
+
+
 # ------------------------------------------------------------- KV tiers
 
 

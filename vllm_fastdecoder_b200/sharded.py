@@ -97,7 +97,13 @@ class PeerExchange:
     o_view / lse_view are views of the packed send buffer the decode kernel
     writes; exchange_and_merge(final) runs one launch that needs every rank
     to call it for the same step.  Build it collectively (every rank of the
-    group) after torch.cuda.set_device; close() collectively too."""
+    group) after torch.cuda.set_device; close() collectively too.
+
+    A step whose bounded wait ran out (a rank that never delivered) records
+    FD_DEVERR_TIMEOUT in the device error word and leaves `final` unwritten;
+    the launch itself reports nothing.  check() reads the word (a host
+    synchronisation): after a timeout it marks the exchange unusable, so
+    later steps raise until every rank closes it and builds a new one."""
 
     def __init__(self, n: int, H: int, D: int, world: int, device: torch.device, group=None, num_ctas: int = 32,
                  timeout_s: float = 2.0):
@@ -137,6 +143,7 @@ class PeerExchange:
             x.base[q] = p.value
             self._opened.append(p.value)
         self.x = x
+        self.failed: str | None = None
         if world > 1:
             dist.barrier(group=group)  # every rank mapped before the first step
 
@@ -150,12 +157,27 @@ class PeerExchange:
 
         del o_local_unused, lse_local_unused
         nat = self._nat
+        if self.failed is not None:
+            raise RuntimeError(f"PeerExchange is unusable after a failed step ({self.failed}): close it on every "
+                               "rank and build a new one")
         if not (final.is_contiguous() and tuple(final.shape) == (self.n, self.H, self.D)):
             raise RuntimeError("PeerExchange: final must be a contiguous [n, H, D] tensor")
         nat.check(self._lib.fd_exchange_merge(
             ctypes.byref(self.x), self.send.data_ptr(), self.n, self.H, self.D, final.data_ptr(),
             gpu_ops.dtype_code(final.dtype), self.lse_out.data_ptr(), self.num_ctas, self.timeout_ns,
             gpu_ops.error_word(self.device).data_ptr(), gpu_ops._stream(self.device)), "fd_exchange_merge")
+
+    def check(self) -> None:
+        """Synchronise and read the device error word of this rank's GPU;
+        raise RuntimeError (and refuse every later step) if a kernel flagged
+        an error, e.g. a step that timed out waiting for a rank."""
+        from vllm_fastdecoder_b200 import gpu_ops
+
+        try:
+            gpu_ops.check_device_errors(self.device)
+        except RuntimeError as e:
+            self.failed = str(e)
+            raise
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (collective)."""
