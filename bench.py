@@ -450,6 +450,32 @@ def run_ours(args, ws, rank, device):
     torch.cuda.synchronize(device)
     elapsed_eager = t_start.elapsed_time(t_end) * 1e-3
     copy_t = (sum(c0.elapsed_time(c1) for c0, c1 in cevs) * 1e-3 / args.steps) if staged else 0.0
+    phases = None
+    if gather is not None:
+        # per-phase device time of eager sharded steps (outside the timed
+        # regions): decode kernel, its combine, the exchange + merge (which
+        # includes waiting for the slowest rank)
+        pev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        for k in range(args.steps):
+            e = pev[k]
+            e[0].record()
+            gpu_ops.launch_decode(a, device, "partials")
+            e[1].record()
+            if has_combine:
+                gpu_ops.launch_decode(a, device, "combine")
+            e[2].record()
+            gather.exchange_and_merge(out, lse, final)
+            e[3].record()
+        torch.cuda.synchronize(device)
+        ph = torch.tensor([sum(e[j].elapsed_time(e[j + 1]) for e in pev) / args.steps for j in range(3)],
+                          dtype=torch.float64, device=device)
+        lo, hi = ph.clone(), ph.clone()
+        torch.distributed.all_reduce(lo, op=torch.distributed.ReduceOp.MIN)
+        torch.distributed.all_reduce(hi, op=torch.distributed.ReduceOp.MAX)
+        phases = {nm: {"min_ms": round(float(lo[j]), 4), "max_ms": round(float(hi[j]), 4)}
+                  for j, nm in enumerate(("decode", "combine", "exchange_merge"))}
+        phases["note"] = ("eager steps, CUDA events per rank; min / max over ranks; exchange_merge includes the "
+                          "wait for the slowest rank")
     # the timed region of `value`: K graph replays (or the eager steps above).
     # A short step makes K steps shorter than nvidia-smi's sampling period,
     # so the sampler starts under an untimed pre-roll of replays (~0.3 s of
@@ -603,6 +629,8 @@ def run_ours(args, ws, rank, device):
     }
     if parity is not None:
         line["parity"] = parity
+    if phases is not None:
+        line["run"]["phases"] = phases
     if graph is not None:
         graph.reset()  # a graph holding NCCL calls goes before the process group does
     if gather is not None and hasattr(gather, "close"):

@@ -200,8 +200,10 @@ FD_API int fd_decode_attn_combine(const fd_decode_args *a, void *stream);
  * before anything is launched; a larger tiles_per_split needs less scratch.
  *
  * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress, with that device current) and caches it; make that
- * first call before any stream capture.  All calls share the one array and it
+ * (cudaGetSymbolAddress, with that device current) and caches it with the
+ * CUDA context it belongs to; make that first call before any stream
+ * capture.  A context torn down and created again (cudaDeviceReset) is seen
+ * by the next call, which looks the address up again.  All calls share the one array and it
  * keeps the last call's contents; nothing in it needs to start at zero (every
  * partial, and the row-tile prefix, is written by the decode kernel before
  * the combine kernel of the same call reads it).  Calls whose

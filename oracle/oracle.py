@@ -110,24 +110,46 @@ def _tier(k: torch.Tensor | None, v: torch.Tensor | None):
     return t
 
 
-def decode_attn_tiered(q, tier0, tier1, split, block_table, lens, scale, out, lse=None) -> None:
+def decode_attn_tiered(q, tier0, tier1, split, block_table, lens, scale, out, lse=None, threads: int = 1) -> None:
     """Two-tier version: tier0/tier1 are (k, v) views [B, KVH, BS, D] (any
     strides, contiguous last dim) or None; ids < split -> tier0, else tier1
-    at id - split.  out [n,H,D] of q's dtype or fp32; lse [H,n] or None."""
+    at id - split.  out [n,H,D] of q's dtype or fp32; lse [H,n] or None.
+    threads > 1 splits the rows over host threads (each row is computed by
+    one call of the same C code, so the result does not depend on it)."""
     n, H, D = q.shape
     t0 = _tier(*tier0) if tier0 is not None else None
     t1 = _tier(*tier1) if tier1 is not None else None
     ref = tier0 if tier0 is not None else tier1
     KVH, BS = ref[0].shape[1], ref[0].shape[2]
-    rc = lib().fdo_decode_attn(
-        q.data_ptr(), q.stride(0), q.stride(1), ctypes.byref(t0) if t0 else None,
-        ctypes.byref(t1) if t1 else None, int(split), block_table.data_ptr(), block_table.stride(0),
-        block_table.shape[1], lens.data_ptr(), n, H, KVH, D, BS, float(scale), _CODE[q.dtype],
-        out.data_ptr(), _CODE[out.dtype], out.stride(0), out.stride(1),
-        lse.data_ptr() if lse is not None else None,
-        lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0)
-    if rc != 0:
-        raise RuntimeError(f"oracle decode_attn_tiered: error {rc}")
+    assert block_table.stride(1) == 1 and lens.is_contiguous()
+    qe, oe = q.element_size(), out.element_size()
+
+    def run(i0: int, i1: int) -> int:
+        return lib().fdo_decode_attn(
+            q.data_ptr() + i0 * q.stride(0) * qe, q.stride(0), q.stride(1), ctypes.byref(t0) if t0 else None,
+            ctypes.byref(t1) if t1 else None, int(split), block_table.data_ptr() + i0 * block_table.stride(0) * 4,
+            block_table.stride(0), block_table.shape[1], lens.data_ptr() + i0 * 4, i1 - i0, H, KVH, D, BS,
+            float(scale), _CODE[q.dtype], out.data_ptr() + i0 * out.stride(0) * oe, _CODE[out.dtype], out.stride(0),
+            out.stride(1), lse.data_ptr() + i0 * lse.stride(1) * 4 if lse is not None else None,
+            lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0)
+
+    if threads <= 1 or n <= 1:
+        rcs = [run(0, n)]
+    else:
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(max_workers=min(threads, n)) as ex:  # ctypes calls release the GIL
+            rcs = list(ex.map(lambda i: run(i, i + 1), range(n)))
+    bad = [rc for rc in rcs if rc != 0]
+    if bad:
+        raise RuntimeError(f"oracle decode_attn_tiered: error {bad[0]}")
+
+
+def host_threads() -> int:
+    """Threads the tests give the oracle (all of this host's cores)."""
+    import os
+
+    return os.cpu_count() or 1
 
 
 def store_kv(k, v, slots, k_cache, v_cache) -> None:

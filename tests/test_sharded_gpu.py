@@ -1,11 +1,11 @@
-"""KV-sharded decode on 2 GPUs: each rank decodes its contiguous shard of
+"""KV-sharded decode on 2, 4 and 8 GPUs: each rank decodes its contiguous shard of
 every row with the split-KV kernel into the packed exchange buffer; the
 partials are exchanged and merged either with NCCL (all-gather, then
 fd_merge_partials) or over peer memory (fd_exchange_merge: one kernel,
 CUDA-IPC buffers, no multicast).  Both must match the oracle over the
 unsharded rows (bf16 output 1.6e-2, lse 1e-4) and each other bit for bit,
 over three consecutive steps (both parities of the peer buffers).  NVLS is
-off.  Skipped with fewer than 2 GPUs."""
+off.  Each world size is skipped on a box with fewer GPUs."""
 
 from __future__ import annotations
 
@@ -80,11 +80,12 @@ def _rank(rank, world, port, path):
         dist.destroy_process_group()
 
 
-def test_sharded_decode_two_gpus(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_decode_on_several_gpus(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     path = str(tmp_path / "res.pt")
-    mp.start_processes(_rank, args=(2, _free_port(), path), nprocs=2, start_method="spawn")
+    mp.start_processes(_rank, args=(world, _free_port(), path), nprocs=world, start_method="spawn")
     res = torch.load(path)
     q, kc, vc, bt, lens = _case()
     D = q.shape[2]

@@ -5,9 +5,13 @@ device memory through its own allocator).  It keeps its split partials in a
 scratch array built into the library instead of a caller workspace.
 
 The checks call both entry points through the C ABI on the same arguments and
-require the same output, on two calls in a row with different batches (so a
-call cannot lean on what the previous one left in the shared scratch), and
-that arguments needing more scratch than the array holds are refused.  This
+require the same output, and the C oracle's (the restatement of the reference
+decode_attn) within the decode tests' tolerances, on two calls in a row with
+different batches (so a call cannot lean on what the previous one left in the
+shared scratch).  Both schedules are covered: the split grid (fixed
+tiles_per_split) and the default persistent schedule, on the CUDA-core kernel
+(fp16 MHA) and the tensor-core kernel (bf16, 32 query heads over 8 kv heads).
+Arguments needing more scratch than the array holds must be refused.  This
 file is collected last so that a run stopping at the first failure has run
 every other test first; it also passes alone in a fresh process.
 """
@@ -37,17 +41,22 @@ def _batch(dtype, H, KVH, seed, max_len):
     return q, kc, vc, bt, lens
 
 
-def _args(q, kc, vc, bt, lens, out, lse):
+def _args(q, kc, vc, bt, lens, out, lse, tiles_per_split=8):
     from vllm_fastdecoder_b200 import gpu_ops
     from vllm_fastdecoder_b200.gpu_ops import KVTier
 
     D = q.shape[-1]
     return gpu_ops.decode_args(q, (KVTier(kc, vc), None), 1 << 40, bt, lens, 1.0 / math.sqrt(D), out, lse,
-                               tiles_per_split=8)
+                               tiles_per_split=tiles_per_split)
 
 
-@pytest.mark.parametrize("dtype,H,KVH", [(torch.float16, 8, 8), (torch.bfloat16, 16, 4)])
-def test_noalloc_matches_workspace_entry_point_twice(dtype, H, KVH):
+@pytest.mark.parametrize("dtype,H,KVH,tps,kernel", [
+    (torch.float16, 8, 8, 8, "fd_decode_kernel"),  # split grid
+    (torch.bfloat16, 16, 4, 8, "fd_decode_kernel"),
+    (torch.float16, 8, 8, 0, "fd_decode_kernel"),  # persistent schedule, CUDA cores
+    (torch.bfloat16, 32, 8, 0, "fd_decode_mma_kernel"),  # persistent schedule, tensor cores
+])
+def test_noalloc_matches_workspace_entry_point_and_oracle_twice(dtype, H, KVH, tps, kernel):
     from vllm_fastdecoder_b200 import _native as nat
     from vllm_fastdecoder_b200 import gpu_ops
 
@@ -55,24 +64,32 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, H, KVH):
     dev = torch.device("cuda")
     stream = torch.cuda.current_stream(dev).cuda_stream
     for call, (seed, max_len) in enumerate([(1, 3000), (2, 1700)]):
-        q, kc, vc, bt, lens = (t.to(dev) for t in _batch(dtype, H, KVH, seed, max_len))
+        q_c, kc_c, vc_c, bt_c, lens_c = _batch(dtype, H, KVH, seed, max_len)
+        q, kc, vc, bt, lens = (t.to(dev) for t in (q_c, kc_c, vc_c, bt_c, lens_c))
         n, _, D = q.shape
+        assert gpu_ops.decode_kernel_name(dtype, D, H, KVH, kc.shape[2], n, tps) == kernel
         out_ws = torch.full((n, H, D), float("nan"), dtype=dtype, device=dev)
         lse_ws = torch.full((H, n), float("nan"), device=dev)
-        a = _args(q, kc, vc, bt, lens, out_ws, lse_ws)
+        a = _args(q, kc, vc, bt, lens, out_ws, lse_ws, tps)
         assert lib.fd_decode_workspace_size(ctypes.byref(a)) > 0, "case must use split scratch"
         nat.check(lib.fd_decode_attn(ctypes.byref(a), stream), "fd_decode_attn")
 
         out_na = torch.full((n, H, D), float("nan"), dtype=dtype, device=dev)
         lse_na = torch.full((H, n), float("nan"), device=dev)
-        b = _args(q, kc, vc, bt, lens, out_na, lse_na)
+        b = _args(q, kc, vc, bt, lens, out_na, lse_na, tps)
         b.workspace = None
         b.workspace_bytes = 0
         nat.check(lib.fd_decode_attn_noalloc(ctypes.byref(b), stream), f"fd_decode_attn_noalloc (call {call})")
         torch.cuda.synchronize(dev)
         gpu_ops.check_device_errors(dev)
 
-        nz = lens.cpu() > 0
+        ref = torch.empty(n, H, D, dtype=dtype)
+        ref_l = torch.empty(H, n)
+        O.decode_attn(q_c, kc_c, vc_c, bt_c, lens_c, 1.0 / math.sqrt(D), ref, ref_l)
+        nz = lens_c > 0
+        for out, lse in ((out_na, lse_na), (out_ws, lse_ws)):
+            assert (out.cpu().float() - ref.float()).abs().max().item() <= TOL[dtype]
+            assert (lse.cpu()[:, nz] - ref_l[:, nz]).abs().max().item() <= LSE_TOL
         torch.testing.assert_close(out_na.cpu().float(), out_ws.cpu().float(), atol=TOL[dtype], rtol=TOL[dtype])
         assert (lse_na.cpu()[:, nz] - lse_ws.cpu()[:, nz]).abs().max().item() <= LSE_TOL
         assert torch.all(out_na.cpu()[~nz] == 0) and torch.all(torch.isneginf(lse_na.cpu()[:, ~nz]))

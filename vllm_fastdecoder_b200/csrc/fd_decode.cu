@@ -1211,23 +1211,58 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[FD_NOALLOC_SCRA
 
 namespace {
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device ordinal
+// Device address of g_noalloc_scratch per device ordinal, with the CUDA
+// context it was looked up in: a context torn down and created again
+// (cudaDeviceReset) loads the module afresh, so the address is looked up
+// again whenever the current context differs from the cached one.
+struct NoallocSlot {
+  void* ctx;
+  void* addr;
+};
+NoallocSlot g_noalloc_slot[64] = {};
 
-// Device address of the scratch on the current device, looked up on the first
-// call for that device (with the device current) and cached.
+typedef CUresult (*ctx_get_current_fn)(CUcontext*);
+
+ctx_get_current_fn ctx_get_current() {
+  static ctx_get_current_fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<ctx_get_current_fn>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// Device address of the scratch on the current device: looked up with the
+// device current on the first call in each CUDA context, then cached.
 int noalloc_scratch(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fdh::cuda_status(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fdh::fail(FD_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  CUcontext ctx = nullptr;
+  ctx_get_current_fn get = ctx_get_current();
+  if (get == nullptr || get(&ctx) != CUDA_SUCCESS)
+    return fdh::fail(FD_ERR_CUDA, "fd_decode_attn_noalloc: cuCtxGetCurrent unavailable");
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  if (slot.addr == nullptr || ctx == nullptr || slot.ctx != static_cast<void*>(ctx)) {
+    // no context current on this thread yet, or another one than the cached
+    // address belongs to: the lookup makes the device's context current
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return fdh::cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
-    g_noalloc_addr[dev] = p;
+    if (get(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return fdh::fail(FD_ERR_CUDA, "fd_decode_attn_noalloc: no current CUDA context");
+    slot.ctx = static_cast<void*>(ctx);
+    slot.addr = p;
   }
-  *out = g_noalloc_addr[dev];
+  *out = slot.addr;
   return FD_OK;
 }
 }  // namespace

@@ -8,6 +8,13 @@
 // first and, if any is outside both tiers, nothing is written and the error
 // word gets FD_DEVERR_SLOT.  slot < 0 means "not this call's" and is skipped,
 // like reshape_and_cache_flash.
+//
+// The all-or-nothing check makes every CTA read all m slots, so the grid is
+// kept to at most two CTAs of 512 threads per SM (a prefill-sized m = 16k
+// reads ~40 MB of slots from L2 in all, not the ~150 MB of one CTA per 256
+// chunks), the scan reads two slots per 16-byte load, and the copy keeps two
+// 16-byte loads of K and V in flight per thread so the few CTAs still stream
+// at HBM rate.
 
 #include "fd_common.cuh"
 #include "fd_internal.h"
@@ -28,48 +35,70 @@ struct StoreParams {
   int32_t* err;
 };
 
-__global__ void fd_store_kv_kernel(const __grid_constant__ StoreParams p) {
-  __shared__ int bad;
-  if (threadIdx.x == 0) bad = 0;
-  __syncthreads();
-  for (int j = threadIdx.x; j < p.m; j += blockDim.x) {
-    const int64_t s = p.slots[j];
-    if (s < 0) continue;
+constexpr int kStoreThreads = 512;
+constexpr int kStoreUnroll = 2;
+
+__global__ void __launch_bounds__(kStoreThreads, 2) fd_store_kv_kernel(const __grid_constant__ StoreParams p) {
+  auto out_of_range = [&](int64_t s) -> bool {
+    if (s < 0) return false;
     int64_t b = s / p.BS;
     int t = 0;
     if (b >= p.split) {
       t = 1;
       b -= p.split;
     }
-    if (b >= p.nblk[t]) bad = 1;
+    return b >= p.nblk[t];
+  };
+  // slots are 8-byte aligned; pairs from a 16-byte boundary, the odd one out alone
+  const int lead = (reinterpret_cast<uintptr_t>(p.slots) & 15u) ? 1 : 0;
+  bool mine = false;
+  if (lead && threadIdx.x == 0 && p.m > 0) mine = out_of_range(p.slots[0]);
+  const int pairs = (p.m - lead) / 2;
+  const longlong2* sp = reinterpret_cast<const longlong2*>(p.slots + lead);
+  for (int j = threadIdx.x; j < pairs; j += blockDim.x) {
+    const longlong2 v = sp[j];
+    mine |= out_of_range(v.x) | out_of_range(v.y);
   }
-  __syncthreads();
-  if (bad) {
+  if (threadIdx.x == 0 && lead + 2 * pairs < p.m) mine |= out_of_range(p.slots[p.m - 1]);
+  if (__syncthreads_or(mine ? 1 : 0)) {
     if (blockIdx.x == 0 && threadIdx.x == 0) set_error(p.err, FD_DEVERR_SLOT);
     return;
   }
-  const int64_t per_row = (int64_t)p.KVH * p.nch;
-  const int64_t total = (int64_t)p.m * per_row;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t j = idx / per_row;
-    const int64_t rem = idx - j * per_row;
-    const int64_t h = rem / p.nch;
-    const int64_t c = rem - h * p.nch;
-    const int64_t s = p.slots[j];
-    if (s < 0) continue;
-    int64_t b = s / p.BS;
-    const int64_t off = s - b * p.BS;
-    int t = 0;
-    if (b >= p.split) {
-      t = 1;
-      b -= p.split;
+  // 32-bit chunk indices (the host refuses calls of 2^31 chunks or more)
+  const uint32_t per_row = (uint32_t)p.KVH * (uint32_t)p.nch;
+  const uint32_t total = (uint32_t)p.m * per_row;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < total; base += stride * kStoreUnroll) {
+    uint4 kv[kStoreUnroll], vv[kStoreUnroll];
+    int64_t dst[kStoreUnroll];
+    int tier[kStoreUnroll];
+#pragma unroll
+    for (int u = 0; u < kStoreUnroll; ++u) {
+      const uint32_t idx = base + u * stride;
+      dst[u] = -1;
+      tier[u] = 0;
+      if (idx >= total) continue;
+      const uint32_t j = idx / per_row;
+      const uint32_t rem = idx - j * per_row;
+      const uint32_t h = rem / (uint32_t)p.nch;
+      const uint32_t c = rem - h * (uint32_t)p.nch;
+      const int64_t s = p.slots[j];
+      if (s < 0) continue;
+      int64_t b = s / p.BS;
+      const int64_t off = s - b * p.BS;
+      const int t = b >= p.split ? 1 : 0;
+      if (t) b -= p.split;
+      tier[u] = t;
+      dst[u] = b * p.blk_sb[t] + (int64_t)h * p.head_sb[t] + off * p.tok_sb[t] + c * 16;
+      kv[u] = *reinterpret_cast<const uint4*>(p.key + j * p.k_sn + h * p.k_sh + c * 16);
+      vv[u] = *reinterpret_cast<const uint4*>(p.value + j * p.v_sn + h * p.v_sh + c * 16);
     }
-    const int64_t dst = b * p.blk_sb[t] + h * p.head_sb[t] + off * p.tok_sb[t] + c * 16;
-    const uint4 kv = *reinterpret_cast<const uint4*>(p.key + j * p.k_sn + h * p.k_sh + c * 16);
-    const uint4 vv = *reinterpret_cast<const uint4*>(p.value + j * p.v_sn + h * p.v_sh + c * 16);
-    *reinterpret_cast<uint4*>(p.tk[t] + dst) = kv;
-    *reinterpret_cast<uint4*>(p.tv[t] + dst) = vv;
+#pragma unroll
+    for (int u = 0; u < kStoreUnroll; ++u) {
+      if (dst[u] < 0) continue;
+      *reinterpret_cast<uint4*>(p.tk[tier[u]] + dst[u]) = kv[u];
+      *reinterpret_cast<uint4*>(p.tv[tier[u]] + dst[u]) = vv[u];
+    }
   }
 }
 
@@ -122,9 +151,15 @@ extern "C" int fd_store_kv(const void* key, int64_t key_stride_n, int64_t key_st
     }
   }
   const int64_t total = (int64_t)m * num_kv_heads * p.nch;
-  const int threads = 256;
-  int64_t blocks = (total + threads - 1) / threads;
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (total >= (int64_t)1 << 31)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "fd_store_kv: %lld 16-byte chunks in one call (at most 2^31 - 1)",
+                     (long long)total);
+  const int threads = fdk::kStoreThreads;
+  int dev = 0, sms = 0;
+  const int st = fdh::device_sms(&dev, &sms);
+  if (st != FD_OK) return st;
+  int64_t blocks = (total + (int64_t)threads * fdk::kStoreUnroll - 1) / ((int64_t)threads * fdk::kStoreUnroll);
+  if (blocks > 2 * (int64_t)sms) blocks = 2 * (int64_t)sms;  // every CTA scans all slots: few, wide CTAs
   fdk::fd_store_kv_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return fdh::cuda_status(cudaGetLastError(), "fd_store_kv_kernel launch");
 }

@@ -1,4 +1,4 @@
-"""CUDA-graph capture of a decode-only step (the survey's "next" row 3).
+"""CUDA-graph capture of a decode-only step.
 
 A decode-only step needs nothing from the host once the device planner has
 run (fd_plan_step: plan and decode list on the GPU), so the whole step over
