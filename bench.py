@@ -356,7 +356,7 @@ def run_ours(args, ws, rank, device):
     if sharded:
         from vllm_fastdecoder_b200 import sharded as sh
 
-        gather = (sh.PeerExchange(n, H, D, ws, device) if args.exchange == "peer"
+        gather = (sh.PeerExchange(n, H, D, ws, device) if args.exchange in ("peer", "peer-split")
                   else sh.PartialExchange(n, H, D, ws, device))
         final = torch.empty(n, H, D, dtype=batch.dtype, device=device)
         out, lse = gather.o_view, gather.lse_view
@@ -377,6 +377,16 @@ def run_ours(args, ws, rank, device):
     a = gpu_ops.decode_args(res.q, dec_tiers, dec_split, res.block_table, res.lens, batch.scale, out, lse,
                             max_len=max_len, tiles_per_split=tps)
     has_combine = a.workspace_bytes > 0
+    # the peer exchange does the decode's combine itself (fd_decode_exchange_merge)
+    fused = gather is not None and args.exchange == "peer"  # "peer-split": decode + combine + fd_exchange_merge
+    if fused:
+        has_combine = False
+
+    def exchange(args_):
+        if fused:
+            gather.decode_exchange_merge(args_, final, decode=False)  # after the caller's decode launch
+        else:
+            gather.exchange_and_merge(out, lse, final)
     copy_evs = []
 
     def stage(ev=None):
@@ -397,7 +407,7 @@ def run_ours(args, ws, rank, device):
         if has_combine:
             gpu_ops.launch_decode(a, device, "combine")
         if gather is not None:
-            gather.exchange_and_merge(out, lse, final)
+            exchange(a)
 
     for _ in range(args.warmup):
         step()
@@ -416,6 +426,9 @@ def run_ours(args, ws, rank, device):
 
         def gstep():
             stage()
+            if fused:
+                gather.decode_exchange_merge(a_g, final)  # decode, then the exchange with the combine in it
+                return
             gpu_ops.launch_decode(a_g, device, "partials")
             if has_combine:
                 gpu_ops.launch_decode(a_g, device, "combine")
@@ -464,7 +477,7 @@ def run_ours(args, ws, rank, device):
             if has_combine:
                 gpu_ops.launch_decode(a, device, "combine")
             e[2].record()
-            gather.exchange_and_merge(out, lse, final)
+            exchange(a)
             e[3].record()
         torch.cuda.synchronize(device)
         ph = torch.tensor([sum(e[j].elapsed_time(e[j + 1]) for e in pev) / args.steps for j in range(3)],
@@ -475,7 +488,8 @@ def run_ours(args, ws, rank, device):
         phases = {nm: {"min_ms": round(float(lo[j]), 4), "max_ms": round(float(hi[j]), 4)}
                   for j, nm in enumerate(("decode", "combine", "exchange_merge"))}
         phases["note"] = ("eager steps, CUDA events per rank; min / max over ranks; exchange_merge includes the "
-                          "wait for the slowest rank")
+                          "wait for the slowest rank" + (" and the decode's combine (done by the exchange kernel)"
+                                                         if fused else ""))
     # the timed region of `value`: K graph replays (or the eager steps above).
     # A short step makes K steps shorter than nvidia-smi's sampling period,
     # so the sampler starts under an untimed pre-roll of replays (~0.3 s of
@@ -486,7 +500,12 @@ def run_ours(args, ws, rank, device):
         torch.cuda.synchronize(device)
         clocks.start()
         time.sleep(0.1)
-        pre = max(1, int(0.3 / max(elapsed_eager / args.steps, 1e-5)))
+        # every rank replays the same number of graphs (they hold collectives):
+        # the pre-roll count comes from the slowest rank's eager step
+        step_est = torch.tensor([elapsed_eager / args.steps], dtype=torch.float64, device=device)
+        if dist:
+            torch.distributed.all_reduce(step_est, op=torch.distributed.ReduceOp.MAX)
+        pre = max(1, int(0.3 / max(float(step_est), 1e-5)))
         for _ in range(pre):
             graph.replay()
         if dist:
@@ -529,10 +548,16 @@ def run_ours(args, ws, rank, device):
         # the staged range comes from the step's host-side table, as a caller
         # holding the plan on the host would compute it
         hr = gpu_ops.host_block_range(h_bt, h_lens, batch.BS, batch.G) if staged else None
-        gpu_ops.decode_tiered(d_q, res.tiers, batch.G, d_bt, d_lens, batch.scale, out, lse,
-                              max_len=max_len, tiles_per_split=tps, host_range=hr)
-        if gather is not None:
-            gather.exchange_and_merge(out, lse, final)
+        if fused:
+            from vllm_fastdecoder_b200 import sharded as sh
+
+            sh.sharded_decode(d_q, res.tiers, batch.G, d_bt, d_lens, batch.scale, gather, final, max_len=max_len,
+                              tiles_per_split=tps)
+        else:
+            gpu_ops.decode_tiered(d_q, res.tiers, batch.G, d_bt, d_lens, batch.scale, out, lse,
+                                  max_len=max_len, tiles_per_split=tps, host_range=hr)
+            if gather is not None:
+                gather.exchange_and_merge(out, lse, final)
         h_out.copy_(e_out, non_blocking=True)
         h_lse.copy_(lse if gather is None else gather.lse_out, non_blocking=True)
         torch.cuda.current_stream(device).synchronize()
@@ -601,15 +626,19 @@ def run_ours(args, ws, rank, device):
                                              "per-segment weight positions)",
         "tiles_per_split": tps, "split_combine": has_combine, "kernel": kname,
         "host_read": (args.host_read if res.tiers[1] is not None else "none (all HBM)"),
-        "timing": ("value: one CUDA graph of the step (decode + combine launches"
+        "timing": ("value: one CUDA graph of the step (the decode launch" + (" + its combine" if has_combine else "")
                    + (", exchange and merge" if gather is not None else "") + ") replayed K times after an "
                    "untimed pre-roll; roofline: eager steps with CUDA events around the decode launch (eager step "
                    f"{elapsed_eager / args.steps * 1e3:.4f} ms)" if graph is not None
                    else "value and roofline: eager steps, CUDA events"),
     }
     if gather is not None:
-        run["exchange"] = ("peer memory: one fd_exchange_merge launch per step (CUDA IPC buffers, NVLink stores)"
-                           if args.exchange == "peer" else "NCCL all_gather_into_tensor + fd_merge_partials")
+        run["exchange"] = {
+            "peer": "peer memory: fd_decode_exchange_merge (the decode, then one exchange launch that also does the "
+                    "decode's combine; CUDA IPC buffers, NVLink stores)",
+            "peer-split": "peer memory: the decode, its combine, then one fd_exchange_merge launch (CUDA IPC "
+                          "buffers, NVLink stores)",
+            "nccl": "NCCL all_gather_into_tensor + fd_merge_partials"}[args.exchange]
     full = workloads.config3(world=1, rank=0, ctx=args.ctx) if args.workload == "c3" else batch
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -621,8 +650,9 @@ def run_ours(args, ws, rank, device):
         "kv_gbs": round((hbm_b + host_b) * ws * args.steps / elapsed / 1e9, 1),
         "e2e": {"value": round(rows_per_step * args.steps / e2e_t, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "vllm_fastdecoder_b200.gpu_ops.decode_tiered (C ABI fd_decode_attn)"
-                       + (" + the exchange and merge" if gather is not None else "")},
+                "api": ("vllm_fastdecoder_b200.sharded.sharded_decode (C ABI fd_decode_exchange_merge)" if fused else
+                        "vllm_fastdecoder_b200.gpu_ops.decode_tiered (C ABI fd_decode_attn)"
+                        + (" + the exchange and merge" if gather is not None else ""))},
         "roofline": roof,
         "clocks": clk,
         "gpu_launches": args.steps * (1 + int(has_combine) + (1 if gather is not None else 0)),
@@ -1007,9 +1037,10 @@ def main() -> int:
     ap.add_argument("--no-parity", action="store_true", help="c3: skip the in-run oracle check of the output")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
-                    help="c3 on N > 1 GPUs: partials exchanged over peer memory in one kernel (fd_exchange_merge) "
-                         "or with an NCCL all-gather and a merge kernel")
+    ap.add_argument("--exchange", choices=["peer", "peer-split", "nccl"], default="nccl",
+                    help="c3 on N > 1 GPUs: partials exchanged over peer memory by the exchange kernel that also "
+                         "does the decode's combine (peer), by the decode's combine and then the exchange kernel "
+                         "(peer-split), or with an NCCL all-gather and a merge kernel (nccl)")
     ap.add_argument("--host-read", choices=["staged", "mapped"], default="staged",
                     help="host tier: staged into HBM by the copy engine each step, or read in place over PCIe")
     ap.add_argument("--no-graph", action="store_true",

@@ -345,20 +345,20 @@ FD_API size_t fd_plan_args_bytes(void);
 
 /* The sharded long-context path (no reference counterpart: the reference
  * has no multi-GPU path) exchanges each rank's fp32 partial over peer
- * memory instead of an NCCL all-gather: fd_exchange_merge pushes the
+ * memory instead of an NCCL all-gather: one launch per step pushes the
  * rank's packed [o (n*H*D) | lse (H*n)] into every rank's receive buffer
  * over NVLink, waits (bounded) for every rank's, and merges with the rule
- * of fd_merge_partials, in one launch per step.  Buffers are plain device
- * memory shared with CUDA IPC (no multicast object). */
+ * of fd_merge_partials.  Buffers are plain device memory shared with CUDA
+ * IPC (no multicast object). */
 #define FD_MAX_PEERS 8
 #define FD_IPC_HANDLE_BYTES 64
-/* Layout of one rank's allocation (fd_peer_alloc): u64 counters of its own
- * steps at byte 0, u64 arrival flags [FD_MAX_PEERS] at FD_PEER_FLAGS_OFFSET
- * (flag q = the last step whose partial rank q delivered here, written only
- * by rank q), the fp32 receive slots [2 parities][world][slot] from
- * FD_PEER_RECV_OFFSET. */
-#define FD_PEER_FLAGS_OFFSET 64
-#define FD_PEER_RECV_OFFSET 256
+/* Layout of one rank's allocation (fd_peer_alloc): u64 step counters of its
+ * exchange CTAs [64] at byte 0; u64 arrival flags [FD_MAX_PEERS][64] at
+ * FD_PEER_FLAGS_OFFSET (flag (q, b) = the last step whose share CTA b of rank
+ * q delivered here, written only by that CTA); the fp32 receive slots
+ * [2 parities][world][slot] from FD_PEER_RECV_OFFSET. */
+#define FD_PEER_FLAGS_OFFSET 512
+#define FD_PEER_RECV_OFFSET 8192
 
 typedef struct fd_peer_exchange {
   void *base[FD_MAX_PEERS]; /* rank q's allocation as mapped in this process:
@@ -380,17 +380,40 @@ FD_API int fd_peer_free(void *ptr);
 /* One step: every rank calls it once per step, in the same order, with the
  * same n / heads / head size / num_ctas (0: 32, at most 64).  send: this rank's packed
  * partial (16-byte aligned); out [n, H, D] in out_dtype; out_lse [H, n] or
- * NULL.  The step waits until every rank's own arrival flag (not a count of
- * arrivals) has reached the step, so a peer that is a step ahead cannot
- * complete another rank's step.  Launched as a programmatic dependent of the
- * kernel ahead of it on the stream (it waits for that kernel before reading
- * send).  A wait longer than timeout_ns (0: 2 s) records FD_DEVERR_TIMEOUT
- * in *error and returns with the outputs unwritten; the caller must read the
- * error word (fd_read_error) after each step it cannot otherwise vouch for,
- * and after a timeout the exchange must be freed and rebuilt on every rank. */
+ * NULL.  The step waits until every CTA of every rank has raised its own
+ * arrival flag to the step (flags, not a count of arrivals, so a rank that
+ * is a step ahead cannot complete another rank's step).  Launched as a
+ * programmatic dependent of the kernel ahead of it on the stream (it waits
+ * for that kernel before reading send).  A wait longer than timeout_ns (0:
+ * 2 s) records FD_DEVERR_TIMEOUT in *error and returns with the outputs
+ * unwritten; the caller must read the error word (fd_read_error) after each
+ * step it cannot otherwise vouch for, and after a timeout the exchange must
+ * be freed and rebuilt on every rank. */
 FD_API int fd_exchange_merge(const fd_peer_exchange *x, const float *send, int32_t n, int32_t num_heads,
                              int32_t head_size, void *out, int32_t out_dtype, float *out_lse, int32_t num_ctas,
                              int64_t timeout_ns, int32_t *error, void *stream);
+
+/* The whole sharded step in two launches: the decode of `a` over this rank's
+ * shard, then the exchange and merge of fd_exchange_merge, which also does
+ * the decode's combine.  `a` must write the rank's packed partial: out_dtype
+ * FD_DTYPE_F32, out = o [n, H, D] contiguous, lse = out + n*H*D laid out
+ * [H, n], no out_rows (this is the exchange's send buffer, 16-byte aligned).
+ * With the persistent schedule the decode's combine launch is skipped: the
+ * exchange pushes each (row, kv-head chunk) segment that one decode CTA
+ * finished straight from `out`, and merges each segment that decode CTAs cut
+ * from their partial slots in the workspace on its way to the other ranks
+ * (the combine's rule and order, so the result equals decode + combine +
+ * fd_exchange_merge bit for bit).  The error word is a->error.  Same
+ * collective rules as fd_exchange_merge. */
+FD_API int fd_decode_exchange_merge(const fd_decode_args *a, const fd_peer_exchange *x, void *out,
+                                    int32_t out_dtype, float *out_lse, int32_t num_ctas, int64_t timeout_ns,
+                                    void *stream);
+/* The exchange half of fd_decode_exchange_merge, for callers that launched
+ * the decode themselves (fd_decode_attn_partials with the same arguments,
+ * earlier on the stream) and want other work or timing events in between. */
+FD_API int fd_exchange_merge_decoded(const fd_decode_args *a, const fd_peer_exchange *x, void *out,
+                                     int32_t out_dtype, float *out_lse, int32_t num_ctas, int64_t timeout_ns,
+                                     void *stream);
 
 /* Two-way log-sum-exp merge, the rule of vLLM merge_attn_states as restated
  * in fastdecode/cpu_ops.py:93-113 and called at fastdecode/backend.py:54-55,
@@ -399,7 +422,8 @@ FD_API int fd_exchange_merge(const fd_peer_exchange *x, const float *send, int32
  *   o_a, o_b: [n, H, D] contiguous, dtype in_dtype (F16/BF16/F32)
  *   lse_a, lse_b: [H, n] fp32
  *   out: rows out_rows[i] (or i) of an [*, H, D] tensor with out_stride_n,
- *        dtype out_dtype; out_lse [H, n] fp32 or NULL. */
+ *        dtype out_dtype (a negative out_rows[i] writes no row);
+ *        out_lse [H, n] fp32 or NULL. */
 FD_API int fd_merge_attn_states(void *out, int32_t out_dtype, int64_t out_stride_n,
                          const int64_t *out_rows, float *out_lse,
                          const void *o_a, const float *lse_a,

@@ -1,8 +1,12 @@
-"""The peer-memory exchange kernel (fd_exchange_merge) on one GPU.
+"""The peer-memory exchange kernel (fd_exchange_merge, fd_decode_exchange_merge)
+on one GPU.
 
 world = 1: the rank merges its own partial, so over several consecutive
 steps (both buffer parities, and replays of a captured CUDA graph) the
-result must equal fd_merge_partials with one part, bit for bit.  A peer
+result must equal fd_merge_partials with one part, bit for bit; the fused
+step (decode, then the exchange that also does the decode's combine) must
+equal decode + combine + merge bit for bit, on both decode kernels, with
+segments cut between CTAs and whole ones, and on the split grid.  A peer
 that never signals (a second local buffer standing in for rank 1) must make
 the bounded wait give up: FD_DEVERR_TIMEOUT in the error word, no fault, the
 context still usable.  The two-rank exchange is tested on 2 GPUs in
@@ -124,8 +128,9 @@ def test_peer_a_step_ahead_does_not_complete_a_missing_rank():
     # plain device buffers stand in for the three ranks' allocations (zeroed:
     # counters, flags and slots start at 0, as fd_peer_alloc leaves them)
     bufs = [torch.zeros(nbytes // 8 + 1, dtype=torch.int64, device=dev) for _ in range(world)]
-    flags0 = bufs[0][nat.PEER_FLAGS_OFFSET // 8: nat.PEER_FLAGS_OFFSET // 8 + nat.MAX_PEERS]
-    flags0[1] = 2  # rank 1 is a step ahead of this rank's first step
+    ctas = 4
+    flags0 = bufs[0][nat.PEER_FLAGS_OFFSET // 8: nat.PEER_FLAGS_OFFSET // 8 + nat.MAX_PEERS * nat.PEER_MAX_CTAS]
+    flags0[nat.PEER_MAX_CTAS: nat.PEER_MAX_CTAS + ctas] = 2  # every CTA of rank 1 is a step ahead
     x = nat.FdPeerExchange()
     x.rank, x.world, x.slot_floats = 0, world, slot
     for q in range(world):
@@ -135,14 +140,15 @@ def test_peer_a_step_ahead_does_not_complete_a_missing_rank():
     lse = torch.full((H, n), 7.0, dtype=torch.float32, device=dev)
     err = gpu_ops.error_word(dev)
     nat.check(lib.fd_exchange_merge(ctypes.byref(x), send.data_ptr(), n, H, D, out.data_ptr(),
-                                    gpu_ops.dtype_code(out.dtype), lse.data_ptr(), 4, 50_000_000,
+                                    gpu_ops.dtype_code(out.dtype), lse.data_ptr(), ctas, 50_000_000,
                                     err.data_ptr(), gpu_ops._stream(dev)), "fd_exchange_merge")
     with pytest.raises(RuntimeError, match="device error 3"):
         gpu_ops.check_device_errors(dev)
     assert bool((out == 7.0).all()) and bool((lse == 7.0).all())
-    # this rank did deliver: its flag of step 1 is in every rank's buffer
+    # this rank did deliver: each of its CTAs raised its flag of step 1 in every rank's buffer
     for q in range(world):
-        assert int(bufs[q][nat.PEER_FLAGS_OFFSET // 8]) == 1
+        row0 = bufs[q][nat.PEER_FLAGS_OFFSET // 8: nat.PEER_FLAGS_OFFSET // 8 + ctas]
+        assert row0.tolist() == [1] * ctas
     torch.cuda.synchronize()
 
 
@@ -170,4 +176,54 @@ def test_check_marks_a_timed_out_exchange_unusable():
             ex.exchange_and_merge(None, None, final)
     finally:
         torch.cuda.synchronize()
+        ex.close()
+
+
+@pytest.mark.parametrize("dtype,H,KVH,lens,tps", [
+    (torch.bfloat16, 32, 8, [20000, 1, 0, 777, 9000], 0),  # tensor-core kernel, long rows cut between CTAs
+    (torch.float16, 16, 16, [3000, 5, 0, 1200], 0),        # CUDA-core kernel
+    (torch.float16, 8, 2, [40, 17, 0, 64], 0),             # short rows: segments whole within a CTA
+    (torch.bfloat16, 32, 8, [9000, 3, 2500], 16),          # split grid: the decode's own combine runs
+])
+def test_fused_step_equals_decode_combine_merge(dtype, H, KVH, lens, tps):
+    from oracle import oracle as O
+    from vllm_fastdecoder_b200 import gpu_ops, sharded
+    from vllm_fastdecoder_b200.gpu_ops import KVTier
+
+    dev = torch.device("cuda")
+    n, D, BS = len(lens), 128, 16
+    C = sum((L + BS - 1) // BS for L in lens) + 4
+    q, kc, vc, bt, _ = O.rand_case(n, H, KVH, D, BS, C, dtype, max_len=max(lens), seed=31)
+    g = torch.Generator().manual_seed(32)
+    perm = torch.randperm(C, generator=g).tolist()
+    bt = torch.zeros(n, bt.shape[1], dtype=torch.int32)
+    for i, L in enumerate(lens):
+        nb = (L + BS - 1) // BS
+        bt[i, :nb] = torch.tensor([perm.pop() for _ in range(nb)], dtype=torch.int32)
+    lens_t = torch.tensor(lens, dtype=torch.int32, device=dev)
+    tiers = (KVTier(kc.to(dev), vc.to(dev)), None)
+    qd, btd = q.to(dev), bt.to(dev)
+    scale = 1.0 / (D ** 0.5)
+    ex = sharded.PeerExchange(n, H, D, 1, dev)
+    try:
+        for decode_in_call in (True, False, True):  # 3 steps: both parities, both entry points
+            # reference: decode + combine into the send views, then the P = 1 merge
+            ref = torch.empty(n, H, D, dtype=dtype, device=dev)
+            ref_lse = torch.empty(H, n, dtype=torch.float32, device=dev)
+            gpu_ops.decode_tiered(qd, tiers, 1 << 40, btd, lens_t, scale, ex.o_view, ex.lse_view, tiles_per_split=tps)
+            gpu_ops.merge_partials(ex.send[: n * H * D + H * n], 1, n, H, D, ref, ref_lse)
+            torch.cuda.synchronize()
+            ex.o_view.fill_(float("nan"))  # the fused step must not lean on the reference's writes
+            ex.lse_view.fill_(float("nan"))
+            final = torch.full((n, H, D), float("nan"), dtype=dtype, device=dev)
+            a = gpu_ops.decode_args(qd, tiers, 1 << 40, btd, lens_t, scale, ex.o_view, ex.lse_view,
+                                    tiles_per_split=tps)
+            if not decode_in_call:
+                gpu_ops.launch_decode(a, dev, "partials")
+            ex.decode_exchange_merge(a, final, decode=decode_in_call)
+            torch.cuda.synchronize()
+            gpu_ops.check_device_errors(dev)
+            assert torch.equal(final, ref)
+            assert torch.equal(ex.lse_out, ref_lse)
+    finally:
         ex.close()

@@ -114,12 +114,15 @@ def _lse(H, n, g, empty_frac=0.15):
     return lse
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
-def test_merge_attn_states_matches_oracle(ops, dtype):
+@pytest.mark.parametrize("dtype,D", [(torch.float16, 128), (torch.bfloat16, 128), (torch.float32, 128),
+                                     (torch.float16, 20), (torch.float32, 6)])
+def test_merge_attn_states_matches_oracle(ops, dtype, D):
+    """D = 128: the vectorized kernel (16-byte chunks); D = 20 fp16 / 6 fp32:
+    rows that are not a whole number of 16-byte chunks (the general kernel)."""
     from oracle import oracle as O
 
     g = torch.Generator().manual_seed(5)
-    n, H, D = 37, 8, 128
+    n, H = 37, 8
     dev = torch.device("cuda")
     o_a = torch.randn(n, H, D, generator=g).to(dtype)
     o_b = torch.randn(n, H, D, generator=g).to(dtype)
@@ -148,12 +151,14 @@ def test_merge_attn_states_matches_oracle(ops, dtype):
     assert torch.all(torch.isnan(out2.cpu()[untouched].float()))
 
 
-@pytest.mark.parametrize("P", [2, 3, 8])
-def test_merge_partials_matches_oracle(ops, P):
+@pytest.mark.parametrize("P,D", [(2, 128), (3, 128), (8, 128), (16, 64), (17, 128), (4, 6)])
+def test_merge_partials_matches_oracle(ops, P, D):
+    """Up to 16 parts with D a multiple of 4: the vectorized kernel; 17 parts
+    or D = 6: the general kernel."""
     from oracle import oracle as O
 
     g = torch.Generator().manual_seed(6 + P)
-    n, H, D = 8, 32, 128
+    n, H = 8, 32
     dev = torch.device("cuda")
     stride = n * H * D + H * n
     parts = torch.empty(P, stride)

@@ -2,7 +2,8 @@
 every row with the split-KV kernel into the packed exchange buffer; the
 partials are exchanged and merged either with NCCL (all-gather, then
 fd_merge_partials) or over peer memory (fd_exchange_merge: one kernel,
-CUDA-IPC buffers, no multicast).  Both must match the oracle over the
+CUDA-IPC buffers, no multicast; and fd_decode_exchange_merge, whose exchange
+kernel also does the decode's combine).  All must match the oracle over the
 unsharded rows (bf16 output 1.6e-2, lse 1e-4) and each other bit for bit,
 over three consecutive steps (both parities of the peer buffers).  NVLS is
 off.  Each world size is skipped on a box with fewer GPUs."""
@@ -61,13 +62,19 @@ def _rank(rank, world, port, path):
         lbt, llens = sharded.shard_rows(bt, lens, BS, world, rank)
         tiers = (KVTier(kc.to(dev), vc.to(dev)), None)
         res = {}
-        for name, ex in (("nccl", sharded.PartialExchange(n, H, D, world, dev)),
-                         ("peer", sharded.PeerExchange(n, H, D, world, dev))):
+        for name in ("nccl", "peer", "peer_fused"):
+            ex = (sharded.PartialExchange(n, H, D, world, dev) if name == "nccl"
+                  else sharded.PeerExchange(n, H, D, world, dev))
             outs = []
             for _ in range(3):
                 final = torch.full((n, H, D), float("nan"), dtype=q.dtype, device=dev)
-                sharded.sharded_decode(q.to(dev), tiers, 1 << 40, lbt.to(dev), llens.to(dev), 1.0 / math.sqrt(D),
-                                       ex, final)
+                if name == "peer":  # decode (with its combine), then fd_exchange_merge
+                    gpu_ops.decode_tiered(q.to(dev), tiers, 1 << 40, lbt.to(dev), llens.to(dev), 1.0 / math.sqrt(D),
+                                          ex.o_view, ex.lse_view)
+                    ex.exchange_and_merge(None, None, final)
+                else:  # nccl, and the fused step (fd_decode_exchange_merge)
+                    sharded.sharded_decode(q.to(dev), tiers, 1 << 40, lbt.to(dev), llens.to(dev),
+                                           1.0 / math.sqrt(D), ex, final)
                 torch.cuda.synchronize(dev)
                 gpu_ops.check_device_errors(dev)
                 outs.append((final.cpu(), ex.lse_out.cpu()))
@@ -92,9 +99,10 @@ def test_sharded_decode_on_several_gpus(tmp_path, world):
     ref_o, ref_l = O.ref_decode_attn_f64(q, kc, vc, bt, lens, 1.0 / math.sqrt(D))
     nz = lens > 0
     for k in range(3):
-        for name in ("nccl", "peer"):
+        for name in ("nccl", "peer", "peer_fused"):
             out, lse = res[name][k]
             torch.testing.assert_close(out[nz].double(), ref_o[nz], atol=1.6e-2, rtol=1.6e-2)
             torch.testing.assert_close(lse[:, nz].double(), ref_l[:, nz], atol=1e-4, rtol=1e-5)
             assert torch.all(out[~nz] == 0) and torch.all(torch.isneginf(lse[:, ~nz]))
-        assert torch.equal(res["nccl"][k][0], res["peer"][k][0]) and torch.equal(res["nccl"][k][1], res["peer"][k][1])
+        for name in ("peer", "peer_fused"):
+            assert torch.equal(res["nccl"][k][0], res[name][k][0]) and torch.equal(res["nccl"][k][1], res[name][k][1])

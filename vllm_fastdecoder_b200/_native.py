@@ -86,8 +86,9 @@ class FdPlanArgs(ctypes.Structure):
 
 MAX_PEERS = 8  # FD_MAX_PEERS
 IPC_HANDLE_BYTES = 64  # FD_IPC_HANDLE_BYTES
-PEER_FLAGS_OFFSET = 64  # FD_PEER_FLAGS_OFFSET
-PEER_RECV_OFFSET = 256  # FD_PEER_RECV_OFFSET
+PEER_FLAGS_OFFSET = 512  # FD_PEER_FLAGS_OFFSET
+PEER_RECV_OFFSET = 8192  # FD_PEER_RECV_OFFSET
+PEER_MAX_CTAS = 64  # flags per rank in a peer buffer
 
 
 class FdPeerExchange(ctypes.Structure):
@@ -131,6 +132,10 @@ SIGNATURES = {
     "fd_exchange_merge": (c_int32, [
         POINTER(FdPeerExchange), c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_int32,
         c_int64, c_void_p, c_void_p]),
+    "fd_decode_exchange_merge": (c_int32, [
+        POINTER(FdDecodeArgs), POINTER(FdPeerExchange), c_void_p, c_int32, c_void_p, c_int32, c_int64, c_void_p]),
+    "fd_exchange_merge_decoded": (c_int32, [
+        POINTER(FdDecodeArgs), POINTER(FdPeerExchange), c_void_p, c_int32, c_void_p, c_int32, c_int64, c_void_p]),
     "fd_plan_args_bytes": (c_size_t, []),
     "fd_version": (c_int32, []),
     "fd_abi_sizes": (c_int32, [POINTER(c_size_t), POINTER(c_size_t)]),

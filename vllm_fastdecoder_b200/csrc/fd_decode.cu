@@ -668,12 +668,12 @@ __global__ void fd_persistent_combine_kernel(const __grid_constant__ DecodeParam
   if (t0 == 0 || t0 >= nt) return;  // starts here, or only weight positions left
   const int64_t g0 = (int64_t)P[i] * Y + (int64_t)y * nv;
   if (g0 + nt - 1 >= gb) return;  // continues into a later CTA, which merges it
-  const int64_t c0 = ((g0 + 1) * N - 1) / T;  // CTA owning position g0
+  // CTAs c0 (owning position g0) .. c (this one, owning the last real tile)
+  // wrote partials; c0 into slot first_slot (seg_span)
+  const SegSpan sp = seg_span(P, Y, p.vtiles, N, T, i, y);
+  const int64_t c0 = sp.c0;
   const int64_t c1 = c;
-  // the segment is c0's first real piece (slot 0) unless c0's range holds
-  // real tiles before g0, i.e. starts before the previous segment's weight
-  // positions
-  const int first_slot = ((c0 * T) / N >= g0 - p.vtiles) ? 0 : 1;
+  const int first_slot = sp.first_slot;
   const int GQ = p.gq;
   const int kh = y / p.gcs, gc = y - kh * p.gcs;
   const int h0 = kh * p.G + gc * GQ;
@@ -1000,7 +1000,8 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
 // Validate `a` and fill the kernel parameters; launch_main / launch_combine
 // select which of the two kernels run.
 int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool launch_combine,
-                void* ws_override = nullptr, size_t ws_override_bytes = 0) {
+                void* ws_override = nullptr, size_t ws_override_bytes = 0, fdk::ShardGeom* geom = nullptr) {
+  if (geom != nullptr) geom->prefix = nullptr;
   if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_decode_attn: null args");
   if (a->n < 0) return fdh::fail(FD_ERR_INVALID, "n must be >= 0");
   if (a->n == 0) return FD_OK;
@@ -1152,6 +1153,19 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
       st = fns.launch(p, dim3((unsigned)ncta), extra, s);
       if (st != FD_OK) return st;
     }
+    if (geom != nullptr) {
+      // the consumer merges the cut segments itself: no combine launch
+      geom->prefix = p.ws_prefix;
+      geom->part_o = p.part_o;
+      geom->part_lse = p.part_lse;
+      geom->ncta = (int)ncta;
+      geom->vtiles = p.vtiles;
+      geom->KVH = p.KVH;
+      geom->gcs = p.gcs;
+      geom->G = p.G;
+      geom->GQ = g.GQ;
+      return st;
+    }
     if (launch_combine && ncta > 1) {
       // programmatic dependent launch: the combine's launch overlaps the
       // decode's last CTAs; the kernel waits for the decode grid before
@@ -1200,6 +1214,12 @@ extern "C" int fd_decode_attn_partials(const fd_decode_args* a, void* stream) {
 extern "C" int fd_decode_attn_combine(const fd_decode_args* a, void* stream) {
   return decode_impl(a, stream, false, true);
 }
+
+namespace fdk {
+int launch_decode_for_exchange(const fd_decode_args* a, void* stream, ShardGeom* geom, bool decode) {
+  return decode_impl(a, stream, decode, true, nullptr, 0, geom);
+}
+}  // namespace fdk
 
 // ------------------------------------------------------------ no-allocation variant
 

@@ -271,4 +271,56 @@ int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem
 // query group 2, 4 or 8, block size a multiple of 16).
 bool mma_eligible(int dtype, int D, int G, int BS);
 
+// The CTAs whose ranges hold real tiles of the segment (row, y) of a
+// persistent launch of N CTAs over T = prefix[n] * Y positions: c0 (the owner
+// of its first position g0) to c1 (the owner of its last real tile); c0 == c1
+// means one CTA wrote the segment's output directly.  Otherwise every CTA of
+// c0..c1 whose range is not empty wrote an fp32 partial: c0 into slot
+// first_slot (0 when the segment is its first real piece, i.e. its range
+// starts at most vtiles weight positions before g0), the others into slot 0
+// (the segment is their first piece).  The owner of position g is the
+// largest c with floor(c * T / N) <= g, i.e. ((g + 1) * N - 1) / T.
+struct SegSpan {
+  int64_t c0, c1;
+  int first_slot;
+};
+
+__device__ __forceinline__ SegSpan seg_span(const int* prefix, int Y, int vtiles, int64_t N, int64_t T, int row,
+                                            int y) {
+  SegSpan sp;
+  const int nv = prefix[row + 1] - prefix[row];
+  const int nt = nv - vtiles;
+  const int64_t g0 = (int64_t)prefix[row] * Y + (int64_t)y * nv;
+  sp.c0 = ((g0 + 1) * N - 1) / T;
+  sp.c1 = ((g0 + nt) * N - 1) / T;
+  sp.first_slot = ((sp.c0 * T) / N >= g0 - vtiles) ? 0 : 1;
+  return sp;
+}
+
+__device__ __forceinline__ bool seg_nonempty(int64_t cc, int64_t N, int64_t T) {
+  return (cc * T) / N != ((cc + 1) * T) / N;
+}
+
+// Where a persistent decode launch left each (row, kv-head chunk) segment of
+// its output, for a kernel that reads the output right after it (the peer
+// exchange of the sharded path) and merges the segments that CTA ranges cut
+// on the way, instead of a separate combine launch.  prefix == nullptr: the
+// output is complete in the decode's out / lse.
+struct ShardGeom {
+  const int* prefix;      // positions per row, [n + 1] (written by the decode's CTA 0)
+  const float* part_o;    // fp32 partial slots [ncta * 2 * GQ][D]
+  const float* part_lse;  // [ncta * 2 * GQ]
+  int ncta;               // CTAs of the decode launch
+  int vtiles;             // weight positions per segment
+  int KVH, gcs, G, GQ;    // segments are (row, kv head * gcs + chunk); a chunk holds GQ of G query heads
+};
+
+// Launch the decode of `a` on `stream` for a consumer that merges cut
+// segments itself: with the persistent schedule only the decode kernel runs
+// and `geom` describes its partials; otherwise (split grid) the decode and its
+// combine run and geom->prefix is null.  decode = false: the caller launched
+// the decode kernel already (fd_decode_attn_partials with the same arguments);
+// only the split grid's combine is launched, and `geom` filled.
+int launch_decode_for_exchange(const fd_decode_args* a, void* stream, ShardGeom* geom, bool decode);
+
 }  // namespace fdk

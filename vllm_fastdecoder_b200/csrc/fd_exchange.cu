@@ -1,62 +1,67 @@
 // Exchange + merge of the sharded decode's partials over peer memory: the
-// fused replacement of "NCCL all-gather, then the P-way merge kernel" of the
-// long-context path (one rank per GPU, KV sharded over the ranks).
+// fused replacement of "combine kernel, NCCL all-gather, then the P-way merge
+// kernel" of the long-context path (one rank per GPU, KV sharded over the
+// ranks).
 //
 // Each rank owns one device allocation, mapped into every other rank's
 // process with CUDA IPC (plain device memory: no multicast object, no NVLS):
-//   [0]   step counter      u64, this rank's completed steps
-//   [8]   CTA counter       u64, this rank's finished CTAs
-//   [16]  push counter      u64, this rank's CTAs done pushing
-//   [64]  arrival flags     u64 [FD_MAX_PEERS]: flag q holds the last step
-//                            whose slot rank q has delivered into this
-//                            buffer (written only by rank q, st.release.sys)
-//   [256] receive buffer    fp32 [2 parities][world][slot], slot = the packed
+//   [0]    step counters    u64 [kMaxCtas]: CTA b's completed steps (its own)
+//   [512]  arrival flags    u64 [FD_MAX_PEERS][kMaxCtas]: flag (q, b) holds the
+//                            last step CTA b of rank q has delivered its share
+//                            into this buffer (written only by that CTA: a
+//                            system-scope fence, then relaxed stores)
+//   [8192] receive buffer   fp32 [2 parities][world][slot], slot = the packed
 //                            partial [o (n*H*D) | lse (H*n)] rounded to 4
-// One launch per step of at most 64 small CTAs, which the SMs hold at once
-// (every wait is bounded in any case):
+// One launch per step of at most 64 CTAs of 256 threads, which the SMs hold
+// at once (every wait is bounded in any case):
 //   1. every CTA stores its share of the rank's packed partial into slot
 //      [parity][rank] of every rank's receive buffer (16-byte stores over
-//      NVLink; the own copy is local), fences at system scope and counts
-//      itself on the rank's push counter; the last CTA of the rank fences
-//      again and writes the step into flag [rank] of every rank's buffer
-//      (world remote release stores per rank and step);
-//   2. it waits (bounded, %globaltimer) until every flag of its own buffer
-//      holds at least the step: each rank's slot of this step has landed.
-//      Per-source flags, not one summed counter: a peer that is already a
-//      step ahead must not stand in for a rank whose signal of this step is
-//      still in flight;
-//   3. it merges its (row, head) pairs from the receive buffer with the
+//      NVLink; the own copy is local).  Given the decode launch's geometry
+//      (fd_decode_exchange_merge) the share is a set of (row, kv-head chunk)
+//      segments: a segment one decode CTA finished is copied from the
+//      decode's output, a segment that decode CTA ranges cut is merged from
+//      the decode's partial slots on the way (the rule and order of the
+//      decode's own combine), so no combine launch runs before the exchange;
+//   2. the CTA fences at system scope and writes the step into its flag
+//      (rank, b) of every rank's buffer;
+//   3. its threads wait (bounded, %globaltimer) until every flag of its own
+//      buffer (every CTA of every rank) holds at least the step (relaxed
+//      polls, then one acquire fence): every share of this step has landed;
+//   4. it merges its (row, head) pairs from the receive buffer with the
 //      log-sum-exp rule of fd_merge_partials, same operations in the same
 //      order (so the result equals the NCCL path bit for bit);
-//   4. the last CTA to finish advances the step counter, so the next launch
-//      (or graph replay) uses the other parity and the next step number.
+//   5. it advances its own step counter (no atomics anywhere: every CTA
+//      keeps its own step, and all CTAs of a launch agree on it).
 // Double buffering by parity keeps a rank that is one step ahead from
 // overwriting a slot another rank is still merging; it cannot get two steps
-// ahead, because finishing a step needs every rank's flag of that step, and
-// a rank raises its flag of step s + 1 only after its merge of step s ended.
+// ahead, because finishing a step needs every CTA's flag of that step from
+// every rank, and a rank's launch of step s + 1 starts after its launch of
+// step s has completed.
 //
 // The kernel is launched as a programmatic dependent of the kernel before it
-// on the stream (the decode's combine): its launch overlaps that kernel's
-// tail, and griddepcontrol.wait holds every CTA until the partial it pushes
-// is complete.
+// on the stream (the decode): its launch overlaps that kernel's tail, and
+// griddepcontrol.wait holds every CTA until the decode's output is complete.
 
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
 
 #include "fd_common.cuh"
+#include "fd_decode.cuh"
 #include "fd_internal.h"
 
 namespace fdk {
 
+constexpr int kXThreads = 256;  // threads per exchange CTA
+constexpr int kXMaxCtas = 64;   // CTAs per launch, at most (per-CTA counters and flags)
+
 struct ExchangeParams {
-  const float* send;                      // [slot] this rank's packed partial
+  const float* send;                      // [slot] this rank's packed partial [o | lse]
   float* recv[FD_MAX_PEERS];              // rank q's receive buffer (mapped)
-  unsigned long long* flag_at[FD_MAX_PEERS];  // this rank's arrival flag in rank q's buffer (mapped)
-  const unsigned long long* flags;        // this rank's arrival flags [world]
-  unsigned long long* step;               // this rank's step counter
-  unsigned long long* done;               // this rank's finished-CTA counter
-  unsigned long long* pushed;             // this rank's CTAs done pushing
+  unsigned long long* flag_at[FD_MAX_PEERS];  // this rank's row of flags in rank q's buffer [kXMaxCtas]
+  const unsigned long long* flags;        // this rank's flags [world][kXMaxCtas]
+  unsigned long long* steps;              // this rank's per-CTA step counters [kXMaxCtas]
+  ShardGeom geom;                         // the decode launch's segments (prefix null: send is complete)
   int rank, world, n, H, D;
   int64_t slot;                           // floats per rank slot (multiple of 4)
   void* out;
@@ -66,70 +71,170 @@ struct ExchangeParams {
   int32_t* err;
 };
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+// Flags are written and polled with relaxed system-scope accesses; the
+// ordering comes from one fence on each side (a release or acquire access per
+// flag would fence once per flag: `world` system-scope fences per step).
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ float lse_or_empty(float x) { return x == INFINITY ? -INFINITY : x; }
 
-__global__ void fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams p) {
-  __shared__ unsigned long long s_step;
-  __shared__ int s_ok;
-  griddep_wait();  // the partial in p.send is complete (programmatic dependent launch)
-  if (threadIdx.x == 0) {
-    s_step = *reinterpret_cast<volatile unsigned long long*>(p.step) + 1;
-    s_ok = 1;
-  }
-  __syncthreads();
-  const unsigned long long step = s_step;
-  const int par = (int)(step & 1ull);
+// Store at float offset `off` of this rank's slot in every rank's buffer.
+__device__ __forceinline__ void put4(const ExchangeParams& p, int64_t off, const float4& v) {
+  for (int q = 0; q < p.world; ++q) *reinterpret_cast<float4*>(p.recv[q] + off) = v;
+}
+__device__ __forceinline__ void put1(const ExchangeParams& p, int64_t off, float v) {
+  for (int q = 0; q < p.world; ++q) p.recv[q][off] = v;
+}
 
-  // 1. push this rank's slot to every rank
-  const float4* src = reinterpret_cast<const float4*>(p.send);
-  const int64_t nvec = p.slot / 4;
-  const int64_t dst_off = ((int64_t)par * p.world + p.rank) * p.slot;
-  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nvec; c += (int64_t)gridDim.x * blockDim.x) {
-    const float4 v = src[c];
-    for (int q = 0; q < p.world; ++q) reinterpret_cast<float4*>(p.recv[q] + dst_off)[c] = v;
-  }
-  __syncthreads();  // the CTA's stores happen before thread 0's fence and release
+// Up to this many CTAs share a cut segment on the fast path (their partials
+// are loaded at once, two memory round trips); more fall back to a loop.
+constexpr int kSpanFast = 4;
 
-  // 2. the rank's last CTA to finish pushing raises the rank's flag in every
-  // rank's buffer; then every CTA waits for every rank's flag of this step
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned long long prev = atomicAdd(p.pushed, 1ull);
-    if (prev + 1 == step * gridDim.x) {
-      __threadfence_system();  // the other CTAs' fenced stores happen before the flags
-      for (int q = 0; q < p.world; ++q) st_release_sys(p.flag_at[q], step);
+// Push this rank's partial segment by segment (1.): items are 4 consecutive
+// dims of one head of one (row, kv-head chunk) segment, spread over the grid.
+// A segment one decode CTA finished is copied from `send`, where the decode
+// wrote it (empty rows included); a cut segment is merged from the decode's
+// fp32 partial slots with the decode combine's rule and order: M = max lse,
+// w = 2^((lse - M) log2 e), o = sum(w o) / sum(w), lse = M + ln sum(w).
+__device__ void push_segments(const ExchangeParams& p, int64_t dst_off) {
+  const ShardGeom& g = p.geom;
+  const int Y = g.KVH * g.gcs;
+  const int* P = g.prefix;
+  const int64_t T = (int64_t)P[p.n] * Y;
+  const int64_t N = g.ncta;
+  const int c4 = p.D / 4;
+  const int64_t per_seg = (int64_t)g.GQ * c4;
+  const int64_t items = (int64_t)p.n * Y * per_seg;
+  const int64_t o_floats = (int64_t)p.n * p.H * p.D;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sgi = it / per_seg;
+    const int e = (int)(it - sgi * per_seg);
+    const int gq = e / c4, d = (e - gq * c4) * 4;
+    const int i = (int)(sgi / Y), y = (int)(sgi - (int64_t)i * Y);
+    const int kh = y / g.gcs, gc = y - kh * g.gcs;
+    const int h = kh * g.G + gc * g.GQ + gq;
+    const int64_t oi = ((int64_t)i * p.H + h) * p.D + d;
+    const int64_t li = o_floats + (int64_t)h * p.n + i;
+    SegSpan sp{0, 0, 0};
+    if (P[i + 1] > P[i]) sp = seg_span(P, Y, g.vtiles, N, T, i, y);  // else an empty row, written to send
+    if (sp.c0 == sp.c1) {
+      put4(p, dst_off + oi, __ldcg(reinterpret_cast<const float4*>(p.send + oi)));
+      if (d == 0) put1(p, dst_off + li, __ldcg(p.send + li));
+      continue;
     }
+    float M = -INFINITY, L = 0.f;
+    float O[4] = {0.f, 0.f, 0.f, 0.f};
+    if (sp.c1 - sp.c0 < kSpanFast) {
+      float l[kSpanFast];
+      float4 o[kSpanFast];
+      bool on[kSpanFast];
+#pragma unroll
+      for (int k = 0; k < kSpanFast; ++k) {
+        const int64_t cc = sp.c0 + k;
+        on[k] = cc <= sp.c1 && seg_nonempty(cc, N, T);
+        const int64_t sl = (cc * 2 + (k == 0 ? sp.first_slot : 0)) * g.GQ + gq;
+        l[k] = on[k] ? __ldcg(g.part_lse + sl) : -INFINITY;
+        o[k] = on[k] ? __ldcg(reinterpret_cast<const float4*>(g.part_o + sl * p.D + d)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < kSpanFast; ++k)
+        if (on[k]) M = fmaxf(M, l[k]);
+#pragma unroll
+      for (int k = 0; k < kSpanFast; ++k) {
+        if (!on[k]) continue;
+        const float w = exp2f((l[k] - M) * kLog2e);
+        L += w;
+        O[0] = fmaf(w, o[k].x, O[0]);
+        O[1] = fmaf(w, o[k].y, O[1]);
+        O[2] = fmaf(w, o[k].z, O[2]);
+        O[3] = fmaf(w, o[k].w, O[3]);
+      }
+    } else {
+      for (int64_t cc = sp.c0; cc <= sp.c1; ++cc) {
+        if (!seg_nonempty(cc, N, T)) continue;
+        M = fmaxf(M, __ldcg(g.part_lse + (cc * 2 + (cc == sp.c0 ? sp.first_slot : 0)) * g.GQ + gq));
+      }
+      for (int64_t cc = sp.c0; cc <= sp.c1; ++cc) {
+        if (!seg_nonempty(cc, N, T)) continue;
+        const int64_t sl = (cc * 2 + (cc == sp.c0 ? sp.first_slot : 0)) * g.GQ + gq;
+        const float w = exp2f((__ldcg(g.part_lse + sl) - M) * kLog2e);
+        const float4 ov = __ldcg(reinterpret_cast<const float4*>(g.part_o + sl * p.D + d));
+        L += w;
+        O[0] = fmaf(w, ov.x, O[0]);
+        O[1] = fmaf(w, ov.y, O[1]);
+        O[2] = fmaf(w, ov.z, O[2]);
+        O[3] = fmaf(w, ov.w, O[3]);
+      }
+    }
+    put4(p, dst_off + oi, make_float4(O[0] / L, O[1] / L, O[2] / L, O[3] / L));
+    if (d == 0) put1(p, dst_off + li, M + logf(L));
+  }
+}
+
+__global__ void __launch_bounds__(kXThreads) fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams p) {
+  const int cta = blockIdx.x;
+  // this CTA's own step counter (written only by this CTA of the previous
+  // launch, which has completed): read before waiting for the decode
+  const unsigned long long step = *reinterpret_cast<volatile const unsigned long long*>(p.steps + cta) + 1;
+  const int par = (int)(step & 1ull);
+  griddep_wait();  // the decode's output is complete (programmatic dependent launch)
+
+  // 1. push this rank's share to every rank
+  const int64_t dst_off = ((int64_t)par * p.world + p.rank) * p.slot;
+  if (p.geom.prefix != nullptr) {
+    push_segments(p, dst_off);
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(p.send);
+    const int64_t nvec = p.slot / 4;
+    for (int64_t c = (int64_t)cta * blockDim.x + threadIdx.x; c < nvec; c += (int64_t)gridDim.x * blockDim.x)
+      put4(p, dst_off + c * 4, __ldcg(src + c));
+  }
+  __syncthreads();  // the CTA's stores happen before thread 0's fence
+
+  // 2. this CTA's flag in every rank's buffer
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // the CTA's share is visible system-wide before its flag
+    for (int q = 0; q < p.world; ++q) st_relaxed_sys(p.flag_at[q] + cta, step);
+  }
+
+  // 3. every CTA of every rank delivered (each thread watches a few flags)
+  bool ok = true;
+  {
     const uint64_t t0 = globaltimer_ns();
-    uint32_t it = 0;
-    for (int q = 0; q < p.world && s_ok; ++q) {
-      while (ld_acquire_sys(p.flags + q) < step) {
-        if ((++it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
+    const int nf = p.world * gridDim.x;
+    for (int f = threadIdx.x; ok && f < nf; f += blockDim.x) {
+      const int q = f / gridDim.x, c = f - q * gridDim.x;
+      const unsigned long long* fl = p.flags + q * kXMaxCtas + c;
+      for (uint32_t it = 1; ld_relaxed_sys(fl) < step; ++it) {
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
           set_error(p.err, FD_DEVERR_TIMEOUT);
-          s_ok = 0;
+          ok = false;
           break;
         }
       }
     }
+    fence_acq_rel_sys();  // acquire: the shares behind the flags seen above are read after this
   }
-  __syncthreads();
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;
 
-  // 3. merge (one warp per (row, head) pair)
-  if (s_ok) {
+  // 4. merge (one warp per (row, head) pair)
+  if (ok) {
     const float* base = p.recv[p.rank] + (int64_t)par * p.world * p.slot;
     const int64_t o_floats = (int64_t)p.n * p.H * p.D;
     const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int64_t pairs = (int64_t)p.n * p.H;
-    for (int64_t pr = (int64_t)blockIdx.x * nw + (threadIdx.x >> 5); pr < pairs; pr += (int64_t)gridDim.x * nw) {
+    for (int64_t pr = (int64_t)cta * nw + (threadIdx.x >> 5); pr < pairs; pr += (int64_t)gridDim.x * nw) {
       const int i = (int)(pr / p.H), h = (int)(pr - (int64_t)i * p.H);
       const int64_t lo = o_floats + (int64_t)h * p.n + i;
       // lane q reads rank q's lse; every lane then holds all of them
@@ -167,26 +272,19 @@ __global__ void fd_exchange_merge_kernel(const __grid_constant__ ExchangeParams 
     }
   }
 
-  // 4. the last CTA of the step advances the step counter
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned long long prev = atomicAdd(p.done, 1ull);
-    if (prev + 1 == step * gridDim.x) {
-      __threadfence();
-      *reinterpret_cast<volatile unsigned long long*>(p.step) = step;
-    }
-  }
+  // 5. this CTA's step is done
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(p.steps + cta) = step;
 }
 
 }  // namespace fdk
 
 namespace {
-constexpr size_t kStepOffset = 0;
-constexpr size_t kDoneOffset = 8;
-constexpr size_t kPushedOffset = 16;
-constexpr size_t kFlagsOffset = 64;
-constexpr size_t kRecvOffset = 256;
-static_assert(kFlagsOffset + 8 * FD_MAX_PEERS <= kRecvOffset, "arrival flags overlap the receive buffer");
+constexpr size_t kStepsOffset = 0;
+constexpr size_t kFlagsOffset = FD_PEER_FLAGS_OFFSET;
+constexpr size_t kRecvOffset = FD_PEER_RECV_OFFSET;
+static_assert(kStepsOffset + 8 * fdk::kXMaxCtas <= kFlagsOffset, "step counters overlap the arrival flags");
+static_assert(kFlagsOffset + 8 * FD_MAX_PEERS * fdk::kXMaxCtas <= kRecvOffset,
+              "arrival flags overlap the receive buffer");
 }
 
 extern "C" size_t fd_peer_buffer_bytes(int32_t world, int64_t slot_floats) {
@@ -231,60 +329,64 @@ extern "C" int fd_peer_free(void* ptr) {
   return fdh::cuda_status(cudaFree(ptr), "fd_peer_free: cudaFree");
 }
 
-extern "C" int fd_exchange_merge(const fd_peer_exchange* x, const float* send, int32_t n, int32_t num_heads,
-                                 int32_t head_size, void* out, int32_t out_dtype, float* out_lse, int32_t num_ctas,
-                                 int64_t timeout_ns, int32_t* error, void* stream) {
-  if (x == nullptr || send == nullptr || out == nullptr)
-    return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: null argument");
+namespace {
+
+// Validate the exchange arguments and fill the kernel parameters (all but
+// the decode geometry).
+int exchange_params(const fd_peer_exchange* x, const float* send, int32_t n, int32_t num_heads, int32_t head_size,
+                    void* out, int32_t out_dtype, float* out_lse, int32_t num_ctas, int64_t timeout_ns,
+                    int32_t* error, const char* what, fdk::ExchangeParams* p, int* ctas) {
+  if (x == nullptr || send == nullptr || out == nullptr) return fdh::fail(FD_ERR_INVALID, "%s: null argument", what);
   if (x->world < 1 || x->world > FD_MAX_PEERS || x->rank < 0 || x->rank >= x->world)
-    return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: rank %d of world %d (at most %d)", x->rank, x->world,
-                     FD_MAX_PEERS);
-  if (n < 0 || num_heads < 1 || head_size < 1) return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: bad shape");
+    return fdh::fail(FD_ERR_INVALID, "%s: rank %d of world %d (at most %d)", what, x->rank, x->world, FD_MAX_PEERS);
+  if (n < 0 || num_heads < 1 || head_size < 1) return fdh::fail(FD_ERR_INVALID, "%s: bad shape", what);
   const int64_t need = (int64_t)n * num_heads * head_size + (int64_t)num_heads * n;
   if (x->slot_floats < need || x->slot_floats % 4 != 0)
-    return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: slot of %lld floats, need >= %lld and a multiple of 4",
+    return fdh::fail(FD_ERR_INVALID, "%s: slot of %lld floats, need >= %lld and a multiple of 4", what,
                      (long long)x->slot_floats, (long long)need);
-  if (fdh::elem_size(out_dtype) == 0) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_exchange_merge: out dtype");
+  if (fdh::elem_size(out_dtype) == 0) return fdh::fail(FD_ERR_UNSUPPORTED, "%s: out dtype", what);
   if ((reinterpret_cast<uintptr_t>(send) & 15u) != 0)
-    return fdh::fail(FD_ERR_ALIGN, "fd_exchange_merge: send buffer not 16-byte aligned");
+    return fdh::fail(FD_ERR_ALIGN, "%s: send buffer not 16-byte aligned", what);
   for (int q = 0; q < x->world; ++q)
-    if (x->base[q] == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: rank %d buffer unmapped", q);
-  constexpr int kThreads = 256;
-  const int ctas = num_ctas > 0 ? num_ctas : 32;
-  if (ctas > 64) return fdh::fail(FD_ERR_INVALID, "fd_exchange_merge: at most 64 CTAs (%d)", ctas);
-  fdk::ExchangeParams p{};
-  p.send = send;
+    if (x->base[q] == nullptr) return fdh::fail(FD_ERR_INVALID, "%s: rank %d buffer unmapped", what, q);
+  *ctas = num_ctas > 0 ? num_ctas : 32;
+  if (*ctas > fdk::kXMaxCtas) return fdh::fail(FD_ERR_INVALID, "%s: at most %d CTAs (%d)", what, fdk::kXMaxCtas, *ctas);
+  *p = fdk::ExchangeParams{};
+  p->send = send;
   unsigned char* own = static_cast<unsigned char*>(x->base[x->rank]);
   for (int q = 0; q < x->world; ++q) {
     unsigned char* b = static_cast<unsigned char*>(x->base[q]);
-    p.recv[q] = reinterpret_cast<float*>(b + kRecvOffset);
-    p.flag_at[q] = reinterpret_cast<unsigned long long*>(b + kFlagsOffset) + x->rank;
+    p->recv[q] = reinterpret_cast<float*>(b + kRecvOffset);
+    p->flag_at[q] = reinterpret_cast<unsigned long long*>(b + kFlagsOffset) + (size_t)x->rank * fdk::kXMaxCtas;
   }
-  p.flags = reinterpret_cast<const unsigned long long*>(own + kFlagsOffset);
-  p.step = reinterpret_cast<unsigned long long*>(own + kStepOffset);
-  p.done = reinterpret_cast<unsigned long long*>(own + kDoneOffset);
-  p.pushed = reinterpret_cast<unsigned long long*>(own + kPushedOffset);
-  p.rank = x->rank;
-  p.world = x->world;
-  p.n = n;
-  p.H = num_heads;
-  p.D = head_size;
-  p.slot = x->slot_floats;
-  p.out = out;
-  p.out_dtype = out_dtype;
-  p.out_lse = out_lse;
-  p.timeout_ns = timeout_ns > 0 ? timeout_ns : (int64_t)fdk::kWaitLimitNs;
-  p.err = error;
-  // Every CTA waits for every other.  A cooperative launch would guarantee
-  // co-residency but cost ~55 us per step on B200 (measured); at most 64
-  // CTAs of 256 threads and no shared memory are resident together on an
-  // otherwise idle stream, and the bounded wait turns any exception into
-  // FD_DEVERR_TIMEOUT rather than a hang.  Programmatic dependent launch:
-  // the CTAs may start while the kernel ahead on the stream finishes and
-  // wait for it in griddepcontrol.wait.
+  p->flags = reinterpret_cast<const unsigned long long*>(own + kFlagsOffset);
+  p->steps = reinterpret_cast<unsigned long long*>(own + kStepsOffset);
+  p->geom.prefix = nullptr;
+  p->rank = x->rank;
+  p->world = x->world;
+  p->n = n;
+  p->H = num_heads;
+  p->D = head_size;
+  p->slot = x->slot_floats;
+  p->out = out;
+  p->out_dtype = out_dtype;
+  p->out_lse = out_lse;
+  p->timeout_ns = timeout_ns > 0 ? timeout_ns : (int64_t)fdk::kWaitLimitNs;
+  p->err = error;
+  return FD_OK;
+}
+
+// Every CTA waits for every other.  A cooperative launch would guarantee
+// co-residency but cost ~55 us per step on B200 (measured); at most 64 CTAs
+// of 256 threads and no shared memory are resident together on an otherwise
+// idle stream, and the bounded wait turns any exception into
+// FD_DEVERR_TIMEOUT rather than a hang.  Programmatic dependent launch: the
+// CTAs may start while the kernel ahead on the stream finishes and wait for
+// it in griddepcontrol.wait.
+int launch_exchange(const fdk::ExchangeParams& p, int ctas, void* stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ctas);
-  cfg.blockDim = dim3((unsigned)kThreads);
+  cfg.blockDim = dim3((unsigned)fdk::kXThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
@@ -292,7 +394,56 @@ extern "C" int fd_exchange_merge(const fd_peer_exchange* x, const float* send, i
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, fdk::fd_exchange_merge_kernel, p);
-  if (e != cudaSuccess) return fdh::cuda_status(e, "fd_exchange_merge_kernel launch");
-  return fdh::cuda_status(cudaGetLastError(), "fd_exchange_merge_kernel launch");
+  return fdh::cuda_status(cudaLaunchKernelEx(&cfg, fdk::fd_exchange_merge_kernel, p), "fd_exchange_merge_kernel launch");
+}
+
+}  // namespace
+
+extern "C" int fd_exchange_merge(const fd_peer_exchange* x, const float* send, int32_t n, int32_t num_heads,
+                                 int32_t head_size, void* out, int32_t out_dtype, float* out_lse, int32_t num_ctas,
+                                 int64_t timeout_ns, int32_t* error, void* stream) {
+  fdk::ExchangeParams p;
+  int ctas = 0;
+  const int st = exchange_params(x, send, n, num_heads, head_size, out, out_dtype, out_lse, num_ctas, timeout_ns,
+                                 error, "fd_exchange_merge", &p, &ctas);
+  if (st != FD_OK) return st;
+  return launch_exchange(p, ctas, stream);
+}
+
+namespace {
+int decode_exchange(const fd_decode_args* a, const fd_peer_exchange* x, void* out, int32_t out_dtype, float* out_lse,
+                    int32_t num_ctas, int64_t timeout_ns, void* stream, bool decode, const char* what) {
+  if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "%s: null args", what);
+  const int64_t n = a->n, H = a->num_heads, D = a->head_size;
+  const float* send = static_cast<const float*>(a->out);
+  // the decode's output must be this rank's packed partial: fp32 o [n, H, D]
+  // contiguous, then lse [H, n]
+  if (a->out_dtype != FD_DTYPE_F32 || a->out_rows != nullptr || a->out_stride_h != D || a->out_stride_n != H * D ||
+      a->lse != send + n * H * D || a->lse_stride_h != n || a->lse_stride_n != 1)
+    return fdh::fail(FD_ERR_INVALID,
+                     "%s: the decode must write fp32 o [n, H, D] and lse [H, n] packed back to back (the "
+                     "exchange's send buffer), without out_rows", what);
+  if (D % 4 != 0) return fdh::fail(FD_ERR_UNSUPPORTED, "%s: head_size must be a multiple of 4", what);
+  fdk::ExchangeParams p;
+  int ctas = 0;
+  int st = exchange_params(x, send, a->n, a->num_heads, a->head_size, out, out_dtype, out_lse, num_ctas, timeout_ns,
+                           a->error, what, &p, &ctas);
+  if (st != FD_OK) return st;
+  st = fdk::launch_decode_for_exchange(a, stream, &p.geom, decode);
+  if (st != FD_OK) return st;
+  return launch_exchange(p, ctas, stream);
+}
+}  // namespace
+
+extern "C" int fd_decode_exchange_merge(const fd_decode_args* a, const fd_peer_exchange* x, void* out,
+                                        int32_t out_dtype, float* out_lse, int32_t num_ctas, int64_t timeout_ns,
+                                        void* stream) {
+  return decode_exchange(a, x, out, out_dtype, out_lse, num_ctas, timeout_ns, stream, true, "fd_decode_exchange_merge");
+}
+
+extern "C" int fd_exchange_merge_decoded(const fd_decode_args* a, const fd_peer_exchange* x, void* out,
+                                         int32_t out_dtype, float* out_lse, int32_t num_ctas, int64_t timeout_ns,
+                                         void* stream) {
+  return decode_exchange(a, x, out, out_dtype, out_lse, num_ctas, timeout_ns, stream, false,
+                         "fd_exchange_merge_decoded");
 }

@@ -11,7 +11,8 @@ the reference itself has no multi-GPU path.
 Two exchanges with the same interface: PartialExchange (NCCL all-gather,
 then the merge kernel) and PeerExchange (fd_exchange_merge: one kernel per
 step pushes the partial into every rank's buffer over NVLink, waits for
-every rank's and merges; buffers shared with CUDA IPC, no multicast).
+every rank's and merges; buffers shared with CUDA IPC, no multicast; with
+decode_exchange_merge the same kernel also does the decode's combine).
 
 One process per GPU (torchrun); the process group is the caller's.
 """
@@ -179,6 +180,30 @@ class PeerExchange:
             self.failed = str(e)
             raise
 
+    def decode_exchange_merge(self, args, final: torch.Tensor, decode: bool = True) -> None:
+        """The whole sharded step (C ABI fd_decode_exchange_merge): the decode
+        of `args` (gpu_ops.decode_args writing o_view / lse_view, fp32), then
+        one exchange launch that also merges the segments the decode's CTAs
+        cut, so no combine launch runs in between.  `final` [n, H, D].
+        decode=False: only the exchange (fd_exchange_merge_decoded), after the
+        caller's own gpu_ops.launch_decode(args, ..., "partials")."""
+        import ctypes
+
+        nat = self._nat
+        if self.failed is not None:
+            raise RuntimeError(f"PeerExchange is unusable after a failed step ({self.failed}): close it on every "
+                               "rank and build a new one")
+        if not (final.is_contiguous() and tuple(final.shape) == (self.n, self.H, self.D)):
+            raise RuntimeError("PeerExchange: final must be a contiguous [n, H, D] tensor")
+        if args.out != self.o_view.data_ptr() or args.lse != self.lse_view.data_ptr():
+            raise RuntimeError("PeerExchange: the decode must write this exchange's o_view / lse_view")
+        from vllm_fastdecoder_b200 import gpu_ops
+
+        fn = self._lib.fd_decode_exchange_merge if decode else self._lib.fd_exchange_merge_decoded
+        nat.check(fn(ctypes.byref(args), ctypes.byref(self.x), final.data_ptr(), gpu_ops.dtype_code(final.dtype),
+                     self.lse_out.data_ptr(), self.num_ctas, self.timeout_ns, gpu_ops._stream(self.device)),
+                  "fd_decode_exchange_merge" if decode else "fd_exchange_merge_decoded")
+
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (collective)."""
         if self._own is None:
@@ -195,9 +220,17 @@ class PeerExchange:
 
 def sharded_decode(q: torch.Tensor, tiers, tier_split: int, local_bt: torch.Tensor, local_lens: torch.Tensor,
                    scale: float, exchange: PartialExchange, final: torch.Tensor, **kw) -> None:
-    """One decode step over the local shard followed by the exchange + merge."""
+    """One decode step over the local shard followed by the exchange + merge
+    (over peer memory: one decode launch and one exchange launch that also
+    combines the decode's cut segments)."""
     from vllm_fastdecoder_b200 import gpu_ops
 
+    if isinstance(exchange, PeerExchange) and kw.get("host_range") is None:
+        kw.pop("host_range", None)
+        a = gpu_ops.decode_args(q, tiers, tier_split, local_bt, local_lens, scale, exchange.o_view,
+                                exchange.lse_view, **kw)
+        exchange.decode_exchange_merge(a, final)
+        return
     gpu_ops.decode_tiered(q, tiers, tier_split, local_bt, local_lens, scale, exchange.o_view, exchange.lse_view,
                           **kw)
     exchange.exchange_and_merge(None, None, final)
