@@ -370,6 +370,11 @@ def run_ours(args, ws, rank, device):
     # copy engine each step and read at HBM rate
     staged = args.host_read == "staged" and res.tiers[1] is not None
     host_range = gpu_ops.host_block_range(batch.block_table, batch.lens, batch.BS, batch.G) if staged else None
+    # chunked: host blocks staged in chunks on a side stream, each chunk
+    # decoded into partials once it has landed, then one P-way merge
+    chunked = args.host_read == "chunked" and res.tiers[1] is not None
+    cplan = (gpu_ops.plan_chunked_staging(batch.block_table, batch.lens, batch.BS, batch.G, args.stage_chunks)
+             if chunked else None)
     dec_tiers, dec_split = res.tiers, batch.G
     if staged:
         dec_tiers = (res.tiers[0], gpu_ops.stage_host_blocks(res.tiers[1], *host_range, device))
@@ -398,6 +403,13 @@ def run_ours(args, ws, rank, device):
                 ev[1].record()
 
     def step(ev=None, cev=None):
+        if chunked:  # the whole overlapped step (copies, decodes, merge) is the timed unit
+            if ev is not None:
+                ev[0].record()
+            gpu_ops.decode_staged_chunks(res.q, res.tiers, batch.scale, out, lse, cplan)
+            if ev is not None:
+                ev[1].record()
+            return
         stage(cev)
         if ev is not None:
             ev[0].record()
@@ -424,7 +436,13 @@ def run_ours(args, ws, rank, device):
         a_g = gpu_ops.decode_args(res.q, dec_tiers, dec_split, res.block_table, res.lens, batch.scale, out, lse,
                                   max_len=max_len, tiles_per_split=tps, workspace_buf=ws_g)
 
+        parts_g = (torch.empty((1 + len(cplan.chunks)) * (n * H * D + H * n), dtype=torch.float32, device=device)
+                   if chunked else None)
+
         def gstep():
+            if chunked:
+                gpu_ops.decode_staged_chunks(res.q, res.tiers, batch.scale, out, lse, cplan, parts_buf=parts_g)
+                return
             stage()
             if fused:
                 gather.decode_exchange_merge(a_g, final)  # decode, then the exchange with the combine in it
@@ -548,7 +566,10 @@ def run_ours(args, ws, rank, device):
         # the staged range comes from the step's host-side table, as a caller
         # holding the plan on the host would compute it
         hr = gpu_ops.host_block_range(h_bt, h_lens, batch.BS, batch.G) if staged else None
-        if fused:
+        if chunked:
+            cp = gpu_ops.plan_chunked_staging(h_bt, h_lens, batch.BS, batch.G, args.stage_chunks)
+            gpu_ops.decode_staged_chunks(d_q, res.tiers, batch.scale, out, lse, cp)
+        elif fused:
             from vllm_fastdecoder_b200 import sharded as sh
 
             sh.sharded_decode(d_q, res.tiers, batch.G, d_bt, d_lens, batch.scale, gather, final, max_len=max_len,
@@ -579,6 +600,8 @@ def run_ours(args, ws, rank, device):
         e2e_t = float(t[0])
     gpu_ops.check_device_errors(device)
     h2d = h_q.numel() * h_q.element_size() + h_bt.numel() * 4 + h_lens.numel() * 4
+    if chunked:  # the per-part tables and lengths, copied to the device by each step's call
+        h2d += 4 * sum(t.numel() for t in cplan.tables) + 4 * sum(ln.numel() for ln in cplan.lens)
     d2h = h_out.numel() * h_out.element_size() + h_lse.numel() * 4
 
     # ---- roofline of the decode kernel (per launch, this rank's batch)
@@ -599,7 +622,16 @@ def run_ours(args, ws, rank, device):
         pcie = pcie_h2d_gbs(device)
         t_ideal = (step_b - host_b) / (peaks["hbm_gbs"] * 1e9) + host_b / (pcie * 1e9)
         t_step = kern_t + copy_t  # staged: the host-tier copy, then the decode at HBM rate
-        if staged:
+        if chunked:
+            # overlapped: the copies bound the step (the HBM-tier bytes and the
+            # decode of landed chunks run under them)
+            t_ideal = max(host_b / (pcie * 1e9), step_b / (peaks["hbm_gbs"] * 1e9))
+            roof.update({"achieved": round(step_b / t_step / 1e9, 1),
+                         "host_read": f"chunked: host blocks staged in {len(cplan.chunks)} chunks on a side stream, "
+                                      "each decoded into partials once landed (HBM blocks first), then one P-way "
+                                      "merge; achieved and frac over the whole step (kernel_ms), ideal = the "
+                                      "host-tier copy at the pinned-copy rate"})
+        elif staged:
             roof.update({"achieved": round(step_b / t_step / 1e9, 1), "copy_ms": round(copy_t * 1e3, 4),
                          "host_read": "staged: host blocks copied to HBM by the copy engine (cudaMemcpyAsync), "
                                       "then decoded at HBM rate; achieved and frac over copy + kernel"})
@@ -655,7 +687,8 @@ def run_ours(args, ws, rank, device):
                         + (" + the exchange and merge" if gather is not None else ""))},
         "roofline": roof,
         "clocks": clk,
-        "gpu_launches": args.steps * (1 + int(has_combine) + (1 if gather is not None else 0)),
+        "gpu_launches": args.steps * ((1 + len(cplan.chunks)) * (1 + int(has_combine)) + 1 if chunked else
+                                      1 + int(has_combine) + (1 if gather is not None else 0)),
     }
     if parity is not None:
         line["parity"] = parity
@@ -1041,8 +1074,10 @@ def main() -> int:
                     help="c3 on N > 1 GPUs: partials exchanged over peer memory by the exchange kernel that also "
                          "does the decode's combine (peer), by the decode's combine and then the exchange kernel "
                          "(peer-split), or with an NCCL all-gather and a merge kernel (nccl)")
-    ap.add_argument("--host-read", choices=["staged", "mapped"], default="staged",
-                    help="host tier: staged into HBM by the copy engine each step, or read in place over PCIe")
+    ap.add_argument("--host-read", choices=["staged", "chunked", "mapped"], default="staged",
+                    help="host tier: staged into HBM by the copy engine each step, staged in chunks on a side "
+                         "stream with the decode of landed chunks overlapping the copies, or read in place over PCIe")
+    ap.add_argument("--stage-chunks", type=int, default=8, help="--host-read chunked: chunks per step")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of a captured CUDA graph of the step")
     ap.add_argument("--ctx", type=int, default=131072,

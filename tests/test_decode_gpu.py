@@ -239,6 +239,23 @@ def test_decode_fp32_partials_and_row_maps(ops):
     assert torch.all(got[untouched] == 0)
 
 
+def test_row_maps_must_be_int64(ops):
+    """q_rows / out_rows are read as int64 by the kernels: any other dtype is
+    refused on the host, before a launch."""
+    from vllm_fastdecoder_b200.gpu_ops import KVTier
+
+    dev = torch.device("cuda")
+    n, H, KVH, D, BS, C = 2, 8, 2, 128, 16, 8
+    q, kc, vc, bt, lens = O.rand_case(n, H, KVH, D, BS, C, torch.bfloat16, max_len=40, seed=4)
+    out = torch.zeros(n, H, D, dtype=torch.bfloat16, device=dev)
+    tiers = (KVTier(kc.to(dev), vc.to(dev)), None)
+    rows32 = torch.arange(n, dtype=torch.int32, device=dev)
+    for kw in ({"q_rows": rows32}, {"out_rows": rows32}, {"q_rows": torch.arange(n)}):
+        with pytest.raises(RuntimeError, match="int64"):
+            ops.decode_tiered(q.to(dev), tiers, 1 << 40, bt.to(dev), lens.to(dev), D ** -0.5, out, None, **kw)
+    torch.cuda.synchronize()
+
+
 def test_decode_bad_block_id_sets_error(ops):
     """An out-of-range block id is reported through the error word (no fault)."""
     dev = torch.device("cuda")
@@ -288,6 +305,57 @@ def test_staged_host_tier_equals_mapped(ops, H, KVH):
         outs.append((out.cpu(), lse.cpu()))
     assert ops.host_block_range(bt, lens, BS, G)[0] >= 5
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("H,KVH", [(8, 8), (16, 4)])
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_staged_chunks_match_oracle(ops, H, KVH, chunks):
+    """Host tier staged in chunks on a side stream, each chunk's blocks
+    decoded into fp32 partials once its copy has landed, the HBM blocks
+    first, then one P-way merge (decode_staged_chunks): matches the oracle
+    over the whole two-tier rows (row maps on q and out, an empty row, rows
+    with no host block, rows whose last partly filled block sits in any
+    chunk), over two calls in a row on the same staging buffer."""
+    from vllm_fastdecoder_b200.gpu_ops import KVTier
+
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(7 * H + chunks)
+    D, BS, G, C, n = 128, 16, 40, 80, 8
+    dt = torch.bfloat16
+    hk = torch.randn(G, KVH, BS, D, generator=g).to(dt)
+    hv = torch.randn(G, KVH, BS, D, generator=g).to(dt)
+    ck = torch.randn(C, KVH, BS, D, generator=g).to(dt).pin_memory()
+    cv = torch.randn(C, KVH, BS, D, generator=g).to(dt).pin_memory()
+    lens = torch.tensor([1, 90, 0, 300, 17, 64, 200, 33], dtype=torch.int32)
+    W = 20
+    bt = torch.zeros(n, W, dtype=torch.int32)
+    ids = torch.randperm(G - 1, generator=g).tolist()
+    host = (torch.randperm(C - 10, generator=g) + 5).tolist()
+    for i in range(n):
+        nb = (int(lens[i]) + BS - 1) // BS
+        for j in range(nb):
+            bt[i, j] = (host.pop() + G) if (j % 3 and i != 5) else ids.pop()  # row 5: HBM only
+    T = n + 3
+    q_rows = torch.randperm(T, generator=g)[:n]  # int64, as fd_decode_args reads them
+    out_rows = torch.randperm(T, generator=g)[:n]
+    qa = torch.randn(T, H, D, generator=g).to(dt)
+    tiers = (KVTier(hk.to(dev), hv.to(dev)), KVTier(ck, cv))
+    plan = ops.plan_chunked_staging(bt, lens, BS, G, chunks)
+    assert len(plan.chunks) == min(chunks, plan.hi - plan.lo)
+    ref = torch.empty(n, H, D, dtype=dt)
+    ref_l = torch.empty(H, n)
+    O.decode_attn_tiered(qa[q_rows], (hk, hv), (ck, cv), G, bt, lens, D ** -0.5, ref, ref_l)
+    nz = lens > 0
+    for _ in range(2):
+        out = torch.full((T, H, D), float("nan"), dtype=dt, device=dev)
+        lse = torch.full((H, n), float("nan"), dtype=torch.float32, device=dev)
+        ops.decode_staged_chunks(qa.to(dev), tiers, D ** -0.5, out, lse, plan, q_rows=q_rows.to(dev),
+                                 out_rows=out_rows.to(dev))
+        ops.check_device_errors(dev)
+        o = out.cpu()[out_rows]
+        assert (o[nz].float() - ref[nz].float()).abs().max().item() <= TOL_ORACLE[dt]
+        assert (lse.cpu()[:, nz] - ref_l[:, nz]).abs().max().item() <= LSE_TOL
+        assert torch.all(o[~nz] == 0) and torch.all(torch.isneginf(lse.cpu()[:, ~nz]))
 
 
 @pytest.mark.parametrize("vtiles", ["0", "1", "12", "40"])

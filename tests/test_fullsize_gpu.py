@@ -11,7 +11,8 @@ lse 1e-4 absolute; KV writes bit-exact.
 
   c0  16 rows, one 4096-block fp16 pool (CUDA-core kernel)
   c1  64 rows over the 2048-block HBM tier and the pinned host tier, read in
-      place over PCIe and staged into HBM by the copy engine
+      place over PCIe, staged into HBM by the copy engine, and staged in
+      chunks on a side stream with the decode overlapping the copies
   c2  256 GQA bf16 rows, lognormal lengths (tensor-core kernel)
   c3  8 rows x 131072 tokens on one GPU, and the same context cut into four
       shards (decoded separately on this GPU into fp32 partials and merged by
@@ -50,14 +51,18 @@ def _check(out, lse, ref, ref_l, lens, dtype):
     return err_o, err_l
 
 
-def _decode_and_check(batch, res, dev, host_range=None):
+def _decode_and_check(batch, res, dev, host_range=None, chunks=0):
     from vllm_fastdecoder_b200 import gpu_ops
 
     n, H, D = batch.n, batch.H, batch.D
     out = torch.full((n, H, D), float("nan"), dtype=batch.dtype, device=dev)
     lse = torch.full((H, n), float("nan"), dtype=torch.float32, device=dev)
-    gpu_ops.decode_tiered(res.q, res.tiers, batch.G, res.block_table, res.lens, batch.scale, out, lse,
-                          max_len=int(batch.lens.max()), host_range=host_range)
+    if chunks:
+        plan = gpu_ops.plan_chunked_staging(batch.block_table, batch.lens, batch.BS, batch.G, chunks)
+        gpu_ops.decode_staged_chunks(res.q, res.tiers, batch.scale, out, lse, plan)
+    else:
+        gpu_ops.decode_tiered(res.q, res.tiers, batch.G, res.block_table, res.lens, batch.scale, out, lse,
+                              max_len=int(batch.lens.max()), host_range=host_range)
     gpu_ops.check_device_errors(dev)
     ref = torch.empty(n, H, D, dtype=batch.dtype)
     ref_l = torch.empty(H, n)
@@ -86,6 +91,7 @@ def test_config1_full_size_mapped_and_staged():
     _decode_and_check(b, res, dev)  # host tier read in place over PCIe
     hr = gpu_ops.host_block_range(b.block_table, b.lens, b.BS, b.G)
     _decode_and_check(b, res, dev, host_range=hr)  # staged by the copy engine
+    _decode_and_check(b, res, dev, chunks=8)  # staged in 8 chunks on a side stream, overlapping the decode
 
 
 def test_config2_full_size():

@@ -208,6 +208,187 @@ def host_block_range(block_table: torch.Tensor, lens: torch.Tensor, block_size: 
     return int(ids.min()) - tier_split, int(ids.max()) - tier_split + 1
 
 
+@dataclass
+class ChunkedStaging:
+    """One step's host-tier blocks cut into chunks that are staged into HBM
+    one after another on a side stream (plan_chunked_staging).  Part 0 is
+    every row's HBM-tier blocks; part j (1..k) is every row's host blocks
+    with host-relative ids in chunks[j - 1] = [c_lo, c_hi).  Per part,
+    `tables[p]` (int32 [n, W_p], CPU) lists a row's blocks of that part in
+    table order, the row's last (partly filled) block moved to the end, with
+    ids as the part's decode reads them (HBM ids for part 0, ids relative to
+    the staged range [lo, hi) for the others), and `lens[p]` (int32 [n]) is
+    the tokens they hold (0: the row has no block in the part)."""
+
+    lo: int
+    hi: int
+    chunks: list[tuple[int, int]]
+    tables: list[torch.Tensor]
+    lens: list[torch.Tensor]
+    _dev: dict | None = None
+
+    def on(self, device: torch.device) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        """(table, lens) of every part on `device`, copied once (one packed
+        host-to-device copy) and cached, so that a step captured in a CUDA
+        graph copies nothing."""
+        key = str(device)
+        if self._dev is None:
+            self._dev = {}
+        if key not in self._dev:
+            flat = torch.cat([t.flatten() for t in self.tables] + list(self.lens)).to(device)
+            out, o = [], 0
+            for t in self.tables:
+                out.append(flat[o:o + t.numel()].view(t.shape))
+                o += t.numel()
+            lens = []
+            for ln in self.lens:
+                lens.append(flat[o:o + ln.numel()])
+                o += ln.numel()
+            self._dev[key] = list(zip(out, lens))
+        return self._dev[key]
+
+
+def plan_chunked_staging(block_table: torch.Tensor, lens: torch.Tensor, block_size: int, tier_split: int,
+                         chunks: int) -> ChunkedStaging:
+    """Cut a step's host-tier range [lo, hi) into `chunks` equal block ranges
+    and build the per-part block tables of ChunkedStaging from CPU copies of
+    the step's block table and lengths (blocks may lie anywhere in the range:
+    each part holds whichever of a row's blocks fall into it)."""
+    _check(chunks >= 1, "plan_chunked_staging: chunks must be >= 1")
+    n, W = block_table.shape
+    BS = block_size
+    L = lens.to(torch.int64).clamp(min=0)
+    nb = ((L + BS - 1) // BS).clamp(max=W)
+    col = torch.arange(W).unsqueeze(0).expand(n, W)
+    used = col < nb.unsqueeze(1)
+    ids = block_table.to(torch.int64)
+    host = used & (ids >= tier_split)
+    rel = ids - tier_split
+    if bool(host.any()):
+        lo, hi = int(rel[host].min()), int(rel[host].max()) + 1
+    else:
+        lo = hi = 0
+    k = max(1, min(chunks, hi - lo)) if hi > lo else 0
+    bounds = [lo + ((hi - lo) * j) // k for j in range(k + 1)] if k else []
+    spans = [(bounds[j], bounds[j + 1]) for j in range(k)]
+    last = col == (nb - 1).unsqueeze(1)  # the row's last block (L - (nb-1)*BS tokens)
+    tail = (L - (nb - 1).clamp(min=0) * BS).unsqueeze(1).expand(n, W)
+    tok = torch.where(last, tail, torch.full_like(tail, BS))
+    masks = [used & (ids < tier_split)] + [host & (rel >= c_lo) & (rel < c_hi) for c_lo, c_hi in spans]
+    tables, part_lens = [], []
+    for p, m in enumerate(masks):
+        key = torch.where(m, torch.where(last, torch.full_like(col, W), col), torch.full_like(col, 2 * W))
+        order = key.argsort(dim=1, stable=True)
+        cnt = m.sum(dim=1)
+        wp = max(1, int(cnt.max()) if n else 1)
+        vals = (ids if p == 0 else rel - lo).gather(1, order)[:, :wp]
+        keep = torch.arange(wp).unsqueeze(0) < cnt.unsqueeze(1)
+        tables.append(torch.where(keep, vals, torch.zeros_like(vals)).to(torch.int32).contiguous())
+        part_lens.append(torch.where(m, tok, torch.zeros_like(tok)).sum(dim=1).to(torch.int32))
+    return ChunkedStaging(lo, hi, spans, tables, part_lens)
+
+
+_SIDE: dict[int, torch.cuda.Stream] = {}
+_PARTS: dict[int, torch.Tensor] = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _SIDE.get(idx)
+    if st is None:
+        st = torch.cuda.Stream(torch.device("cuda", idx))
+        _SIDE[idx] = st
+    return st
+
+
+def decode_staged_chunks(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None],
+                         scale: float, out: torch.Tensor, lse: torch.Tensor | None, plan: ChunkedStaging, *,
+                         q_rows: torch.Tensor | None = None, out_rows: torch.Tensor | None = None,
+                         parts_buf: torch.Tensor | None = None) -> None:
+    """Decode over an HBM tier and a pinned host tier whose blocks are
+    staged into HBM chunk by chunk, the copies overlapping the decode.
+
+    The copy engine copies chunk j of `plan` into the staging buffer on a
+    side stream and records an event; on the current stream the HBM-tier
+    blocks are decoded first (while the first chunk copies), then each
+    chunk's blocks once its event has fired, every part into fp32 partials
+    (o, lse), and one P-way log-sum-exp merge (fd_merge_partials) combines
+    the k + 1 partials into `out` (rows out_rows[i] or i) and `lse` [H, n].
+    Only the last chunk's decode and the merge follow the last copy.  The
+    staging buffer is the one stage_host_blocks uses; the side stream waits
+    for earlier work on the current stream before overwriting it.  The
+    side stream forks from and joins the current stream, so a step can be
+    captured in a CUDA graph (`parts_buf`: fp32 partials owned by the
+    caller, e.g. for a captured step)."""
+    host = tiers[1]
+    _check(host is not None and host.host, "decode_staged_chunks: tiers[1] must be the pinned host tier")
+    _check(host.k.is_contiguous() and host.v.is_contiguous(), "decode_staged_chunks: host tier must be contiguous")
+    dev = q.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    n = plan.tables[0].shape[0]
+    H, D = q.shape[-2], q.shape[-1]
+    P = 1 + len(plan.chunks)
+    stride = n * H * D + H * n
+    if parts_buf is None:
+        parts_buf = _PARTS.get(idx)
+        if parts_buf is None or parts_buf.numel() < P * stride:
+            parts_buf = torch.empty(P * stride, dtype=torch.float32, device=dev)
+            _PARTS[idx] = parts_buf
+    _check(parts_buf.dtype == torch.float32 and parts_buf.numel() >= P * stride, "parts_buf too small")
+    parts = parts_buf[: P * stride].view(P, stride)
+    main = torch.cuda.current_stream(dev)
+    side = _side_stream(dev)
+    lo, hi = plan.lo, plan.hi
+    per = host.k[0].numel()
+    need = 2 * max(1, hi - lo) * per
+    buf = _STAGE.get(idx)
+    if buf is None or buf.numel() < need or buf.dtype != host.k.dtype:
+        buf = torch.empty(need, dtype=host.k.dtype, device=torch.device("cuda", idx))
+        _STAGE[idx] = buf
+    shape = (max(1, hi - lo),) + tuple(host.k.shape[1:])
+    kb = buf[: need // 2].view(shape)
+    vb = buf[need // 2: need].view(shape)
+    staged = KVTier(kb, vb)
+    dev_parts = plan.on(dev)
+
+    def part(p: int, t: tuple[KVTier | None, KVTier | None], split: int) -> None:
+        bt, ln = dev_parts[p]
+        o = parts[p, : n * H * D].view(n, H, D)
+        ls = parts[p, n * H * D:].view(H, n)
+        a = decode_args(q, t, split, bt, ln, scale, o, ls, q_rows=q_rows,
+                        max_len=int(plan.lens[p].max()) if n else 0)
+        launch_decode(a, dev)
+
+    ready = torch.cuda.Event()
+    ready.record(main)  # earlier readers of the staging buffer come first
+    side.wait_event(ready)
+    evs = []
+    with torch.cuda.stream(side):
+        for c_lo, c_hi in plan.chunks:
+            kb[c_lo - lo: c_hi - lo].copy_(host.k[c_lo:c_hi], non_blocking=True)
+            vb[c_lo - lo: c_hi - lo].copy_(host.v[c_lo:c_hi], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            evs.append(ev)
+    # no record_stream for the side stream: every use of the buffer there is
+    # followed, on the current stream, by a wait on its event, so the
+    # buffer's lifetime on the current stream covers the side stream's too
+    if tiers[0] is not None:
+        part(0, (tiers[0], None), 1 << 40)
+    else:
+        parts[0, : n * H * D].zero_()
+        parts[0, n * H * D:].fill_(float("-inf"))
+    for j, ev in enumerate(evs):
+        main.wait_event(ev)
+        part(j + 1, (None, staged), 0)
+    if out_rows is None:
+        merge_partials(parts, P, n, H, D, out, lse)
+    else:
+        tmp = torch.empty(n, H, D, dtype=out.dtype, device=dev)
+        merge_partials(parts, P, n, H, D, tmp, lse)
+        out.index_copy_(0, out_rows.to(torch.int64), tmp)
+
+
 # ------------------------------------------------------------- decode
 
 
@@ -258,6 +439,10 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
     if bt_rows is not None:
         _check(bt_rows.dtype == torch.int32 and bt_rows.device == dev and bt_rows.numel() >= n,
                "bt_rows must be int32 on q's device with n entries")
+    for nm, rows in (("q_rows", q_rows), ("out_rows", out_rows)):
+        if rows is not None:  # the kernels read them as int64 (fd_decode_args)
+            _check(rows.dtype == torch.int64 and rows.device == dev and rows.is_contiguous() and rows.numel() >= n,
+                   f"{nm} must be a contiguous int64 tensor on q's device with n entries")
     _check(block_table.dtype == torch.int32 and lens.dtype == torch.int32, "block_table and lens must be int32")
     _check(block_table.stride(-1) == 1, "block_table rows must be contiguous")
     _check(block_table.device == dev and lens.device == dev, "block_table and lens must be on q's device")
@@ -455,6 +640,9 @@ def merge_attn_states(out: torch.Tensor, o_a: torch.Tensor, lse_a: torch.Tensor,
     _check(lse_a.is_contiguous() and lse_b.is_contiguous(), "lse must be contiguous")
     _check(out.stride(-1) == 1 and out.stride(1) == D, "out rows must be [H, D] contiguous")
     dev = o_a.device
+    if out_rows is not None:  # read as int64 by the kernel
+        _check(out_rows.dtype == torch.int64 and out_rows.device == dev and out_rows.is_contiguous()
+               and out_rows.numel() >= n, "out_rows must be a contiguous int64 tensor on the device with n entries")
     nat.check(nat.load().fd_merge_attn_states(
         out.data_ptr(), dtype_code(out.dtype), out.stride(0), _ptr(out_rows), _ptr(out_lse),
         o_a.data_ptr(), lse_a.data_ptr(), o_b.data_ptr(), lse_b.data_ptr(), dtype_code(o_a.dtype),

@@ -16,6 +16,11 @@ serves (and larger than the 126 MB L2 where the kernel streams data):
                     D128 (config 3's merge at 8 GPUs)
   split_merge       fd_split_merge_kernel: the split-grid combine of config 2
                     (tiles_per_split 16)
+  combine           fd_persistent_combine_kernel: the persistent schedule's
+                    merge of cut segments, config 2
+  host_mapped       fd_decode_kernel reading only the host tier in place over
+                    PCIe (pinned, device-mapped): 16 rows x 4096 tokens, 32/32
+                    heads, D128, fp16 (1.07 GB in host memory)
   plan              fd_plan_kernel: the device planner on a 128-request
                     decode step of the config-4 trace
   exchange1         fd_exchange_merge_kernel with one rank (push, flags, merge
@@ -23,7 +28,9 @@ serves (and larger than the 126 MB L2 where the kernel streams data):
 
 Each line: the kernel, the mean device time per launch (CUDA events around
 `--launches` back-to-back launches after warm-up), the algorithmic bytes per
-launch, and achieved GB/s against the measured HBM copy rate.
+launch, and achieved GB/s against the measured HBM copy rate (for
+host_mapped: against a pinned host-to-device cudaMemcpyAsync of the same
+bytes timed in the same run, and against PCIe Gen5 x16's nominal 63 GB/s).
 """
 
 from __future__ import annotations
@@ -39,6 +46,7 @@ from vllm_fastdecoder_b200 import gpu_ops, workloads
 from vllm_fastdecoder_b200.gpu_ops import KVTier
 
 ROOT = Path(__file__).resolve().parents[1]
+PCIE5_X16_GBS = 63.0  # PCIe Gen5 x16, per direction, nominal (32 GT/s x 16 lanes, 128b/130b)
 
 
 def _hbm_peak() -> float:
@@ -122,6 +130,58 @@ def case_split_merge(dev):
     return (lambda: gpu_ops.launch_decode(a, dev, "combine")), nbytes, "fd_split_merge_kernel"
 
 
+def case_combine(dev):
+    b = workloads.config2()
+    res = workloads.materialize(b, dev)
+    out = torch.empty(b.n, b.H, b.D, dtype=b.dtype, device=dev)
+    lse = torch.empty(b.H, b.n, dtype=torch.float32, device=dev)
+    a = gpu_ops.decode_args(res.q, res.tiers, b.G, res.block_table, res.lens, b.scale, out, lse,
+                            max_len=int(b.lens.max()))
+    gpu_ops.launch_decode(a, dev, "partials")
+    torch.cuda.synchronize()
+    # every decode CTA's two fp32 partial slots (GQ heads of D + 1 floats)
+    # are read at most once, and one merged segment (GQ heads of D outputs
+    # and an lse) is written per CTA at most: an upper bound of the bytes the
+    # kernel must move.  The tensor-core decode runs one CTA per SM.
+    ctas = torch.cuda.get_device_properties(dev).multi_processor_count
+    gq = b.H // b.KVH
+    nbytes = ctas * 2 * gq * (b.D + 1) * 4 + ctas * gq * (b.D * 2 + 4)
+    return (lambda: gpu_ops.launch_decode(a, dev, "combine")), nbytes, "fd_persistent_combine_kernel"
+
+
+def case_host_mapped(dev):
+    n, H, D, BS, L, dt = 16, 32, 128, 16, 4096, torch.float16
+    nb = L // BS
+    C = n * nb
+    g = torch.Generator().manual_seed(3)
+    hk = torch.empty(C, H, BS, D, dtype=dt, pin_memory=True)
+    hv = torch.empty(C, H, BS, D, dtype=dt, pin_memory=True)
+    tmp = torch.empty(nb, H, BS, D, dtype=dt, device=dev)
+    for dst in (hk, hv):
+        for r in range(n):
+            tmp.normal_()
+            dst[r * nb:(r + 1) * nb].copy_(tmp)
+    del tmp
+    bt = torch.randperm(C, generator=g).to(torch.int32).view(n, nb).to(dev)  # host ids from tier_split 0
+    lens = torch.full((n,), L, dtype=torch.int32, device=dev)
+    q = torch.randn(n, H, D, dtype=dt, device=dev)
+    out = torch.empty(n, H, D, dtype=dt, device=dev)
+    lse = torch.empty(H, n, dtype=torch.float32, device=dev)
+    tiers = (None, KVTier(hk, hv))
+    torch.cuda.synchronize()
+    nbytes = 2 * n * L * H * D * 2 + n * H * (2 * D * 2 + 4) + n * nb * 4
+    return (lambda: gpu_ops.decode_tiered(q, tiers, 0, bt, lens, 1.0 / math.sqrt(D), out, lse)), nbytes, \
+        "fd_decode_kernel"
+
+
+def pinned_copy_gbs(dev, nbytes: int = 1 << 30) -> float:
+    """Pinned host-to-device cudaMemcpyAsync rate (GB/s), the PCIe reference."""
+    src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    t = _time(lambda: dst.copy_(src, non_blocking=True), 5, warmup=2)
+    return nbytes / t / 1e9
+
+
 def case_plan(dev):
     from vllm_fastdecoder_b200 import plan
 
@@ -157,6 +217,8 @@ CASES = {
     "merge2": case_merge2,
     "merge_partials": case_merge_partials,
     "split_merge": case_split_merge,
+    "combine": case_combine,
+    "host_mapped": case_host_mapped,
     "plan": case_plan,
     "exchange1": case_exchange1,
 }
@@ -175,9 +237,16 @@ def main() -> None:
         t = _time(fn, args.launches)
         gpu_ops.check_device_errors(dev)
         gbs = nbytes / t / 1e9
-        print(json.dumps({"case": name, "kernel": kernel, "us_per_launch": round(t * 1e6, 2),
-                          "algorithmic_bytes": int(nbytes), "achieved_gbs": round(gbs, 1),
-                          "frac_of_hbm": round(gbs / peak, 4), "launches": args.launches}), flush=True)
+        line = {"case": name, "kernel": kernel, "us_per_launch": round(t * 1e6, 2),
+                "algorithmic_bytes": int(nbytes), "achieved_gbs": round(gbs, 1)}
+        if name == "host_mapped":
+            pcie = pinned_copy_gbs(dev)
+            line.update({"pinned_copy_gbs": round(pcie, 1), "frac_of_pinned_copy": round(gbs / pcie, 4),
+                         "frac_of_pcie5_x16_nominal": round(gbs / PCIE5_X16_GBS, 4)})
+        else:
+            line["frac_of_hbm"] = round(gbs / peak, 4)
+        line["launches"] = args.launches
+        print(json.dumps(line), flush=True)
         del fn
         torch.cuda.empty_cache()
 
