@@ -431,10 +431,16 @@ def run_ours(args, ws, rank, device):
     # peer-memory kernel, whose step counter lives on the device), with its
     # own workspace so no later call can move it
     graph = None
+    # steps per graph: consecutive steps in one graph, so that each decode
+    # is a programmatic dependent of the previous step's last kernel (its
+    # combine or exchange, which write none of the decode's inputs) and its
+    # set-up overlaps that kernel, as consecutive layers' decodes do in a
+    # model; K must be a multiple
+    gsteps = next(c for c in (args.graph_steps, 4, 2, 1) if c >= 1 and args.steps % c == 0)
     if not args.no_graph:
         ws_g = torch.empty(max(256, a.workspace_bytes), dtype=torch.uint8, device=device)
         a_g = gpu_ops.decode_args(res.q, dec_tiers, dec_split, res.block_table, res.lens, batch.scale, out, lse,
-                                  max_len=max_len, tiles_per_split=tps, workspace_buf=ws_g)
+                                  max_len=max_len, tiles_per_split=tps, workspace_buf=ws_g, pdl=not args.no_pdl)
 
         parts_g = (torch.empty((1 + len(cplan.chunks)) * (n * H * D + H * n), dtype=torch.float32, device=device)
                    if chunked else None)
@@ -457,7 +463,8 @@ def run_ours(args, ws, rank, device):
         torch.cuda.synchronize(device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            gstep()
+            for _ in range(gsteps):
+                gstep()
         for _ in range(args.warmup):
             graph.replay()
         torch.cuda.synchronize(device)
@@ -523,13 +530,13 @@ def run_ours(args, ws, rank, device):
         step_est = torch.tensor([elapsed_eager / args.steps], dtype=torch.float64, device=device)
         if dist:
             torch.distributed.all_reduce(step_est, op=torch.distributed.ReduceOp.MAX)
-        pre = max(1, int(0.3 / max(float(step_est), 1e-5)))
+        pre = max(1, int(0.3 / max(float(step_est) * gsteps, 1e-5)))
         for _ in range(pre):
             graph.replay()
         if dist:
             torch.distributed.barrier()  # NCCL barrier on the stream: after the pre-roll everywhere
         t_start.record()
-        for _ in range(args.steps):
+        for _ in range(args.steps // gsteps):
             graph.replay()
         t_end.record()
         torch.cuda.synchronize(device)
@@ -658,9 +665,12 @@ def run_ours(args, ws, rank, device):
                                              "per-segment weight positions)",
         "tiles_per_split": tps, "split_combine": has_combine, "kernel": kname,
         "host_read": (args.host_read if res.tiers[1] is not None else "none (all HBM)"),
-        "timing": ("value: one CUDA graph of the step (the decode launch" + (" + its combine" if has_combine else "")
-                   + (", exchange and merge" if gather is not None else "") + ") replayed K times after an "
-                   "untimed pre-roll; roofline: eager steps with CUDA events around the decode launch (eager step "
+        "timing": (f"value: one CUDA graph of {gsteps} consecutive steps (each: the decode launch"
+                   + (" + its combine" if has_combine else "")
+                   + (", exchange and merge" if gather is not None else "") + "; decodes launched as programmatic "
+                   "dependents of the kernel ahead" + (", off" if args.no_pdl else "") + f") replayed K/{gsteps} "
+                   "times after an untimed pre-roll; roofline: eager steps with CUDA events around the decode launch "
+                   "(eager step "
                    f"{elapsed_eager / args.steps * 1e3:.4f} ms)" if graph is not None
                    else "value and roofline: eager steps, CUDA events"),
     }
@@ -1078,6 +1088,10 @@ def main() -> int:
                     help="host tier: staged into HBM by the copy engine each step, staged in chunks on a side "
                          "stream with the decode of landed chunks overlapping the copies, or read in place over PCIe")
     ap.add_argument("--stage-chunks", type=int, default=8, help="--host-read chunked: chunks per step")
+    ap.add_argument("--graph-steps", type=int, default=8,
+                    help="consecutive steps captured in one CUDA graph (the largest of this, 4, 2, 1 dividing K)")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch the graph's decodes as ordinary launches, not programmatic dependents")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of a captured CUDA graph of the step")
     ap.add_argument("--ctx", type=int, default=131072,

@@ -149,7 +149,22 @@ typedef struct fd_decode_args {
    * address rows of their tensors: row indices are the caller's contract
    * and are not range-checked (block ids and lengths are). */
   const int32_t *bt_rows;
+
+  /* FD_DECODE_* bits (0: none) */
+  int32_t flags;
+  int32_t _pad1;
 } fd_decode_args;
+
+/* fd_decode_args.flags: launch the decode as a programmatic dependent of the
+ * kernel ahead of it on the stream (CUDA programmatic dependent launch), so
+ * that its set-up -- reading lens, the block table, bt_rows / q_rows /
+ * out_rows and q, and prefetching block ids -- overlaps that kernel's tail.
+ * K/V reads and every write of the decode wait until that kernel has
+ * completed.  The caller guarantees that the kernel directly ahead does not
+ * write lens, the block table, the row maps or q (e.g. it is the layer's KV
+ * write, or the previous decode's combine or exchange).  No effect on a
+ * stream whose previous operation is not a kernel. */
+#define FD_DECODE_PDL 1
 
 /* ---------------------------------------------------------------- decode */
 

@@ -49,8 +49,11 @@ class FdDecodeArgs(ctypes.Structure):
         ("lse", c_void_p), ("lse_stride_h", c_int64), ("lse_stride_n", c_int64),
         ("max_len", c_int32), ("tiles_per_split", c_int32),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("error", c_void_p),
-        ("bt_rows", c_void_p),
+        ("bt_rows", c_void_p), ("flags", c_int32), ("_pad1", c_int32),
     ]
+
+
+FD_DECODE_PDL = 1  # fd_decode_args.flags: programmatic dependent launch
 
 
 # fd_plan_header slots and fd_plan_flags bits

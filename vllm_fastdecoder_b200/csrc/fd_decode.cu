@@ -147,28 +147,14 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   }
   if (p.persistent) __syncthreads();
 
+  // Programmatic dependent launch (fd_decode_args.flags & FD_DECODE_PDL):
+  // everything up to here, and the producers' block-id and q prefetch below,
+  // only reads inputs the caller guarantees the kernel ahead on the stream
+  // does not write; every thread passes griddep_wait() before its first
+  // K/V read and its first global write (a no-op for an ordinary launch).
   int64_t g_cur = 0, g_end = 0;
   int row_cur = 0;
   if (p.persistent) {
-    if (blockIdx.x == 0 && p.ws_prefix != nullptr)
-      for (int i = threadIdx.x; i <= p.n; i += blockDim.x) p.ws_prefix[i] = prefix[i];
-    // rows without tiles: empty -> o = 0, lse = -inf (reference
-    // cpu_attn.cpp:324-331); overrun -> error word
-    for (int i = blockIdx.x; i < p.n; i += gridDim.x) {
-      if (prefix[i + 1] != prefix[i]) continue;
-      const int len = p.lens[i];
-      if (len > 0) {
-        if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
-        continue;
-      }
-      const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-      for (int o = threadIdx.x; orow >= 0 && o < p.H * D; o += blockDim.x) {
-        const int h = o / D, d = o - h * D;
-        store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
-      }
-      if (p.lse != nullptr)
-        for (int h = threadIdx.x; h < p.H; h += blockDim.x) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
-    }
     const int64_t total = (int64_t)prefix[p.n] * Y;
     g_cur = (int64_t)blockIdx.x * total / gridDim.x;
     g_end = (int64_t)(blockIdx.x + 1) * total / gridDim.x;
@@ -185,6 +171,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     const int i = blockIdx.z;
     const int len = p.lens[i];
     if (len <= 0) {
+      griddep_wait();
       if (blockIdx.x == 0) {
         const int kh = blockIdx.y / p.gcs, gc = blockIdx.y - kh * p.gcs;
         const int h0 = kh * p.G + gc * GQ;
@@ -252,6 +239,7 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
     ids.ring = id_ring + pw * (kIdRingBytes / 4);
     ids.issued = 0;
     for (int i = 0; i < kIdAhead; ++i) ids.push(p, lane, q_heads, C::kRB, slot0, C::kTilesPerProd);
+    griddep_wait();  // K/V below may be written by the kernel ahead (the KV write)
     int k = 0;
     Piece pc;
     while (next_piece(pc)) {
@@ -369,6 +357,29 @@ __global__ void __launch_bounds__(Cfg<T, D, GQ>::kThreads, 2)
   }
 
   // -------------------------------------------------------------- consumers
+  griddep_wait();  // outputs, partial slots and the prefix are written below
+  constexpr int kCT = C::kNW * 32;  // consumer threads
+  if (p.persistent) {
+    if (blockIdx.x == 0 && p.ws_prefix != nullptr)
+      for (int i = threadIdx.x; i <= p.n; i += kCT) p.ws_prefix[i] = prefix[i];
+    // rows without tiles: empty -> o = 0, lse = -inf (reference
+    // cpu_attn.cpp:324-331); overrun -> error word
+    for (int i = blockIdx.x; i < p.n; i += gridDim.x) {
+      if (prefix[i + 1] != prefix[i]) continue;
+      const int len = p.lens[i];
+      if (len > 0) {
+        if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
+        continue;
+      }
+      const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+      for (int o = threadIdx.x; orow >= 0 && o < p.H * D; o += kCT) {
+        const int h = o / D, d = o - h * D;
+        store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
+      }
+      if (p.lse != nullptr)
+        for (int h = threadIdx.x; h < p.H; h += kCT) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
+    }
+  }
   const int tp = lane / C::kTPT;
   const int sub = lane - tp * C::kTPT;
   const int rot = tp % C::kCPL;
@@ -721,19 +732,20 @@ struct Geometry {
   size_t off_lse, off_prefix;
 };
 
-// launch(p, grid, extra dynamic smem, stream) / resident CTAs per SM
-typedef int (*launch_fn)(const DecodeParams&, dim3, size_t, cudaStream_t);
+// launch(p, grid, extra dynamic smem, stream, programmatic dependent launch)
+// / resident CTAs per SM
+typedef int (*launch_fn)(const DecodeParams&, dim3, size_t, cudaStream_t, bool);
 typedef int (*occ_fn)(int*);
 
 template <typename T, int D, int GQ>
-int launch_impl(const DecodeParams& p, dim3 grid, size_t extra, cudaStream_t s) {
+int launch_impl(const DecodeParams& p, dim3 grid, size_t extra, cudaStream_t s, bool pdl) {
   using C = Cfg<T, D, GQ>;
   static unsigned long long done = 0;
   auto kern = fdk::fd_decode_kernel<T, D, GQ>;
   int st = fdh::ensure_smem(reinterpret_cast<const void*>(kern), C::kSmem + C::kPrefixMax, &done);
   if (st != FD_OK) return st;
-  kern<<<grid, C::kThreads, C::kSmem + extra, s>>>(p);
-  return fdh::cuda_status(cudaGetLastError(), "fd_decode_kernel launch");
+  return fdh::launch_maybe_pdl(reinterpret_cast<const void*>(kern), grid, dim3(C::kThreads), C::kSmem + extra, s,
+                               pdl, p, "fd_decode_kernel launch");
 }
 
 // resident CTAs per SM of this kernel (queried once per device)
@@ -1112,6 +1124,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
     return fdh::fail(FD_ERR_UNSUPPORTED, "too many heads for the grid");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const KernelFns fns = pick_kernel(a->dtype, D, g.GQ);
+  const bool pdl = (a->flags & FD_DECODE_PDL) != 0;
   if (g.persistent) {
     // as many CTAs as fit on the device at once (capped by the partial slots
     // and by the tile count, at least 16 tiles each)
@@ -1141,7 +1154,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
       DecodeParams pm = p;
       pm.ncta = n_mma;
       if (launch_main) {
-        st = fdk::launch_decode_mma(pm, a->dtype, D, extra, s, &n_mma, &launched);
+        st = fdk::launch_decode_mma(pm, a->dtype, D, extra, s, &n_mma, &launched, pdl);
         if (st != FD_OK) return st;
         if (!launched) return fdh::fail(FD_ERR_UNSUPPORTED, "tensor-core decode kernel declined the call");
       } else {
@@ -1150,7 +1163,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
       p.ncta = n_mma;
       ncta = n_mma;
     } else if (launch_main) {
-      st = fns.launch(p, dim3((unsigned)ncta), extra, s);
+      st = fns.launch(p, dim3((unsigned)ncta), extra, s, pdl);
       if (st != FD_OK) return st;
     }
     if (geom != nullptr) {
@@ -1188,7 +1201,7 @@ int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool la
   }
   if (launch_main) {
     dim3 grid(g.max_splits, a->num_kv_heads * g.gcs, a->n);
-    st = fns.launch(p, grid, 0, s);
+    st = fns.launch(p, grid, 0, s, pdl);
     if (st != FD_OK) return st;
   }
   if (launch_combine && g.max_splits > 1) {

@@ -265,7 +265,7 @@ struct IdPrefetch {
 // sets *launched when it handled the call, FD_OK with *launched = false when
 // the shape is not one it covers.
 int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem, cudaStream_t s, int* ncta,
-                      bool* launched);
+                      bool* launched, bool pdl);
 
 // Whether the tcgen05 kernel covers this shape (16-bit KV, head size 128,
 // query group 2, 4 or 8, block size a multiple of 16).

@@ -253,23 +253,12 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (blockIdx.x == 0 && p.ws_prefix != nullptr)
-    for (int i = threadIdx.x; i <= p.n; i += blockDim.x) p.ws_prefix[i] = prefix[i];
-  for (int i = blockIdx.x; i < p.n; i += gridDim.x) {
-    if (prefix[i + 1] != prefix[i]) continue;
-    const int len = lens_s[i];
-    if (len > 0) {
-      if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
-      continue;
-    }
-    const int64_t orow = p.out_rows ? p.out_rows[i] : i;
-    for (int o = threadIdx.x; orow >= 0 && o < p.H * kD; o += blockDim.x) {
-      const int h = o / kD, d = o - h * kD;
-      store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
-    }
-    if (p.lse != nullptr)
-      for (int h = threadIdx.x; h < p.H; h += blockDim.x) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
-  }
+  // Programmatic dependent launch (fd_decode_args.flags & FD_DECODE_PDL): the
+  // setup above and the producers' block-id and q prefetch below only read
+  // inputs the caller guarantees the kernel ahead on the stream does not
+  // write; the producers pass griddep_wait() before their first K/V read and
+  // the softmax warps before their first global write (a no-op for an
+  // ordinary launch; the MMA warp touches no global memory).
   const int64_t total = (int64_t)prefix[p.n] * Y;
   const int64_t g0 = (int64_t)blockIdx.x * total / gridDim.x;
   const int64_t g1 = (int64_t)(blockIdx.x + 1) * total / gridDim.x;
@@ -328,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     bool aborted = false;
     bool have = advance(cur);
     if (have) fetch(cur, q_c);
+    griddep_wait();  // K/V below may be written by the kernel ahead (the KV write)
     while (have) {
       const bool have_n = advance(nxt);
       if (have_n) fetch(nxt, q_n);
@@ -512,6 +502,26 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
     // so that round trip and the epilogue overlap the next piece's products.
     const int r = threadIdx.x;  // token row of S, dim of O (TMEM lane)
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    griddep_wait();  // outputs, partial slots and the prefix are written below
+    if (blockIdx.x == 0 && p.ws_prefix != nullptr)
+      for (int i = r; i <= p.n; i += 128) p.ws_prefix[i] = prefix[i];
+    // rows without tiles: empty -> o = 0, lse = -inf (reference
+    // cpu_attn.cpp:324-331); overrun -> error word
+    for (int i = blockIdx.x; i < p.n; i += gridDim.x) {
+      if (prefix[i + 1] != prefix[i]) continue;
+      const int len = lens_s[i];
+      if (len > 0) {
+        if (r == 0) set_error(p.err, FD_DEVERR_LEN);
+        continue;
+      }
+      const int64_t orow = p.out_rows ? p.out_rows[i] : i;
+      for (int o = r; orow >= 0 && o < p.H * kD; o += 128) {
+        const int h = o / kD, d = o - h * kD;
+        store_out(p.out, orow * p.out_sn + (int64_t)h * p.out_sh + d, p.out_dtype, 0.f);
+      }
+      if (p.lse != nullptr)
+        for (int h = r; h < p.H; h += 128) p.lse[(int64_t)h * p.lse_sh + (int64_t)i * p.lse_sn] = -INFINITY;
+    }
     StageIter it;
     it.init(g0, g1, row0, prefix, lens_s, p.n, Y, kTilesPerStage, p.vtiles);
     int k = 0;
@@ -732,20 +742,16 @@ __global__ void __launch_bounds__(kThreads, 1) fd_decode_mma_kernel(const __grid
 }  // namespace mma
 
 template <int GM>
-int launch_mma_g(const DecodeParams& q, int dtype, size_t smem, int n, cudaStream_t s) {
+int launch_mma_g(const DecodeParams& q, int dtype, size_t smem, int n, cudaStream_t s, bool pdl) {
   static unsigned long long done_h = 0, done_b = 0;
   const int budget = mma::kSmemFixed + 3 * mma::kRowsBytes;
-  int st;
-  if (dtype == FD_DTYPE_BF16) {
-    st = fdh::ensure_smem(reinterpret_cast<const void*>(mma::fd_decode_mma_kernel<__nv_bfloat16, GM>), budget, &done_b);
-    if (st != FD_OK) return st;
-    mma::fd_decode_mma_kernel<__nv_bfloat16, GM><<<n, mma::kThreads, smem, s>>>(q);
-  } else {
-    st = fdh::ensure_smem(reinterpret_cast<const void*>(mma::fd_decode_mma_kernel<__half, GM>), budget, &done_h);
-    if (st != FD_OK) return st;
-    mma::fd_decode_mma_kernel<__half, GM><<<n, mma::kThreads, smem, s>>>(q);
-  }
-  return fdh::cuda_status(cudaGetLastError(), "fd_decode_mma_kernel launch");
+  const void* kern = dtype == FD_DTYPE_BF16
+                         ? reinterpret_cast<const void*>(mma::fd_decode_mma_kernel<__nv_bfloat16, GM>)
+                         : reinterpret_cast<const void*>(mma::fd_decode_mma_kernel<__half, GM>);
+  const int st = fdh::ensure_smem(kern, budget, dtype == FD_DTYPE_BF16 ? &done_b : &done_h);
+  if (st != FD_OK) return st;
+  return fdh::launch_maybe_pdl(kern, dim3((unsigned)n), dim3(mma::kThreads), smem, s, pdl, q,
+                               "fd_decode_mma_kernel launch");
 }
 
 bool mma_eligible(int dtype, int D, int G, int BS) {
@@ -754,7 +760,7 @@ bool mma_eligible(int dtype, int D, int G, int BS) {
 }
 
 int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem, cudaStream_t s, int* ncta,
-                      bool* launched) {
+                      bool* launched, bool pdl) {
   *launched = false;
   if (!mma_eligible(dtype, D, p.G, p.BS) || p.gcs != 1 || p.TT != mma::kTT || !p.persistent) return FD_OK;
   for (int t = 0; t < 2; ++t)
@@ -768,9 +774,9 @@ int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem
   q.ncta = n;
   int st;
   switch (p.G) {
-    case 2: st = launch_mma_g<2>(q, dtype, smem, n, s); break;
-    case 4: st = launch_mma_g<4>(q, dtype, smem, n, s); break;
-    default: st = launch_mma_g<8>(q, dtype, smem, n, s); break;
+    case 2: st = launch_mma_g<2>(q, dtype, smem, n, s, pdl); break;
+    case 4: st = launch_mma_g<4>(q, dtype, smem, n, s, pdl); break;
+    default: st = launch_mma_g<8>(q, dtype, smem, n, s, pdl); break;
   }
   if (st == FD_OK) {
     *launched = true;

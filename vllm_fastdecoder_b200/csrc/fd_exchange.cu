@@ -189,6 +189,10 @@ __global__ void __launch_bounds__(kXThreads) fd_exchange_merge_kernel(const __gr
   const unsigned long long step = *reinterpret_cast<volatile const unsigned long long*>(p.steps + cta) + 1;
   const int par = (int)(step & 1ull);
   griddep_wait();  // the decode's output is complete (programmatic dependent launch)
+  // the next step's decode, when launched as a programmatic dependent of this
+  // kernel (FD_DECODE_PDL), may start its set-up now; it waits for this grid
+  // to complete before writing the partial this kernel pushes
+  griddep_launch_dependents();
 
   // 1. push this rank's share to every rank
   const int64_t dst_off = ((int64_t)par * p.world + p.rank) * p.slot;

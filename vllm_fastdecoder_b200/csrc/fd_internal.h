@@ -37,4 +37,25 @@ int ensure_smem(const void* kernel, int bytes, unsigned long long* done_mask);
 // The current device and its SM count (queried once per device).
 int device_sms(int* dev, int* sms);
 
+// Launch `kernel(param)` (a kernel taking one parameter struct by value),
+// as a programmatic dependent of the kernel ahead on the stream when `pdl`
+// (the kernel then must pass griddepcontrol.wait before touching what that
+// kernel writes), else as an ordinary launch.
+template <typename P>
+int launch_maybe_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, const P& param,
+                     const char* what) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* args[1] = {const_cast<P*>(&param)};
+  return cuda_status(cudaLaunchKernelExC(&cfg, kernel, args), what);
+}
+
 }  // namespace fdh

@@ -422,14 +422,18 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
                 out_rows: torch.Tensor | None = None, max_len: int = 0,
                 tiles_per_split: int = 0, n: int | None = None,
                 bt_rows: torch.Tensor | None = None,
-                workspace_buf: torch.Tensor | None = None) -> nat.FdDecodeArgs:
+                workspace_buf: torch.Tensor | None = None, pdl: bool = False) -> nat.FdDecodeArgs:
     """Validate and pack the arguments of fd_decode_attn (workspace included).
     The tensors must stay alive, unmoved, while the returned args are used.
     With bt_rows (int32 [n]) work row i reads table row bt_rows[i]; a
     negative out_rows[i] writes nothing for row i (a device-built decode
     list, plan.plan_on_device).  workspace_buf (uint8, on q's device) replaces
     the shared grow-only workspace, e.g. for launches captured in a CUDA graph,
-    whose pointers must stay valid for the graph's lifetime."""
+    whose pointers must stay valid for the graph's lifetime.  pdl=True
+    launches the decode as a programmatic dependent of the kernel ahead on
+    the stream (FD_DECODE_PDL): only when that kernel writes none of lens,
+    block_table, the row maps and q (e.g. it is the layer's KV write or the
+    previous decode's combine)."""
     lib = nat.load()
     dev = q.device
     _check(dev.type == "cuda", "q must be a CUDA tensor")
@@ -486,6 +490,7 @@ def decode_args(q: torch.Tensor, tiers: tuple[KVTier | None, KVTier | None], tie
         a.lse_stride_h = lse.stride(0)
         a.lse_stride_n = lse.stride(1)
     a.bt_rows = _ptr(bt_rows)
+    a.flags = nat.FD_DECODE_PDL if pdl else 0
     a.max_len = int(max_len)
     a.tiles_per_split = int(tiles_per_split)
     a.error = error_word(dev).data_ptr()
