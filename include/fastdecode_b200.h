@@ -368,11 +368,10 @@ FD_API size_t fd_plan_args_bytes(void);
 #define FD_MAX_PEERS 8
 #define FD_IPC_HANDLE_BYTES 64
 /* Layout of one rank's allocation (fd_peer_alloc): u64 step counters of its
- * exchange CTAs [64] at byte 0; u64 arrival flags [FD_MAX_PEERS][64] at
- * FD_PEER_FLAGS_OFFSET (flag (q, b) = the last step whose share CTA b of rank
- * q delivered here, written only by that CTA); the fp32 receive slots
- * [2 parities][world][slot] from FD_PEER_RECV_OFFSET. */
-#define FD_PEER_FLAGS_OFFSET 512
+ * exchange CTAs [64] at byte 0; the receive slots [2 parities][world][slot]
+ * from FD_PEER_RECV_OFFSET, float i of a slot stored as the 8-byte word
+ * {u32 value bits, u32 step} (the step travels with each value, so a reader
+ * needs no fence and no separate arrival flag). */
 #define FD_PEER_RECV_OFFSET 8192
 
 typedef struct fd_peer_exchange {
@@ -384,7 +383,7 @@ typedef struct fd_peer_exchange {
   int64_t slot_floats;      /* floats per rank slot: >= n*H*D + H*n, multiple of 4 */
 } fd_peer_exchange;
 
-/* Bytes of one rank's allocation (counters + 2 x world slots). */
+/* Bytes of one rank's allocation (counters + 2 x world slots of 8-byte words). */
 FD_API size_t fd_peer_buffer_bytes(int32_t world, int64_t slot_floats);
 /* cudaMalloc + zero + IPC handle (FD_IPC_HANDLE_BYTES written to ipc_handle). */
 FD_API int fd_peer_alloc(size_t bytes, void **ptr, void *ipc_handle);
@@ -395,9 +394,10 @@ FD_API int fd_peer_free(void *ptr);
 /* One step: every rank calls it once per step, in the same order, with the
  * same n / heads / head size / num_ctas (0: 32, at most 64).  send: this rank's packed
  * partial (16-byte aligned); out [n, H, D] in out_dtype; out_lse [H, n] or
- * NULL.  The step waits until every CTA of every rank has raised its own
- * arrival flag to the step (flags, not a count of arrivals, so a rank that
- * is a step ahead cannot complete another rank's step).  Launched as a
+ * NULL.  Each value a rank pushes carries the step number in the same
+ * 8-byte word; the merge waits until every word it reads carries this step
+ * exactly (so neither an old value nor a rank that is a step ahead can
+ * complete another rank's step).  Launched as a
  * programmatic dependent of the kernel ahead of it on the stream (it waits
  * for that kernel before reading send).  A wait longer than timeout_ns (0:
  * 2 s) records FD_DEVERR_TIMEOUT in *error and returns with the outputs

@@ -113,10 +113,11 @@ def test_silent_peer_times_out_without_fault():
 
 def test_peer_a_step_ahead_does_not_complete_a_missing_rank():
     """World 3 on one GPU with two stand-in peer buffers: "rank 1" has already
-    delivered the next step (its arrival flag is one step ahead) and "rank 2"
-    never signals.  A count of arrivals would reach step x world and merge
-    rank 2's stale slot; the per-source flags must make the wait run out
-    (FD_DEVERR_TIMEOUT) and leave the outputs unwritten."""
+    delivered the next step (every word of its slot carries step 2 where
+    step 1 is due) and "rank 2" never delivers.  Neither may complete step 1:
+    the merge waits for words carrying exactly this step, so the wait runs
+    out (FD_DEVERR_TIMEOUT) and the outputs stay unwritten.  This rank's own
+    words of step 1 reach every rank's buffer."""
     from vllm_fastdecoder_b200 import _native as nat
     from vllm_fastdecoder_b200 import gpu_ops
 
@@ -125,12 +126,16 @@ def test_peer_a_step_ahead_does_not_complete_a_missing_rank():
     n, H, D, world = 2, 4, 64, 3
     slot = (n * H * D + H * n + 3) // 4 * 4
     nbytes = lib.fd_peer_buffer_bytes(world, slot)
+    assert nbytes == nat.PEER_RECV_OFFSET + 2 * world * slot * 8
     # plain device buffers stand in for the three ranks' allocations (zeroed:
-    # counters, flags and slots start at 0, as fd_peer_alloc leaves them)
+    # counters and slots start at 0, as fd_peer_alloc leaves them); word i of
+    # slot (parity, q) is the int64 at PEER_RECV_OFFSET / 8 + (parity * world + q) * slot + i,
+    # its high 32 bits the step
     bufs = [torch.zeros(nbytes // 8 + 1, dtype=torch.int64, device=dev) for _ in range(world)]
-    ctas = 4
-    flags0 = bufs[0][nat.PEER_FLAGS_OFFSET // 8: nat.PEER_FLAGS_OFFSET // 8 + nat.MAX_PEERS * nat.PEER_MAX_CTAS]
-    flags0[nat.PEER_MAX_CTAS: nat.PEER_MAX_CTAS + ctas] = 2  # every CTA of rank 1 is a step ahead
+    r0 = nat.PEER_RECV_OFFSET // 8
+    par = 1  # step 1
+    ahead = bufs[0][r0 + (par * world + 1) * slot: r0 + (par * world + 2) * slot]
+    ahead.fill_((2 << 32) | 0x3F800000)  # rank 1's words: value 1.0, step 2
     x = nat.FdPeerExchange()
     x.rank, x.world, x.slot_floats = 0, world, slot
     for q in range(world):
@@ -139,16 +144,19 @@ def test_peer_a_step_ahead_does_not_complete_a_missing_rank():
     out = torch.full((n, H, D), 7.0, dtype=torch.float16, device=dev)
     lse = torch.full((H, n), 7.0, dtype=torch.float32, device=dev)
     err = gpu_ops.error_word(dev)
+    ctas = 4
     nat.check(lib.fd_exchange_merge(ctypes.byref(x), send.data_ptr(), n, H, D, out.data_ptr(),
                                     gpu_ops.dtype_code(out.dtype), lse.data_ptr(), ctas, 50_000_000,
                                     err.data_ptr(), gpu_ops._stream(dev)), "fd_exchange_merge")
     with pytest.raises(RuntimeError, match="device error 3"):
         gpu_ops.check_device_errors(dev)
     assert bool((out == 7.0).all()) and bool((lse == 7.0).all())
-    # this rank did deliver: each of its CTAs raised its flag of step 1 in every rank's buffer
+    # this rank did deliver: its slot of step 1 in every rank's buffer holds
+    # send (1.0) tagged with step 1
     for q in range(world):
-        row0 = bufs[q][nat.PEER_FLAGS_OFFSET // 8: nat.PEER_FLAGS_OFFSET // 8 + ctas]
-        assert row0.tolist() == [1] * ctas
+        own = bufs[q][r0 + (par * world + 0) * slot: r0 + (par * world + 1) * slot].cpu()
+        assert bool(((own >> 32) == 1).all())
+        assert bool(((own & 0xFFFFFFFF) == 0x3F800000).all())
     torch.cuda.synchronize()
 
 

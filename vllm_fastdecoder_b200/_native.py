@@ -89,9 +89,8 @@ class FdPlanArgs(ctypes.Structure):
 
 MAX_PEERS = 8  # FD_MAX_PEERS
 IPC_HANDLE_BYTES = 64  # FD_IPC_HANDLE_BYTES
-PEER_FLAGS_OFFSET = 512  # FD_PEER_FLAGS_OFFSET
 PEER_RECV_OFFSET = 8192  # FD_PEER_RECV_OFFSET
-PEER_MAX_CTAS = 64  # flags per rank in a peer buffer
+PEER_MAX_CTAS = 64  # exchange CTAs per launch, at most
 
 
 class FdPeerExchange(ctypes.Structure):

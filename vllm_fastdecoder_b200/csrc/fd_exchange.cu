@@ -6,36 +6,35 @@
 // Each rank owns one device allocation, mapped into every other rank's
 // process with CUDA IPC (plain device memory: no multicast object, no NVLS):
 //   [0]    step counters    u64 [kMaxCtas]: CTA b's completed steps (its own)
-//   [512]  arrival flags    u64 [FD_MAX_PEERS][kMaxCtas]: flag (q, b) holds the
-//                            last step CTA b of rank q has delivered its share
-//                            into this buffer (written only by that CTA: a
-//                            system-scope fence, then relaxed stores)
-//   [8192] receive buffer   fp32 [2 parities][world][slot], slot = the packed
-//                            partial [o (n*H*D) | lse (H*n)] rounded to 4
+//   [8192] receive slots    [2 parities][world][slot] tagged words: float i of
+//                            a slot is the 8-byte word {value bits, step}
 // One launch per step of at most 64 CTAs of 256 threads, which the SMs hold
 // at once (every wait is bounded in any case):
 //   1. every CTA stores its share of the rank's packed partial into slot
-//      [parity][rank] of every rank's receive buffer (16-byte stores over
-//      NVLink; the own copy is local).  Given the decode launch's geometry
-//      (fd_decode_exchange_merge) the share is a set of (row, kv-head chunk)
-//      segments: a segment one decode CTA finished is copied from the
-//      decode's output, a segment that decode CTA ranges cut is merged from
-//      the decode's partial slots on the way (the rule and order of the
-//      decode's own combine), so no combine launch runs before the exchange;
-//   2. the CTA fences at system scope and writes the step into its flag
-//      (rank, b) of every rank's buffer;
-//   3. its threads wait (bounded, %globaltimer) until every flag of its own
-//      buffer (every CTA of every rank) holds at least the step (relaxed
-//      polls, then one acquire fence): every share of this step has landed;
-//   4. it merges its (row, head) pairs from the receive buffer with the
-//      log-sum-exp rule of fd_merge_partials, same operations in the same
-//      order (so the result equals the NCCL path bit for bit);
-//   5. it advances its own step counter (no atomics anywhere: every CTA
-//      keeps its own step, and all CTAs of a launch agree on it).
-// Double buffering by parity keeps a rank that is one step ahead from
-// overwriting a slot another rank is still merging; it cannot get two steps
-// ahead, because finishing a step needs every CTA's flag of that step from
-// every rank, and a rank's launch of step s + 1 starts after its launch of
+//      [parity][rank] of every rank's buffer over NVLink, each float with the
+//      step number in the same 8-byte word (16-byte volatile stores of two
+//      tagged words; the own copy is local).  Given the decode launch's
+//      geometry (fd_decode_exchange_merge) the share is a set of (row,
+//      kv-head chunk) segments: a segment one decode CTA finished is copied
+//      from the decode's output, a segment that decode CTA ranges cut is
+//      merged from the decode's partial slots on the way (the rule and order
+//      of the decode's own combine), so no combine launch runs before the
+//      exchange;
+//   2. each warp merges (row, head) pairs: it reads every rank's words for
+//      its pair from its own buffer, re-reading each until it carries this
+//      step (bounded, %globaltimer), and applies the log-sum-exp rule of
+//      fd_merge_partials with the same operations in the same order (so the
+//      result equals the NCCL path bit for bit);
+//   3. the CTA advances its own step counter (every CTA keeps its own step,
+//      and all CTAs of a launch agree on it).
+// A value and its step land together (an aligned 8-byte word is written and
+// read as a whole), so no fence and no separate arrival flag is needed: a
+// reader that sees the step sees the value.  A word of another step (an
+// older one in the slot, or a rank that is ahead) never matches, since a
+// reader waits for equality.  Double buffering by parity keeps a rank that
+// is one step ahead from overwriting a slot another rank is still merging;
+// it cannot get two steps ahead, because finishing a step needs every rank's
+// words of that step, and a rank writes step s + 1 only after its launch of
 // step s has completed.
 //
 // The kernel is launched as a programmatic dependent of the kernel before it
@@ -53,13 +52,11 @@
 namespace fdk {
 
 constexpr int kXThreads = 256;  // threads per exchange CTA
-constexpr int kXMaxCtas = 64;   // CTAs per launch, at most (per-CTA counters and flags)
+constexpr int kXMaxCtas = 64;   // CTAs per launch, at most (per-CTA step counters)
 
 struct ExchangeParams {
   const float* send;                      // [slot] this rank's packed partial [o | lse]
-  float* recv[FD_MAX_PEERS];              // rank q's receive buffer (mapped)
-  unsigned long long* flag_at[FD_MAX_PEERS];  // this rank's row of flags in rank q's buffer [kXMaxCtas]
-  const unsigned long long* flags;        // this rank's flags [world][kXMaxCtas]
+  uint32_t* recv[FD_MAX_PEERS];           // rank q's receive slots (mapped): word i = u32 [2 i, 2 i + 1]
   unsigned long long* steps;              // this rank's per-CTA step counters [kXMaxCtas]
   ShardGeom geom;                         // the decode launch's segments (prefix null: send is complete)
   int rank, world, n, H, D;
@@ -71,29 +68,48 @@ struct ExchangeParams {
   int32_t* err;
 };
 
-// Flags are written and polled with relaxed system-scope accesses; the
-// ordering comes from one fence on each side (a release or acquire access per
-// flag would fence once per flag: `world` system-scope fences per step).
-__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+__device__ __forceinline__ float lse_or_empty(float x) { return x == INFINITY ? -INFINITY : x; }
+
+// Tagged words: float i of a slot is the 8-byte word {value, step} at u32
+// index 2 i.  Volatile accesses (not cached in L1, not merged or split by
+// the compiler); an aligned 8-byte word is written and read whole.
+__device__ __forceinline__ void st_tagged2(uint32_t* w, float a, float b, uint32_t tag) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(w), "r"(__float_as_uint(a)), "r"(tag),
+               "r"(__float_as_uint(b)), "r"(tag)
+               : "memory");
+}
+__device__ __forceinline__ void st_tagged1(uint32_t* w, float a, uint32_t tag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(w), "r"(__float_as_uint(a)), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint2 ld_tagged1(const uint32_t* w) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(w) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Read tagged word w until it carries `tag`; false once the wait, measured
+// from t0, exceeds timeout_ns.
+__device__ __forceinline__ bool get_tagged(const uint32_t* w, uint32_t tag, uint64_t t0, int64_t timeout_ns, float& v) {
+  uint2 x = ld_tagged1(w);
+  for (uint32_t it = 1; x.y != tag; ++it) {
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)timeout_ns) return false;
+    x = ld_tagged1(w);
+  }
+  v = __uint_as_float(x.x);
+  return true;
 }
 
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-__device__ __forceinline__ float lse_or_empty(float x) { return x == INFINITY ? -INFINITY : x; }
-
-// Store at float offset `off` of this rank's slot in every rank's buffer.
-__device__ __forceinline__ void put4(const ExchangeParams& p, int64_t off, const float4& v) {
-  for (int q = 0; q < p.world; ++q) *reinterpret_cast<float4*>(p.recv[q] + off) = v;
+// Store at float offset `off` (a multiple of 4 for put4) of this rank's slot
+// in every rank's buffer, tagged with the step.
+__device__ __forceinline__ void put4(const ExchangeParams& p, int64_t off, const float4& v, uint32_t tag) {
+  for (int q = 0; q < p.world; ++q) {
+    uint32_t* w = p.recv[q] + 2 * off;
+    st_tagged2(w, v.x, v.y, tag);
+    st_tagged2(w + 4, v.z, v.w, tag);
+  }
 }
-__device__ __forceinline__ void put1(const ExchangeParams& p, int64_t off, float v) {
-  for (int q = 0; q < p.world; ++q) p.recv[q][off] = v;
+__device__ __forceinline__ void put1(const ExchangeParams& p, int64_t off, float v, uint32_t tag) {
+  for (int q = 0; q < p.world; ++q) st_tagged1(p.recv[q] + 2 * off, v, tag);
 }
 
 // Up to this many CTAs share a cut segment on the fast path (their partials
@@ -106,7 +122,7 @@ constexpr int kSpanFast = 4;
 // wrote it (empty rows included); a cut segment is merged from the decode's
 // fp32 partial slots with the decode combine's rule and order: M = max lse,
 // w = 2^((lse - M) log2 e), o = sum(w o) / sum(w), lse = M + ln sum(w).
-__device__ void push_segments(const ExchangeParams& p, int64_t dst_off) {
+__device__ void push_segments(const ExchangeParams& p, int64_t dst_off, uint32_t tag) {
   const ShardGeom& g = p.geom;
   const int Y = g.KVH * g.gcs;
   const int* P = g.prefix;
@@ -129,8 +145,8 @@ __device__ void push_segments(const ExchangeParams& p, int64_t dst_off) {
     SegSpan sp{0, 0, 0};
     if (P[i + 1] > P[i]) sp = seg_span(P, Y, g.vtiles, N, T, i, y);  // else an empty row, written to send
     if (sp.c0 == sp.c1) {
-      put4(p, dst_off + oi, __ldcg(reinterpret_cast<const float4*>(p.send + oi)));
-      if (d == 0) put1(p, dst_off + li, __ldcg(p.send + li));
+      put4(p, dst_off + oi, __ldcg(reinterpret_cast<const float4*>(p.send + oi)), tag);
+      if (d == 0) put1(p, dst_off + li, __ldcg(p.send + li), tag);
       continue;
     }
     float M = -INFINITY, L = 0.f;
@@ -177,8 +193,8 @@ __device__ void push_segments(const ExchangeParams& p, int64_t dst_off) {
         O[3] = fmaf(w, ov.w, O[3]);
       }
     }
-    put4(p, dst_off + oi, make_float4(O[0] / L, O[1] / L, O[2] / L, O[3] / L));
-    if (d == 0) put1(p, dst_off + li, M + logf(L));
+    put4(p, dst_off + oi, make_float4(O[0] / L, O[1] / L, O[2] / L, O[3] / L), tag);
+    if (d == 0) put1(p, dst_off + li, M + logf(L), tag);
   }
 }
 
@@ -187,6 +203,7 @@ __global__ void __launch_bounds__(kXThreads) fd_exchange_merge_kernel(const __gr
   // this CTA's own step counter (written only by this CTA of the previous
   // launch, which has completed): read before waiting for the decode
   const unsigned long long step = *reinterpret_cast<volatile const unsigned long long*>(p.steps + cta) + 1;
+  const uint32_t tag = (uint32_t)step;
   const int par = (int)(step & 1ull);
   griddep_wait();  // the decode's output is complete (programmatic dependent launch)
   // the next step's decode, when launched as a programmatic dependent of this
@@ -194,89 +211,107 @@ __global__ void __launch_bounds__(kXThreads) fd_exchange_merge_kernel(const __gr
   // to complete before writing the partial this kernel pushes
   griddep_launch_dependents();
 
-  // 1. push this rank's share to every rank
+  // 1. push this rank's share to every rank, each value tagged with the step
   const int64_t dst_off = ((int64_t)par * p.world + p.rank) * p.slot;
   if (p.geom.prefix != nullptr) {
-    push_segments(p, dst_off);
+    push_segments(p, dst_off, tag);
   } else {
     const float4* src = reinterpret_cast<const float4*>(p.send);
     const int64_t nvec = p.slot / 4;
     for (int64_t c = (int64_t)cta * blockDim.x + threadIdx.x; c < nvec; c += (int64_t)gridDim.x * blockDim.x)
-      put4(p, dst_off + c * 4, __ldcg(src + c));
-  }
-  __syncthreads();  // the CTA's stores happen before thread 0's fence
-
-  // 2. this CTA's flag in every rank's buffer
-  if (threadIdx.x == 0) {
-    __threadfence_system();  // the CTA's share is visible system-wide before its flag
-    for (int q = 0; q < p.world; ++q) st_relaxed_sys(p.flag_at[q] + cta, step);
+      put4(p, dst_off + c * 4, __ldcg(src + c), tag);
   }
 
-  // 3. every CTA of every rank delivered (each thread watches a few flags)
+  // 2. merge (one warp per (row, head) pair): every word the pair needs is
+  // requested at once, then the ones not yet carrying this step re-read
+  // until they do (bounded)
+  const uint32_t* base = p.recv[p.rank] + 2 * (int64_t)par * p.world * p.slot;
+  const int64_t o_floats = (int64_t)p.n * p.H * p.D;
+  const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int64_t pairs = (int64_t)p.n * p.H;
+  const uint64_t t0 = globaltimer_ns();
+  constexpr int kJ = 4;  // dims per lane per pass: 128 dims a pass
   bool ok = true;
-  {
-    const uint64_t t0 = globaltimer_ns();
-    const int nf = p.world * gridDim.x;
-    for (int f = threadIdx.x; ok && f < nf; f += blockDim.x) {
-      const int q = f / gridDim.x, c = f - q * gridDim.x;
-      const unsigned long long* fl = p.flags + q * kXMaxCtas + c;
-      for (uint32_t it = 1; ld_relaxed_sys(fl) < step; ++it) {
-        if ((it & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
-          set_error(p.err, FD_DEVERR_TIMEOUT);
+  for (int64_t pr = (int64_t)cta * nw + (threadIdx.x >> 5); ok && pr < pairs; pr += (int64_t)gridDim.x * nw) {
+    const int i = (int)(pr / p.H), h = (int)(pr - (int64_t)i * p.H);
+    const int64_t lo = o_floats + (int64_t)h * p.n + i;
+    const int64_t ob = ((int64_t)i * p.H + h) * p.D;
+    // lane q < world: rank q's lse word
+    const uint32_t* lw = base + 2 * ((int64_t)(lane < p.world ? lane : 0) * p.slot + lo);
+    uint2 l = lane < p.world ? ld_tagged1(lw) : make_uint2(__float_as_uint(-INFINITY), tag);
+    float w[FD_MAX_PEERS];
+    float inv = 1.f, m = 0.f, tot = 1.f;
+    bool all_empty = true;
+    for (int d0 = 0; ok && d0 < p.D; d0 += 32 * kJ) {
+      uint2 v[FD_MAX_PEERS][kJ];
+#pragma unroll
+      for (int q = 0; q < FD_MAX_PEERS; ++q)
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+          const int d = d0 + lane + 32 * j;
+          v[q][j] = (q < p.world && d < p.D) ? ld_tagged1(base + 2 * ((int64_t)q * p.slot + ob + d)) : make_uint2(0u, tag);
+        }
+      for (uint32_t it = 1;; ++it) {
+        bool mine = l.y == tag;
+#pragma unroll
+        for (int q = 0; q < FD_MAX_PEERS; ++q)
+#pragma unroll
+          for (int j = 0; j < kJ; ++j) mine = mine && v[q][j].y == tag;
+        if (__all_sync(0xffffffffu, mine)) break;
+        // the lanes agree on giving up (a warp-wide vote), so the warp stays converged
+        if ((it & 15u) == 0 && __any_sync(0xffffffffu, globaltimer_ns() - t0 > (uint64_t)p.timeout_ns)) {
           ok = false;
           break;
         }
+        if (l.y != tag) l = ld_tagged1(lw);
+#pragma unroll
+        for (int q = 0; q < FD_MAX_PEERS; ++q)
+#pragma unroll
+          for (int j = 0; j < kJ; ++j)
+            if (v[q][j].y != tag) v[q][j] = ld_tagged1(base + 2 * ((int64_t)q * p.slot + ob + d0 + lane + 32 * j));
       }
-    }
-    fence_acq_rel_sys();  // acquire: the shares behind the flags seen above are read after this
-  }
-  ok = __syncthreads_and(ok ? 1 : 0) != 0;
-
-  // 4. merge (one warp per (row, head) pair)
-  if (ok) {
-    const float* base = p.recv[p.rank] + (int64_t)par * p.world * p.slot;
-    const int64_t o_floats = (int64_t)p.n * p.H * p.D;
-    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int64_t pairs = (int64_t)p.n * p.H;
-    for (int64_t pr = (int64_t)cta * nw + (threadIdx.x >> 5); pr < pairs; pr += (int64_t)gridDim.x * nw) {
-      const int i = (int)(pr / p.H), h = (int)(pr - (int64_t)i * p.H);
-      const int64_t lo = o_floats + (int64_t)h * p.n + i;
-      // lane q reads rank q's lse; every lane then holds all of them
-      const float mine = lane < p.world ? lse_or_empty(__ldcg(base + lane * p.slot + lo)) : -INFINITY;
-      float lse_q[FD_MAX_PEERS];
+      if (!ok) break;
+      if (d0 == 0) {
+        // every lane holds every rank's lse after the shuffles
+        const float mine = lse_or_empty(__uint_as_float(l.x));
+        float lse_q[FD_MAX_PEERS];
 #pragma unroll
-      for (int q = 0; q < FD_MAX_PEERS; ++q) lse_q[q] = __shfl_sync(0xffffffffu, mine, q);
-      float m = -INFINITY;
+        for (int q = 0; q < FD_MAX_PEERS; ++q) lse_q[q] = __shfl_sync(0xffffffffu, mine, q);
+        m = -INFINITY;
 #pragma unroll
-      for (int q = 0; q < FD_MAX_PEERS; ++q)
-        if (q < p.world) m = fmaxf(m, lse_q[q]);
-      const bool all_empty = (m == -INFINITY);
-      if (all_empty) m = 0.f;
-      float w[FD_MAX_PEERS];
-      float tot = 0.f;
+        for (int q = 0; q < FD_MAX_PEERS; ++q)
+          if (q < p.world) m = fmaxf(m, lse_q[q]);
+        all_empty = (m == -INFINITY);
+        if (all_empty) m = 0.f;
+        tot = 0.f;
 #pragma unroll
-      for (int q = 0; q < FD_MAX_PEERS; ++q) {
-        w[q] = q < p.world ? expf(lse_q[q] - m) : 0.f;
-        if (q < p.world) tot += w[q];
+        for (int q = 0; q < FD_MAX_PEERS; ++q) {
+          w[q] = q < p.world ? expf(lse_q[q] - m) : 0.f;
+          if (q < p.world) tot += w[q];
+        }
+        if (all_empty) tot = 1.f;
+        inv = 1.f / tot;
       }
-      if (all_empty) tot = 1.f;
-      const float inv = 1.f / tot;
-      const int64_t ob = ((int64_t)i * p.H + h) * p.D;
-      for (int d = lane; d < p.D; d += 32) {
-        float o_q[FD_MAX_PEERS];
 #pragma unroll
-        for (int q = 0; q < FD_MAX_PEERS; ++q) o_q[q] = q < p.world ? __ldcg(base + q * p.slot + ob + d) : 0.f;
+      for (int j = 0; j < kJ; ++j) {
+        const int d = d0 + lane + 32 * j;
+        if (d >= p.D) continue;
         float x = 0.f;
 #pragma unroll
         for (int q = 0; q < FD_MAX_PEERS; ++q)
-          if (q < p.world) x = fmaf(w[q] * inv, o_q[q], x);
+          if (q < p.world) x = fmaf(w[q] * inv, __uint_as_float(v[q][j].x), x);
         store_out(p.out, ob + d, p.out_dtype, x);
       }
-      if (lane == 0 && p.out_lse != nullptr) p.out_lse[(int64_t)h * p.n + i] = all_empty ? -INFINITY : m + logf(tot);
     }
+    if (!ok) {
+      if (lane == 0) set_error(p.err, FD_DEVERR_TIMEOUT);
+      break;
+    }
+    if (lane == 0 && p.out_lse != nullptr) p.out_lse[(int64_t)h * p.n + i] = all_empty ? -INFINITY : m + logf(tot);
   }
 
-  // 5. this CTA's step is done
+  // 3. this CTA's step is done
+  __syncthreads();
   if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(p.steps + cta) = step;
 }
 
@@ -284,17 +319,15 @@ __global__ void __launch_bounds__(kXThreads) fd_exchange_merge_kernel(const __gr
 
 namespace {
 constexpr size_t kStepsOffset = 0;
-constexpr size_t kFlagsOffset = FD_PEER_FLAGS_OFFSET;
+
 constexpr size_t kRecvOffset = FD_PEER_RECV_OFFSET;
-static_assert(kStepsOffset + 8 * fdk::kXMaxCtas <= kFlagsOffset, "step counters overlap the arrival flags");
-static_assert(kFlagsOffset + 8 * FD_MAX_PEERS * fdk::kXMaxCtas <= kRecvOffset,
-              "arrival flags overlap the receive buffer");
+static_assert(kStepsOffset + 8 * fdk::kXMaxCtas <= kRecvOffset, "step counters overlap the receive slots");
 }
 
 extern "C" size_t fd_peer_buffer_bytes(int32_t world, int64_t slot_floats) {
   if (world < 1 || world > FD_MAX_PEERS || slot_floats < 0) return 0;
   const int64_t slot = (slot_floats + 3) / 4 * 4;
-  return kRecvOffset + (size_t)2 * (size_t)world * (size_t)slot * sizeof(float);
+  return kRecvOffset + (size_t)2 * (size_t)world * (size_t)slot * 8;  // one 8-byte tagged word per float
 }
 
 extern "C" int fd_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
@@ -358,12 +391,8 @@ int exchange_params(const fd_peer_exchange* x, const float* send, int32_t n, int
   *p = fdk::ExchangeParams{};
   p->send = send;
   unsigned char* own = static_cast<unsigned char*>(x->base[x->rank]);
-  for (int q = 0; q < x->world; ++q) {
-    unsigned char* b = static_cast<unsigned char*>(x->base[q]);
-    p->recv[q] = reinterpret_cast<float*>(b + kRecvOffset);
-    p->flag_at[q] = reinterpret_cast<unsigned long long*>(b + kFlagsOffset) + (size_t)x->rank * fdk::kXMaxCtas;
-  }
-  p->flags = reinterpret_cast<const unsigned long long*>(own + kFlagsOffset);
+  for (int q = 0; q < x->world; ++q)
+    p->recv[q] = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(x->base[q]) + kRecvOffset);
   p->steps = reinterpret_cast<unsigned long long*>(own + kStepsOffset);
   p->geom.prefix = nullptr;
   p->rank = x->rank;
