@@ -454,6 +454,56 @@ FD_API int fd_merge_partials(const float *o_parts, const float *lse_parts, int64
                       int32_t num_parts, int32_t n, int32_t num_heads, int32_t head_size,
                       void *out, int32_t out_dtype, float *out_lse, void *stream);
 
+/* ---------------------------------------------------------------- prefill */
+
+/* Causal prefill attention for the P (prefill over cached context) and F
+ * (fresh prefill) request classes, which the reference runs through vLLM's
+ * FlashAttention (fastdecode/backend.py:317-340: flash_attn_varlen_func with
+ * causal=True, paged block_table for P, the batch's own k / v for F).
+ * Request r has q_len[r] queries at batch rows q_start[r] .. + q_len[r] - 1
+ * and k_len[r] >= q_len[r] keys; query i sees keys 0 .. k_len - q_len + i
+ * (FlashAttention's bottom-right causal alignment).  Keys and values come
+ * from the HBM tier of the paged cache (block_table != NULL: key j of request
+ * r lies in block block_table[bt_row[r] * bt_stride + j / block_size], row
+ * j % block_size of `kv`, block_size a multiple of 16) or, block_table ==
+ * NULL, from the batch's own new K/V rows: kv.k / kv.v are [rows, KVH, D]
+ * (kv.tok_stride, kv.head_stride; kv.num_blocks = rows) and key j of request
+ * r is row q_start[r] + j.  out [num_tokens, H, D] rows of the requests'
+ * queries are written in q's dtype; other rows are untouched.  fp16 / bf16,
+ * head size 128, any GQA group.  Replaces FlashAttention on the tcgen05
+ * tensor cores; no lse output. */
+typedef struct fd_prefill_args {
+  const void *q;            /* [num_tokens, H, D] */
+  int64_t q_stride_t;
+  int64_t q_stride_h;
+  void *out;                /* [num_tokens, H, D], q's dtype */
+  int64_t out_stride_t;
+  int64_t out_stride_h;
+  fd_kv_tier kv;            /* device memory only */
+  const int32_t *block_table;
+  int64_t bt_stride;
+  int32_t bt_width;
+  int32_t num_tokens;       /* rows of q and out */
+  const int32_t *q_start;   /* [n] device, int32 */
+  const int32_t *q_len;     /* [n] */
+  const int32_t *k_len;     /* [n] */
+  const int32_t *bt_row;    /* [n] or NULL (row r) */
+  int32_t n;                /* requests, at most 65535 */
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_size;
+  int32_t block_size;
+  float scale;
+  int32_t dtype;
+  int32_t total_q;          /* sum of q_len (an upper bound is fine): sizes the grid */
+  int32_t *error;           /* optional device error word */
+} fd_prefill_args;
+
+FD_API int fd_prefill_attn(const fd_prefill_args *a, void *stream);
+
+/* sizeof(fd_prefill_args) as compiled into the library (binding check). */
+FD_API size_t fd_prefill_args_bytes(void);
+
 /* ---------------------------------------------------------------- KV write */
 
 /* Tier-aware KV write: new K/V rows go straight to their slot in whichever

@@ -109,6 +109,24 @@ class OracleOps:
         return torch.cat(outs).to(q.dtype)
 
 
+    @staticmethod
+    def prefill(query, out, q_start, q_len, k_len, scale, kv=None, block_table=None, k=None, v=None, total_q=None):
+        """fd_prefill_attn's contract: request r's queries are rows q_start[r]
+        .. + q_len[r] - 1, its k_len[r] keys from the paged tier (kv views
+        [B, KVH, BS, D], table row r) or the batch rows q_start[r] + j."""
+        assert total_q is None or total_q >= int(q_len.sum())
+        for r in range(q_len.numel()):
+            qs, ql, kl = int(q_start[r]), int(q_len[r]), int(k_len[r])
+            if block_table is not None:
+                bs = kv[0].shape[2]
+                blks = block_table[r, : (kl + bs - 1) // bs].long()
+                kk = kv[0][blks].transpose(1, 2).reshape(-1, kv[0].shape[1], kv[0].shape[3])[:kl]
+                vv = kv[1][blks].transpose(1, 2).reshape(-1, kv[1].shape[1], kv[1].shape[3])[:kl]
+            else:
+                kk, vv = k[qs: qs + kl], v[qs: qs + kl]
+            out[qs: qs + ql] = attend(query[qs: qs + ql], kk, vv, scale, causal=True).to(out.dtype)
+
+
 @pytest.fixture(autouse=True)
 def _cpu_ops(monkeypatch):
     monkeypatch.setattr(backend, "OPS", OracleOps)
@@ -215,6 +233,30 @@ def test_forward_split_matches_reference(monkeypatch, two_pass, H, KVH, dname, s
     torch.testing.assert_close(torch.from_numpy(gold[key + "/ref_f64"]), sc.ref, atol=0, rtol=0)
     # both tiers hold exactly what the reference left in them
     assert [sha(sc.kv_cache), sha(sc.cpu_k), sha(sc.cpu_v)] == list(gold[key + "/sha_after"])
+
+
+@pytest.mark.parametrize("H,KVH", [(4, 4), (8, 2)])
+def test_forward_split_prefill_rows_on_the_b200_kernel(monkeypatch, H, KVH):
+    """The P and F prefill rows routed to fd_prefill_attn (here its CPU
+    stand-in) with the per-request query starts, query and key counts and
+    table rows the backend derives from the plan: the output equals the
+    reference's recorded forward (FlashAttention for those rows)."""
+    monkeypatch.setattr(backend.FastDecodeImpl, "_prefill_on_b200", lambda self, q: True)
+    gold = np.load(GOLD / "forward_split.npz")
+    dtype, G, C, D, seed = torch.float16, 10, 20, 64, 0
+    sc = scenario(REQS, G, C, H, KVH, D, dtype, seed)
+    key = f"H{H}_KVH{KVH}_float16_s{seed}"
+    output = run_forward(sc, G, C, H, KVH, D, dtype)
+    torch.testing.assert_close(output.double(), sc.ref, atol=3e-3, rtol=3e-3)
+    torch.testing.assert_close(output.double(), torch.from_numpy(gold[key + "/output"]).double(), atol=3e-3, rtol=3e-3)
+
+
+def test_prefill_eligibility():
+    impl = make_impl(8, 2, 128, 0.1)
+    assert impl._prefill_on_b200(torch.empty(1, 8, 128, dtype=torch.bfloat16))
+    assert not impl._prefill_on_b200(torch.empty(1, 8, 128, dtype=torch.float32))
+    impl.head_size = 64
+    assert not impl._prefill_on_b200(torch.empty(1, 8, 64, dtype=torch.float16))
 
 
 def test_forward_none_metadata_zero_fills():

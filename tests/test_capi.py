@@ -44,6 +44,7 @@ def test_struct_mirrors_match_the_library():
     assert a.value == ctypes.sizeof(nat.FdDecodeArgs)
     assert b.value == ctypes.sizeof(nat.FdKvTier)
     assert lib.fd_plan_args_bytes() == ctypes.sizeof(nat.FdPlanArgs)
+    assert lib.fd_prefill_args_bytes() == ctypes.sizeof(nat.FdPrefillArgs)
 
 
 def test_plan_step_host_checks_need_no_gpu():

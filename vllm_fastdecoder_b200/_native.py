@@ -93,6 +93,18 @@ PEER_RECV_OFFSET = 8192  # FD_PEER_RECV_OFFSET
 PEER_MAX_CTAS = 64  # exchange CTAs per launch, at most
 
 
+class FdPrefillArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_stride_t", c_int64), ("q_stride_h", c_int64),
+        ("out", c_void_p), ("out_stride_t", c_int64), ("out_stride_h", c_int64),
+        ("kv", FdKvTier), ("block_table", c_void_p), ("bt_stride", c_int64), ("bt_width", c_int32),
+        ("num_tokens", c_int32), ("q_start", c_void_p), ("q_len", c_void_p), ("k_len", c_void_p),
+        ("bt_row", c_void_p), ("n", c_int32), ("num_heads", c_int32), ("num_kv_heads", c_int32),
+        ("head_size", c_int32), ("block_size", c_int32), ("scale", c_float), ("dtype", c_int32),
+        ("total_q", c_int32), ("error", c_void_p),
+    ]
+
+
 class FdPeerExchange(ctypes.Structure):
     _fields_ = [("base", c_void_p * MAX_PEERS), ("rank", c_int32), ("world", c_int32), ("slot_floats", c_int64)]
 
@@ -139,6 +151,8 @@ SIGNATURES = {
     "fd_exchange_merge_decoded": (c_int32, [
         POINTER(FdDecodeArgs), POINTER(FdPeerExchange), c_void_p, c_int32, c_void_p, c_int32, c_int64, c_void_p]),
     "fd_plan_args_bytes": (c_size_t, []),
+    "fd_prefill_attn": (c_int32, [POINTER(FdPrefillArgs), c_void_p]),
+    "fd_prefill_args_bytes": (c_size_t, []),
     "fd_version": (c_int32, []),
     "fd_abi_sizes": (c_int32, [POINTER(c_size_t), POINTER(c_size_t)]),
 }

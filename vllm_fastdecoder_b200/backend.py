@@ -105,6 +105,13 @@ class _GpuOps:
         gpu_ops.merge_attn_states(out, o_a, lse_a, o_b, lse_b, out_rows=out_rows)
 
     @staticmethod
+    def prefill(query, out, q_start, q_len, k_len, scale, kv=None, block_table=None, k=None, v=None, total_q=None):
+        from vllm_fastdecoder_b200 import gpu_ops
+
+        gpu_ops.prefill_attn(query, out, q_start, q_len, k_len, scale, kv=kv, block_table=block_table, k=k, v=v,
+                             total_q=total_q)
+
+    @staticmethod
     def fa(**kw):
         return _fa.flash_attn_varlen_func(**kw)
 
@@ -347,7 +354,21 @@ class FastDecodeImpl(FlashAttentionImpl):
             OPS.decode(query, (hbm, None), G, dp.pd_bt, dp.pd_seq_lens, self.scale, output,
                        q_rows=dp.pd_tok, out_rows=dp.pd_tok, max_len=hp.pd_max_len)
 
-        # 4) prefills stay on FlashAttention
+        # 4) prefills: this engine's tcgen05 kernel, written straight into the
+        # requests' output rows (FASTDECODE_B200_PREFILL=0: FlashAttention,
+        # as in the reference)
+        if self._prefill_on_b200(query):
+            if hp.pp_req.numel():
+                cu = dp.pp_cu
+                OPS.prefill(query, output, dp.pp_tok.index_select(0, cu[:-1].long()).to(torch.int32),
+                            (cu[1:] - cu[:-1]).to(torch.int32), dp.pp_seqlens, self.scale, kv=hbm,
+                            block_table=dp.pp_bt, total_q=int(hp.pp_tok.numel()))
+            if hp.n_f_tok:
+                cu = dp.f_cu
+                q_len = (cu[1:] - cu[:-1]).to(torch.int32)
+                OPS.prefill(query, output, dp.f_tok.index_select(0, cu[:-1].long()).to(torch.int32), q_len, q_len,
+                            self.scale, k=key, v=value, total_q=int(hp.n_f_tok))
+            return output
         if hp.pp_req.numel():
             q_p = query.index_select(0, dp.pp_tok)
             o_p = OPS.fa(q=q_p, k=key_cache, v=value_cache, cu_seqlens_q=dp.pp_cu, max_seqlen_q=hp.pp_max_q,
@@ -364,6 +385,13 @@ class FastDecodeImpl(FlashAttentionImpl):
                          softcap=self.logits_soft_cap, fa_version=self.vllm_flash_attn_version)
             output.index_copy_(0, dp.f_tok, o_f)
         return output
+
+    def _prefill_on_b200(self, query) -> bool:
+        """Whether this layer's prefill rows run on fd_prefill_attn: enabled
+        (FASTDECODE_B200_PREFILL), fp16 / bf16, head size 128, no soft cap;
+        otherwise FlashAttention, as in the reference."""
+        return (config.b200_prefill() and query.dtype in (torch.float16, torch.bfloat16) and self.head_size == 128
+                and not self.logits_soft_cap)
 
     def _split_two_pass(self, query, tiers, G, dp: DevicePlan, output):
         """The reference's structure (backend.py:293-356): an HBM partial over

@@ -24,6 +24,9 @@ ENV_DEVICE_PLAN = "FASTDECODE_B200_DEVICE_PLAN"
 # host-planned steps copy their host-tier blocks to HBM with the copy engine
 # (when the range they span is dense) unless set to 0
 ENV_STAGE_HOST = "FASTDECODE_B200_STAGE_HOST"
+# prefill rows (P and F classes) on this engine's tcgen05 kernel instead of
+# vLLM's FlashAttention (the reference's choice)
+ENV_PREFILL = "FASTDECODE_B200_PREFILL"
 
 
 def enabled() -> bool:
@@ -44,6 +47,10 @@ def two_pass() -> bool:
 
 def stage_host() -> bool:
     return os.environ.get(ENV_STAGE_HOST, "1") not in ("", "0", "false", "False")
+
+
+def b200_prefill() -> bool:
+    return os.environ.get(ENV_PREFILL, "1") not in ("", "0", "false", "False")
 
 
 def device_plan() -> bool:

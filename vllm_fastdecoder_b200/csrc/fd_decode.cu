@@ -1009,6 +1009,19 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
   return true;
 }
 
+}  // namespace
+
+namespace fdk {
+// Cached 4-D tiled tensor map {D, heads, BS, blocks} with box {64 or D, 1,
+// box_tokens, 1} (the encoder the decode kernels use), for the prefill kernel.
+bool encode_kv_map(CUtensorMap* m, const void* base, int dtype, int D, int heads, int BS, int64_t nblk,
+                   int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int box_tokens, bool swizzle128) {
+  return encode_tier_map(m, base, dtype, D, heads, BS, nblk, head_sb, tok_sb, blk_sb, box_tokens, swizzle128);
+}
+}  // namespace fdk
+
+namespace {
+
 // Validate `a` and fill the kernel parameters; launch_main / launch_combine
 // select which of the two kernels run.
 int decode_impl(const fd_decode_args* a, void* stream, bool launch_main, bool launch_combine,

@@ -1,0 +1,539 @@
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05),
+// sm_100a: the P (prefill with cached context) and F (fresh prefill) request
+// classes of the split path, which the reference hands to FlashAttention
+// (fastdecode/backend.py:317-340, flash_attn_varlen_func with causal=True).
+//
+// A CTA computes 128 query rows of one request for one query head:
+//   S [128 q x 128 keys] = Q [128 x D] . K^T        (tcgen05, K-major A and B)
+//   O [128 q x D]       = P [128 x 128 keys] . V   (tcgen05, V as MN-major B)
+// over the key tiles the causal mask leaves (query i of a request with q_len
+// queries and k_len keys sees keys 0 .. k_len - q_len + i: the bottom-right
+// alignment of FlashAttention's causal mask).  Six warps:
+//   warps 4, 6  TMA producers: warp 4 loads Q once (box {64, 1, 128, 1})
+//            and the K tiles of 128 keys into a 2-slot ring, warp 6 the V
+//            tiles into their own 2-slot ring (a K slot is free once its
+//            q.K^T completed, a V slot once its P.V did), one 16-key box per
+//            lane and 64-dim half (128-byte swizzle, the layout the MMA
+//            reads); keys come from the paged HBM cache through the block
+//            table, or from the batch's own new K/V rows (fresh prefills)
+//   warp 5   MMA issuer (one thread): polls both products and issues q.K^T
+//            of a tile into one of two TMEM S buffers once its keys landed,
+//            P.V of a tile once its P (double-buffered in shared memory) and
+//            V are in place; tcgen05.commit to mbarriers
+//   warps 0-3  softmax: thread r owns query row r (TMEM lane r): loads its S
+//            row into registers, masks and scales it, writes P = 2^(s - m)
+//            as 16-bit values into the swizzled A operand of P.V; O
+//            accumulates in TMEM over the tiles, rescaled only when the
+//            row's maximum moves past its reference m by more than 2^8; at
+//            the end o = O / l.
+// Numerics: scores fp32 from the exact 16-bit q and K, P rounded to the
+// input type for P.V (as FlashAttention does), accumulation fp32.  Every
+// mbarrier wait is bounded (FD_DEVERR_TIMEOUT); TMEM is released on every
+// path.
+
+#include <math.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "fd_common.cuh"
+#include "fd_decode.cuh"
+#include "fd_internal.h"
+#include "fd_tcgen05.cuh"
+
+namespace fdk {
+namespace pf {
+
+constexpr int kD = 128;                 // head size
+constexpr int kM = 128;                 // query rows per CTA (MMA M)
+constexpr int kKT = 128;                // keys per tile (MMA N of S, K of P.V)
+constexpr int kSub = 16;                // keys per TMA box
+constexpr int kSubs = kKT / kSub;       // boxes per 64-dim half of a tile
+constexpr int kPanel = 128 * 128;       // 128 rows x 128 B (64 dims)
+constexpr int kTile = 2 * kPanel;       // K or V of one tile / Q / P (32 KB)
+constexpr int kThreads = 7 * 32;
+constexpr int kTmemCols = 512;          // S0 [0,128) S1 [128,256) O [256,384)
+
+// shared memory: Q | K ring [2] | V ring [2] | P [2] | barriers | TMEM slot | misc
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTile;
+constexpr int kOffV = kOffK + 2 * kTile;
+constexpr int kOffP = kOffV + 2 * kTile;
+constexpr int kOffBar = kOffP + 2 * kTile;
+constexpr int kNumBars = 1 + 4 * 2 + 2 * 2 + 2 * 2 + 1;  // q_full, k/v full/empty, s_full/empty, p_full/free, drain
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kOffMisc = (kOffTmem + 16 + 15) / 16 * 16;  // [0] abort, [1] request, [2] its first tile
+constexpr int kSmem = kOffMisc + 64 + 1024;               // + 1024 to align the base
+static_assert(kSmem <= 227 * 1024, "smem budget");
+
+struct PrefillParams {
+  CUtensorMap tmap_q;   // {D, H, T, 1}, box {64, 1, 128, 1}, swizzled
+  CUtensorMap tmap_k;   // paged: {D, KVH, BS, blocks}; contiguous: {D, KVH, T, 1}; box {64, 1, 16, 1}
+  CUtensorMap tmap_v;
+  void* out;
+  int64_t out_st, out_sh;  // elements
+  const int32_t* bt;       // null: keys are the batch's own rows (q_start + j)
+  int64_t bt_stride;
+  int bt_width;
+  int64_t nblk;            // blocks of the paged cache (range check)
+  const int32_t* q_start;
+  const int32_t* q_len;
+  const int32_t* k_len;
+  const int32_t* bt_row;
+  int n, H, G, BS;
+  float sl2;  // scale * log2(e)
+  int dtype;
+  int32_t* err;
+};
+
+// One producer warp's share of a key tile: lane l < 8 loads keys
+// [128 j + 16 l, +16) of K or V (both 64-dim halves) into `dst`, completion
+// as bytes on `bar` (lane 0 arms it with the bytes of the lanes that load).
+__device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUtensorMap* map, unsigned char* dst,
+                                             uint64_t* bar, int j, int klen, int qst, int trow, int kh, int lane,
+                                             uint64_t pol) {
+  const int t = j * kKT + lane * kSub;
+  bool valid = lane < kSubs && t < klen;
+  int blk = 0, r0 = 0;
+  if (valid) {
+    if (p.bt != nullptr) {
+      const int64_t id = p.bt[(int64_t)trow * p.bt_stride + t / p.BS];
+      r0 = t % p.BS;
+      if (id >= 0 && id < p.nblk) {
+        blk = (int)id;
+      } else {
+        set_error(p.err, FD_DEVERR_BLOCK_ID);
+        valid = false;
+      }
+    } else {
+      r0 = qst + t;
+    }
+  }
+  const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+  if (lane == 0) mbar_expect_tx(bar, (uint32_t)__popc(vmask) * 2u * (kSub * 128u));
+  __syncwarp();
+  if (valid) {
+    tma_load_4d(dst + lane * kSub * 128, map, 0, kh, r0, blk, bar, pol);
+    tma_load_4d(dst + kPanel + lane * kSub * 128, map, 64, kh, r0, blk, bar, pol);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_constant__ PrefillParams p) {
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdQK = instr_desc(kBF16, false, kM, kKT);
+  constexpr uint32_t kIdPV = instr_desc(kBF16, false, kM, kD, true);  // V: MN-major B (dims contiguous)
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((((raw + 1023u) & ~1023u)) - raw);
+  unsigned char* qs = smem + kOffQ;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars;           // producer lane 0 + the TMA bytes of Q
+  uint64_t* k_full = bars + 1;       // [2] K tile landed
+  uint64_t* k_empty = bars + 3;      // [2] MMA commit after q.K^T
+  uint64_t* v_full = bars + 5;       // [2] V tile landed
+  uint64_t* v_empty = bars + 7;      // [2] MMA commit after P.V
+  uint64_t* s_full = bars + 9;       // [2] MMA commit: S ready
+  uint64_t* s_empty = bars + 11;     // [2] 4 softmax warps read S
+  uint64_t* p_full = bars + 13;      // [2] 4 softmax warps wrote P
+  uint64_t* p_free = bars + 15;      // [2] MMA commit after P.V: P buffer free, O up to date
+  uint64_t* drain = bars + 17;       // MMA commit before TMEM release
+  static_assert(kNumBars == 18, "barrier count");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + kOffMisc);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int kh = h / p.G;
+  const int b = blockIdx.x;
+
+  // ---------------------------------------------------------------- setup
+  // this CTA's request: the one whose query tiles (ceil(q_len / 128) each,
+  // in request order) contain tile b; a running scan over the requests
+  if (warp == 0) {
+    int carry = 0, found = -1, first = 0;
+    for (int base = 0; base < p.n && found < 0; base += 32) {
+      const int i = base + lane;
+      const int ql = i < p.n ? p.q_len[i] : 0;
+      const int c = ql > 0 ? (ql + kM - 1) / kM : 0;
+      int v = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += u;
+      }
+      const int lo = carry + v - c;  // first tile of request i
+      const unsigned hit = __ballot_sync(0xffffffffu, i < p.n && c > 0 && lo <= b && b < lo + c);
+      if (hit != 0u) {
+        const int w = __ffs(hit) - 1;
+        found = base + w;
+        first = __shfl_sync(0xffffffffu, lo, w);
+      }
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) {
+      misc[1] = found;
+      misc[2] = first;
+    }
+  }
+  if (threadIdx.x == 32) {
+    misc[0] = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[s], 4);
+      mbar_init(&p_free[s], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int r = misc[1];
+  if (r < 0) return;  // spare CTA of the grid's upper bound (before any TMEM is held)
+  const int q0 = (b - misc[2]) * kM;
+  const int qlen = p.q_len[r];
+  const int klen = p.k_len[r];
+  const int qst = p.q_start[r];
+  const int trow = p.bt_row != nullptr ? p.bt_row[r] : r;
+  if (klen < qlen || (p.bt != nullptr && (klen + p.BS - 1) / p.BS > p.bt_width)) {
+    if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
+    return;
+  }
+  const int i_last = min(q0 + kM, qlen) - 1;         // last query of this tile
+  const int nkv = (klen - qlen + i_last) / kKT + 1;  // key tiles the causal mask leaves
+
+  // K and V rings start as zeros: boxes not loaded (keys past k_len) hold
+  // finite values, which P = 0 cancels
+  for (int o = threadIdx.x * 16; o < 4 * kTile; o += kThreads * 16)
+    sts128(smem + kOffK + o, make_uint4(0u, 0u, 0u, 0u));
+  fence_proxy_async_smem();
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4 || warp == 6) {
+    // ------------------------------------------------------------ producers
+    // warp 4: Q, then K tiles (a K slot is free once its q.K^T completed);
+    // warp 6: V tiles (a V slot is free once its P.V completed)
+    const bool is_k = warp == 4;
+    if (is_k && lane == 0) {
+      mbar_expect_tx(q_full, (uint32_t)kTile);
+      tma_load_4d(qs, &p.tmap_q, 0, h, qst + q0, 0, q_full, 0ull);
+      tma_load_4d(qs + kPanel, &p.tmap_q, 64, h, qst + q0, 0, q_full, 0ull);
+      mbar_arrive(q_full);
+    }
+    const uint64_t pol = l2_evict_first_policy();
+    uint64_t* fullb = is_k ? k_full : v_full;
+    uint64_t* emptyb = is_k ? k_empty : v_empty;
+    unsigned char* ring = smem + (is_k ? kOffK : kOffV);
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (j >= 2 && !mbar_wait(&emptyb[st], (uint32_t)((j >> 1) - 1) & 1u, p.err)) {
+        misc[0] = 1;
+        break;
+      }
+      if (misc[0]) break;
+      load_kv_tile(p, is_k ? &p.tmap_k : &p.tmap_v, ring + st * kTile, &fullb[st], j, klen, qst, trow, kh, lane,
+                   pol);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    // One thread polls both products and issues whichever is ready: q.K^T of
+    // tile kq once K landed and its S buffer is free (at most two ahead),
+    // P.V of tile kp once P and V are in shared memory.
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0u, p.err);
+      const uint32_t sq = smem_u32(qs);
+      int kq = 0, kp = 0;
+      uint32_t spins = 0;
+      uint64_t t_idle = 0;
+      while (ok && kp < nkv) {
+        bool prog = false;
+        if (kq < nkv && kq < kp + 2) {
+          const int sb = kq & 1;
+          if (mbar_test_wait(&k_full[sb], (uint32_t)(kq >> 1) & 1u) &&
+              (kq < 2 || mbar_test_wait(&s_empty[sb], (uint32_t)((kq >> 1) - 1) & 1u))) {
+            tc_fence_after();
+            const uint32_t sk = smem_u32(smem + kOffK + sb * kTile);
+#pragma unroll
+            for (int ks = 0; ks < kD / 16; ++ks) {
+              const uint32_t off = (ks >> 2) * kPanel + (ks & 3) * 32;
+              umma_f16(tmem + sb * kKT, sw128_desc(sq + off, 16, 1024), sw128_desc(sk + off, 16, 1024), kIdQK,
+                       ks > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[sb]);
+            umma_commit(&k_empty[sb]);
+            ++kq;
+            prog = true;
+          }
+        }
+        if (kp < kq) {
+          const int pb = kp & 1;
+          if (mbar_test_wait(&p_full[pb], (uint32_t)(kp >> 1) & 1u) &&
+              mbar_test_wait(&v_full[pb], (uint32_t)(kp >> 1) & 1u)) {
+            tc_fence_after();
+            const uint32_t sp = smem_u32(smem + kOffP + pb * kTile);
+            const uint32_t sv = smem_u32(smem + kOffV + pb * kTile);
+#pragma unroll
+            for (int ks = 0; ks < kKT / 16; ++ks) {
+              const uint32_t poff = (ks >> 2) * kPanel + (ks & 3) * 32;
+              umma_f16(tmem + 2 * kKT, sw128_desc(sp + poff, 16, 1024), sw128_desc(sv + ks * 2048, kPanel, 1024),
+                       kIdPV, (kp > 0 || ks > 0) ? 1u : 0u);  // O accumulates over the tiles
+            }
+            umma_commit(&p_free[pb]);
+            umma_commit(&v_empty[pb]);
+            ++kp;
+            prog = true;
+          }
+        }
+        if (prog) {
+          spins = 0;
+          t_idle = 0;
+        } else if ((++spins & 255u) == 0u) {
+          if (misc[0]) ok = false;
+          const uint64_t now = globaltimer_ns();
+          if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitLimitNs) {
+            set_error(p.err, FD_DEVERR_TIMEOUT);
+            ok = false;
+          }
+        }
+      }
+      if (!ok) misc[0] = 1;
+      // all MMAs issued by this thread complete before TMEM is released
+      umma_commit(drain);
+      mbar_wait(drain, 0u, p.err);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax warps 0-3
+    // O accumulates in TMEM across the tiles (P.V with accumulate); P of a
+    // tile is 2^(s - m) for the row's running reference m, which moves only
+    // when the tile's maximum exceeds it by more than 2^8 (then the row's O
+    // in TMEM and its sum l are rescaled once), so values of P stay <= 256.
+    const int qi = q0 + threadIdx.x;                   // query index within the request
+    const bool row_ok = qi < qlen;
+    const int lim = row_ok ? klen - qlen + qi : -1;    // last key this query sees
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t t_o = tmem + lane_base + 2 * kKT;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; ok && j < nkv; ++j) {
+      if (__any_sync(0xffffffffu, misc[0] != 0)) {  // decisions stay warp-uniform (TMEM access is warp-wide)
+        ok = false;
+        break;
+      }
+      const int sb = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, p.err))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // the S row in registers: four loads, one wait
+      uint32_t sr[kKT / 32][32];
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c) tmem_ld32_nowait(tmem + lane_base + sb * kKT + 32 * c, sr[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[sb]);  // S buffer free for the tile after next
+      const int kbase = j * kKT;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float x = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) * p.sl2 : -INFINITY;
+          sr[c][e] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      // P buffer sb is free once the P.V of tile j - 2 completed
+      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_free[sb], (uint32_t)((j >> 1) - 1) & 1u, p.err))) {
+        ok = false;
+        break;
+      }
+      const bool grow = m != -INFINITY && mx > m + 8.f;
+      if (__any_sync(0xffffffffu, grow)) {
+        // O must hold every tile up to j - 1: wait for the P.V of tile j - 1
+        // (P.V products complete in order); TMEM access is warp-wide
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_free[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float alpha = grow ? exp2f(m - mx) : 1.f;
+#pragma unroll
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32_nowait(t_o + 32 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(t_o + 32 * c, o);
+        }
+        tmem_wait_st();
+        l *= alpha;
+      }
+      if (grow || m == -INFINITY) m = mx;  // the first keys of the row set the reference
+      const float m_use = m == -INFINITY ? 0.f : m;
+      unsigned char* ps = smem + kOffP + sb * kTile;
+      float lsum = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < kKT / 8; ++ch) {  // keys 8 ch .. 8 ch + 7 = 16-byte chunk ch of this row
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const float p0 = exp2f(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e]) - m_use);  // masked: 2^-inf = 0
+          const float p1 = exp2f(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e + 1]) - m_use);
+          const T h0 = Dt<T>::narrow(p0), h1 = Dt<T>::narrow(p1);
+          lsum += Dt<T>::to_f32(h0) + Dt<T>::to_f32(h1);  // the rounded values P.V multiplies
+          pk[e >> 1] = bits16(h0) | (bits16(h1) << 16);
+        }
+        sts128(ps + (ch >> 3) * kPanel + swz(threadIdx.x, ch & 7), make_uint4(pk[0], pk[1], pk[2], pk[3]));
+      }
+      l += lsum;
+      tc_fence_before();
+      fence_proxy_async_smem();  // generic smem writes of P (and TMEM stores of O) before the MMA reads them
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+    }
+    if (ok && nkv > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_free[(nkv - 1) & 1], (uint32_t)((nkv - 1) >> 1) & 1u, p.err));  // the last P.V
+      tc_fence_after();
+    }
+    if (!ok) {
+      misc[0] = 1;
+    } else {
+      uint32_t o[kD / 32][32];
+#pragma unroll
+      for (int c = 0; c < kD / 32; ++c) tmem_ld32_nowait(t_o + 32 * c, o[c]);
+      tmem_wait_ld();
+      if (row_ok) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(qst + qi) * p.out_st + (int64_t)h * p.out_sh;
+#pragma unroll
+        for (int c = 0; c < kD / 8; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float a0 = __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * k]) * inv;
+            const float a1 = __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * k + 1]) * inv;
+            w[k] = bits16(Dt<T>::narrow(a0)) | (bits16(Dt<T>::narrow(a1)) << 16);
+          }
+          *reinterpret_cast<uint4*>(orow + 8 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+}  // namespace pf
+}  // namespace fdk
+
+extern "C" int fd_prefill_attn(const fd_prefill_args* a, void* stream) {
+  using fdk::pf::PrefillParams;
+  if (a == nullptr) return fdh::fail(FD_ERR_INVALID, "fd_prefill_attn: null args");
+  if (a->n < 0 || a->n > 65535)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: %d requests (at most 65535)", a->n);
+  if (a->n == 0 || a->total_q <= 0) return FD_OK;
+  if (a->dtype != FD_DTYPE_F16 && a->dtype != FD_DTYPE_BF16)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: q/K/V must be fp16 or bf16");
+  if (a->head_size != fdk::pf::kD) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: head_size must be 128");
+  if (a->num_kv_heads <= 0 || a->num_heads <= 0 || a->num_heads % a->num_kv_heads != 0)
+    return fdh::fail(FD_ERR_INVALID, "fd_prefill_attn: num_heads must be a multiple of num_kv_heads");
+  if (a->num_heads > 65535) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: too many heads");
+  if (a->q == nullptr || a->out == nullptr || a->kv.k == nullptr || a->kv.v == nullptr || a->q_start == nullptr ||
+      a->q_len == nullptr || a->k_len == nullptr)
+    return fdh::fail(FD_ERR_INVALID, "fd_prefill_attn: q, out, K/V and the per-request arrays are required");
+  if (a->kv.host_mapped) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: K/V must be device memory");
+  if (a->num_tokens <= 0) return fdh::fail(FD_ERR_INVALID, "fd_prefill_attn: num_tokens must be positive");
+  const int es = 2;
+  const int64_t D = a->head_size;
+  if (!fdh::aligned16(a->q) || !fdh::aligned16(a->out) || (a->q_stride_t * es) % 16 != 0 ||
+      (a->q_stride_h * es) % 16 != 0 || (a->out_stride_t * es) % 16 != 0 || (a->out_stride_h * es) % 16 != 0)
+    return fdh::fail(FD_ERR_ALIGN, "fd_prefill_attn: q / out pointers and strides must be 16-byte aligned");
+  const fd_kv_tier& kv = a->kv;
+  if (!fdh::aligned16(kv.k) || !fdh::aligned16(kv.v) || (kv.head_stride * es) % 16 != 0 ||
+      (kv.tok_stride * es) % 16 != 0 || (kv.blk_stride * es) % 16 != 0)
+    return fdh::fail(FD_ERR_ALIGN, "fd_prefill_attn: K/V pointers and strides must be 16-byte aligned");
+  const bool paged = a->block_table != nullptr;
+  if (paged && (a->block_size <= 0 || a->block_size % fdk::pf::kSub != 0 || a->bt_width <= 0 || kv.num_blocks <= 0))
+    return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: paged K/V needs a block size that is a multiple of 16");
+  if (!paged && kv.num_blocks <= 0)
+    return fdh::fail(FD_ERR_INVALID, "fd_prefill_attn: contiguous K/V needs num_blocks = rows of k / v");
+
+  PrefillParams p{};
+  const int H = a->num_heads, KVH = a->num_kv_heads;
+  // q as {D, H, tokens, 1} with a 128-query box
+  bool ok = fdk::encode_kv_map(&p.tmap_q, a->q, a->dtype, (int)D, H, a->num_tokens, 1, a->q_stride_h * es,
+                               a->q_stride_t * es, a->q_stride_t * es * a->num_tokens, fdk::pf::kM, true);
+  if (paged) {
+    ok = ok && fdk::encode_kv_map(&p.tmap_k, kv.k, a->dtype, (int)D, KVH, a->block_size, kv.num_blocks,
+                                  kv.head_stride * es, kv.tok_stride * es, kv.blk_stride * es, fdk::pf::kSub, true);
+    ok = ok && fdk::encode_kv_map(&p.tmap_v, kv.v, a->dtype, (int)D, KVH, a->block_size, kv.num_blocks,
+                                  kv.head_stride * es, kv.tok_stride * es, kv.blk_stride * es, fdk::pf::kSub, true);
+  } else {
+    // the batch's own K/V rows [tokens, KVH, D] as one block of num_blocks tokens
+    const int64_t T = kv.num_blocks;
+    ok = ok && fdk::encode_kv_map(&p.tmap_k, kv.k, a->dtype, (int)D, KVH, (int)T, 1, kv.head_stride * es,
+                                  kv.tok_stride * es, kv.tok_stride * es * T, fdk::pf::kSub, true);
+    ok = ok && fdk::encode_kv_map(&p.tmap_v, kv.v, a->dtype, (int)D, KVH, (int)T, 1, kv.head_stride * es,
+                                  kv.tok_stride * es, kv.tok_stride * es * T, fdk::pf::kSub, true);
+  }
+  if (!ok) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: tensor map encoding rejected the q / K / V views");
+  p.out = a->out;
+  p.out_st = a->out_stride_t;
+  p.out_sh = a->out_stride_h;
+  p.bt = a->block_table;
+  p.bt_stride = a->bt_stride;
+  p.bt_width = a->bt_width;
+  p.nblk = kv.num_blocks;
+  p.q_start = a->q_start;
+  p.q_len = a->q_len;
+  p.k_len = a->k_len;
+  p.bt_row = a->bt_row;
+  p.n = a->n;
+  p.H = H;
+  p.G = H / KVH;
+  p.BS = paged ? a->block_size : 1;
+  p.sl2 = a->scale * fdk::kLog2e;
+  p.dtype = a->dtype;
+  p.err = a->error;
+
+  // grid: an upper bound of the query tiles (sum of ceil(q_len / 128) <=
+  // ceil(total_q / 128) + n) by heads; spare CTAs return at once
+  const int64_t tiles = ((int64_t)a->total_q + fdk::pf::kM - 1) / fdk::pf::kM + a->n;
+  if (tiles > 0x7fffffff) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: too many query tiles");
+  const void* kern = a->dtype == FD_DTYPE_BF16 ? reinterpret_cast<const void*>(fdk::pf::fd_prefill_kernel<__nv_bfloat16>)
+                                               : reinterpret_cast<const void*>(fdk::pf::fd_prefill_kernel<__half>);
+  static unsigned long long done_h = 0, done_b = 0;
+  int st = fdh::ensure_smem(kern, fdk::pf::kSmem, a->dtype == FD_DTYPE_BF16 ? &done_b : &done_h);
+  if (st != FD_OK) return st;
+  return fdh::launch_maybe_pdl(kern, dim3((unsigned)tiles, (unsigned)H), dim3(fdk::pf::kThreads), fdk::pf::kSmem,
+                               static_cast<cudaStream_t>(stream), false, p, "fd_prefill_kernel launch");
+}
+
+extern "C" size_t fd_prefill_args_bytes(void) { return sizeof(fd_prefill_args); }

@@ -631,6 +631,69 @@ def store_kv(k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor, k_cache: tor
 # ------------------------------------------------------------- merge
 
 
+def prefill_attn(q: torch.Tensor, out: torch.Tensor, q_start: torch.Tensor, q_len: torch.Tensor,
+                 k_len: torch.Tensor, scale: float, *, kv: KVTier | None = None,
+                 block_table: torch.Tensor | None = None, bt_row: torch.Tensor | None = None,
+                 k: torch.Tensor | None = None, v: torch.Tensor | None = None,
+                 total_q: int | None = None) -> None:
+    """Causal prefill attention on the tensor cores (fd_prefill_attn), the
+    replacement of flash_attn_varlen_func(causal=True) for the P and F
+    classes (fastdecode/backend.py:317-340).
+
+    q, out [T, H, 128] fp16/bf16 (batch rows); per request r (int32 device
+    tensors [n]): q_start (first query row), q_len, k_len >= q_len; query i
+    sees keys 0 .. k_len - q_len + i.  Keys/values either from the paged
+    HBM tier (kv [B, KVH, BS, D] views, block_table [R, W] int32, optional
+    bt_row [n] int32 table row of each request) or from the batch's own new
+    rows (k, v [T, KVH, D]; key j of request r is row q_start[r] + j).
+    total_q bounds the grid (sum of q_len; computed with a host sync when
+    not given).  Only the requests' rows of out are written."""
+    lib = nat.load()
+    dev = q.device
+    _check(dev.type == "cuda", "q must be a CUDA tensor")
+    _check(q.dim() == 3 and out.shape == q.shape and out.dtype == q.dtype, "q and out must be [T, H, D] alike")
+    _check(q.stride(-1) == 1 and out.stride(-1) == 1, "q and out need a contiguous head dim")
+    for nm, t in (("q_start", q_start), ("q_len", q_len), ("k_len", k_len)) + ((("bt_row", bt_row),) if bt_row is not None else ()):
+        _check(t.dtype == torch.int32 and t.device == dev and t.is_contiguous(), f"{nm} must be contiguous int32 on q's device")
+    n = q_len.numel()
+    _check(q_start.numel() == n and k_len.numel() == n and (bt_row is None or bt_row.numel() == n),
+           "per-request arrays must have the same length")
+    T, H, D = q.shape
+    a = nat.FdPrefillArgs()
+    a.q, a.q_stride_t, a.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
+    a.out, a.out_stride_t, a.out_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+    t = nat.FdKvTier()
+    if block_table is not None:
+        _check(kv is not None and not kv.host, "paged prefill needs the device KV tier")
+        _check(block_table.dtype == torch.int32 and block_table.device == dev and block_table.stride(-1) == 1,
+               "block_table must be int32 on q's device with contiguous rows")
+        _check(kv.k.dtype == q.dtype and kv.k.shape[3] == D, "KV tier dtype / head size mismatch")
+        t = kv.to_c()
+        KVH, BS = kv.k.shape[1], kv.k.shape[2]
+        a.block_table, a.bt_stride, a.bt_width = block_table.data_ptr(), block_table.stride(0), block_table.shape[1]
+        a.block_size = BS
+    else:
+        _check(k is not None and v is not None, "give either kv + block_table or k and v")
+        _check(k.shape == v.shape and k.stride() == v.stride() and k.dim() == 3 and k.stride(-1) == 1,
+               "k and v must be [T, KVH, D] alike with a contiguous head dim")
+        _check(k.dtype == q.dtype and k.device == dev and k.shape[2] == D, "k / v dtype, device or head size mismatch")
+        KVH = k.shape[1]
+        t.k, t.v = k.data_ptr(), v.data_ptr()
+        t.blk_stride, t.head_stride, t.tok_stride = 0, k.stride(1), k.stride(0)
+        t.num_blocks = k.shape[0]
+        a.block_size = 0
+    a.kv = t
+    a.num_tokens = T
+    a.q_start, a.q_len, a.k_len = q_start.data_ptr(), q_len.data_ptr(), k_len.data_ptr()
+    a.bt_row = _ptr(bt_row)
+    a.n, a.num_heads, a.num_kv_heads, a.head_size = n, H, KVH, D
+    a.scale = float(scale)
+    a.dtype = dtype_code(q.dtype)
+    a.total_q = int(q_len.sum().item()) if total_q is None else int(total_q)
+    a.error = error_word(dev).data_ptr()
+    nat.check(lib.fd_prefill_attn(ctypes.byref(a), _stream(dev)), "fd_prefill_attn")
+
+
 def merge_attn_states(out: torch.Tensor, o_a: torch.Tensor, lse_a: torch.Tensor, o_b: torch.Tensor,
                       lse_b: torch.Tensor, out_lse: torch.Tensor | None = None,
                       out_rows: torch.Tensor | None = None) -> None:

@@ -21,6 +21,15 @@ serves (and larger than the 126 MB L2 where the kernel streams data):
   host_mapped       fd_decode_kernel reading only the host tier in place over
                     PCIe (pinned, device-mapped): 16 rows x 4096 tokens, 32/32
                     heads, D128, fp16 (1.07 GB in host memory)
+  prefill           fd_prefill_kernel: 8 requests of 1024 new queries over
+                    1024 cached + 1024 new keys (causal), 32/8 heads, D128,
+                    bf16, paged HBM tier (achieved TFLOP/s against the
+                    measured dense bf16 peak)
+  prefill_fa        the same prefill through FlashAttention, the library the
+                    reference calls for these rows: vLLM's
+                    flash_attn_varlen_func over the paged cache when its
+                    extension loads, else flash-attn 2.8 over the gathered
+                    K/V (a baseline timing, not this engine's path)
   plan              fd_plan_kernel: the device planner on a 128-request
                     decode step of the config-4 trace
   exchange1         fd_exchange_merge_kernel with one rank (push, flags, merge
@@ -52,6 +61,11 @@ PCIE5_X16_GBS = 63.0  # PCIe Gen5 x16, per direction, nominal (32 GT/s x 16 lane
 def _hbm_peak() -> float:
     p = ROOT / "MEASURED_PEAKS.json"
     return float(json.loads(p.read_text())["hbm_gbs"]) if p.exists() else 6650.0
+
+
+def _bf16_peak() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    return float(json.loads(p.read_text())["bf16_tflops"]) if p.exists() else 1590.0
 
 
 def _time(fn, launches: int, warmup: int = 3) -> float:
@@ -182,6 +196,56 @@ def pinned_copy_gbs(dev, nbytes: int = 1 << 30) -> float:
     return nbytes / t / 1e9
 
 
+def case_prefill(dev):
+    n, ql, kl, H, KVH, D, BS, dt = 8, 1024, 2048, 32, 8, 128, 16, torch.bfloat16
+    nb = kl // BS
+    g = torch.Generator().manual_seed(4)
+    phys = torch.empty(n * nb + 8, BS, KVH, 2 * D, dtype=dt, device=dev).normal_()
+    cache = phys.permute(0, 2, 1, 3)
+    kv = KVTier(cache[..., :D], cache[..., D:])
+    bt = torch.randperm(n * nb + 8, generator=g)[: n * nb].to(torch.int32).view(n, nb).to(dev)
+    q = torch.randn(n * ql, H, D, dtype=dt, device=dev)
+    out = torch.empty_like(q)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)  # noqa: E731
+    qs, qls, kls = i32([i * ql for i in range(n)]), i32([ql] * n), i32([kl] * n)
+    # causal: query i sees kl - ql + i + 1 keys; 4 flops per (query, key, dim, head)
+    keys_seen = sum(kl - ql + i + 1 for i in range(ql)) * n
+    flops = 4 * keys_seen * H * D
+    return (lambda: gpu_ops.prefill_attn(q, out, qs, qls, kls, 1.0 / math.sqrt(D), kv=kv, block_table=bt,
+                                         total_q=n * ql)), flops, "fd_prefill_kernel"
+
+
+def case_prefill_fa(dev):
+    n, ql, kl, H, KVH, D, BS, dt = 8, 1024, 2048, 32, 8, 128, 16, torch.bfloat16
+    nb = kl // BS
+    g = torch.Generator().manual_seed(4)
+    phys = torch.empty(n * nb + 8, BS, KVH, 2 * D, dtype=dt, device=dev).normal_()
+    bt = torch.randperm(n * nb + 8, generator=g)[: n * nb].to(torch.int32).view(n, nb).to(dev)
+    q = torch.randn(n * ql, H, D, dtype=dt, device=dev)
+    cu_q = torch.arange(0, (n + 1) * ql, ql, dtype=torch.int32, device=dev)
+    keys_seen = sum(kl - ql + i + 1 for i in range(ql)) * n
+    flops = 4 * keys_seen * H * D
+    scale = 1.0 / math.sqrt(D)
+    try:  # the reference's own call (fastdecode/backend.py:317-329)
+        from vllm.vllm_flash_attn import flash_attn_varlen_func as fa
+
+        k_cache, v_cache = phys[..., :D], phys[..., D:]  # [B, BS, KVH, D] views
+        seqused = torch.full((n,), kl, dtype=torch.int32, device=dev)
+        fn = lambda: fa(q=q, k=k_cache, v=v_cache, cu_seqlens_q=cu_q, max_seqlen_q=ql, seqused_k=seqused,  # noqa: E731
+                        max_seqlen_k=kl, softmax_scale=scale, causal=True, block_table=bt, fa_version=2)
+        fn()
+        return fn, flops, "vllm_flash_attn (fa2, paged)"
+    except Exception:
+        from flash_attn import flash_attn_varlen_func as fa
+
+        k = phys[bt.long().flatten()].reshape(n * kl, KVH, 2 * D)
+        kc, vc = k[..., :D].contiguous(), k[..., D:].contiguous()
+        cu_k = torch.arange(0, (n + 1) * kl, kl, dtype=torch.int32, device=dev)
+        fn = lambda: fa(q, kc, vc, cu_q, cu_k, ql, kl, softmax_scale=scale, causal=True)  # noqa: E731
+        fn()
+        return fn, flops, "flash_attn 2.8 (gathered K/V)"
+
+
 def case_plan(dev):
     from vllm_fastdecoder_b200 import plan
 
@@ -219,6 +283,8 @@ CASES = {
     "split_merge": case_split_merge,
     "combine": case_combine,
     "host_mapped": case_host_mapped,
+    "prefill": case_prefill,
+    "prefill_fa": case_prefill_fa,
     "plan": case_plan,
     "exchange1": case_exchange1,
 }
@@ -239,6 +305,16 @@ def main() -> None:
         gbs = nbytes / t / 1e9
         line = {"case": name, "kernel": kernel, "us_per_launch": round(t * 1e6, 2),
                 "algorithmic_bytes": int(nbytes), "achieved_gbs": round(gbs, 1)}
+        if name in ("prefill", "prefill_fa"):  # flops, not bytes
+            tf = nbytes / t / 1e12
+            peak_tf = _bf16_peak()
+            line = {"case": name, "kernel": kernel, "us_per_launch": round(t * 1e6, 2), "flops": int(nbytes),
+                    "achieved_tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / peak_tf, 4),
+                    "launches": args.launches}
+            print(json.dumps(line), flush=True)
+            del fn
+            torch.cuda.empty_cache()
+            continue
         if name == "host_mapped":
             pcie = pinned_copy_gbs(dev)
             line.update({"pinned_copy_gbs": round(pcie, 1), "frac_of_pinned_copy": round(gbs / pcie, 4),
