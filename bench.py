@@ -1080,7 +1080,7 @@ def main() -> int:
     ap.add_argument("--no-parity", action="store_true", help="c3: skip the in-run oracle check of the output")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split-grid", action="store_true", help="fixed split grid instead of the persistent schedule")
-    ap.add_argument("--exchange", choices=["peer", "peer-split", "nccl"], default="nccl",
+    ap.add_argument("--exchange", choices=["peer", "peer-split", "nccl"], default="peer",
                     help="c3 on N > 1 GPUs: partials exchanged over peer memory by the exchange kernel that also "
                          "does the decode's combine (peer), by the decode's combine and then the exchange kernel "
                          "(peer-split), or with an NCCL all-gather and a merge kernel (nccl)")

@@ -9,21 +9,25 @@
 // over the key tiles the causal mask leaves (query i of a request with q_len
 // queries and k_len keys sees keys 0 .. k_len - q_len + i: the bottom-right
 // alignment of FlashAttention's causal mask).  Six warps:
-//   warps 4, 6  TMA producers: warp 4 loads Q once (box {64, 1, 128, 1})
-//            and the K tiles of 128 keys into a 2-slot ring, warp 6 the V
+//   warps 8, 10  TMA producers: warp 8 loads Q once (box {64, 1, 128, 1})
+//            and the K tiles of 128 keys into a 2-slot ring, warp 10 the V
 //            tiles into their own 2-slot ring (a K slot is free once its
 //            q.K^T completed, a V slot once its P.V did), one 16-key box per
 //            lane and 64-dim half (128-byte swizzle, the layout the MMA
 //            reads); keys come from the paged HBM cache through the block
 //            table, or from the batch's own new K/V rows (fresh prefills)
-//   warp 5   MMA issuer (one thread): polls both products and issues q.K^T
+//   warp 9   MMA issuer (one thread): polls both products and issues q.K^T
 //            of a tile into one of two TMEM S buffers once its keys landed,
 //            P.V of a tile once its P (double-buffered in shared memory) and
 //            V are in place; tcgen05.commit to mbarriers
-//   warps 0-3  softmax: thread r owns query row r (TMEM lane r): loads its S
-//            row into registers, masks and scales it, writes P = 2^(s - m)
-//            as 16-bit values into the swizzled A operand of P.V; O
-//            accumulates in TMEM over the tiles, rescaled only when the
+//   warps 0-7  softmax, two warpgroups: warp w owns query rows 32 (w % 4) ..
+//            + 31 (TMEM lanes) and keys 64 (w / 4) .. + 63 of each tile; it
+//            loads its half of the S row into registers, masks it (tiles
+//            below the causal diagonal skip the mask), exchanges the half-
+//            row maximum with its partner warp through shared memory, and
+//            writes P = 2^(s - m) as 16-bit values into its panel of the
+//            swizzled A operand of P.V; O accumulates in TMEM over the
+//            tiles, rescaled (each warpgroup its 64 dims) only when the
 //            row's maximum moves past its reference m by more than 2^8; at
 //            the end o = O / l.
 // Numerics: scores fp32 from the exact 16-bit q and K, P rounded to the
@@ -51,7 +55,9 @@ constexpr int kSub = 16;                // keys per TMA box
 constexpr int kSubs = kKT / kSub;       // boxes per 64-dim half of a tile
 constexpr int kPanel = 128 * 128;       // 128 rows x 128 B (64 dims)
 constexpr int kTile = 2 * kPanel;       // K or V of one tile / Q / P (32 KB)
-constexpr int kThreads = 7 * 32;
+constexpr int kSoftWarps = 8;           // two warpgroups: keys 0-63 and 64-127 of each tile
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K producer, MMA issuer, V producer
+constexpr int kThreads = 11 * 32;
 constexpr int kTmemCols = 512;          // S0 [0,128) S1 [128,256) O [256,384)
 
 // shared memory: Q | K ring [2] | V ring [2] | P [2] | barriers | TMEM slot | misc
@@ -63,7 +69,8 @@ constexpr int kOffBar = kOffP + 2 * kTile;
 constexpr int kNumBars = 1 + 4 * 2 + 2 * 2 + 2 * 2 + 1;  // q_full, k/v full/empty, s_full/empty, p_full/free, drain
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kOffMisc = (kOffTmem + 16 + 15) / 16 * 16;  // [0] abort, [1] request, [2] its first tile
-constexpr int kSmem = kOffMisc + 64 + 1024;               // + 1024 to align the base
+constexpr int kOffRed = kOffMisc + 64;                     // [2 halves][128 rows] floats: row maxima, then sums
+constexpr int kSmem = kOffRed + 2 * 128 * 4 + 1024;        // + 1024 to align the base
 static_assert(kSmem <= 227 * 1024, "smem budget");
 
 struct PrefillParams {
@@ -188,8 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 4);  // one arrival per softmax warp
-      mbar_init(&p_full[s], 4);
+      mbar_init(&s_empty[s], kSoftWarps);  // one arrival per softmax warp
+      mbar_init(&p_full[s], kSoftWarps);
       mbar_init(&p_free[s], 1);
     }
     mbar_init(drain, 1);
@@ -215,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   for (int o = threadIdx.x * 16; o < 4 * kTile; o += kThreads * 16)
     sts128(smem + kOffK + o, make_uint4(0u, 0u, 0u, 0u));
   fence_proxy_async_smem();
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
@@ -226,11 +233,11 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4 || warp == 6) {
+  if (warp == kWarpK || warp == kWarpV) {
     // ------------------------------------------------------------ producers
-    // warp 4: Q, then K tiles (a K slot is free once its q.K^T completed);
-    // warp 6: V tiles (a V slot is free once its P.V completed)
-    const bool is_k = warp == 4;
+    // warp 8: Q, then K tiles (a K slot is free once its q.K^T completed);
+    // warp 10: V tiles (a V slot is free once its P.V completed)
+    const bool is_k = warp == kWarpK;
     if (is_k && lane == 0) {
       mbar_expect_tx(q_full, (uint32_t)kTile);
       tma_load_4d(qs, &p.tmap_q, 0, h, qst + q0, 0, q_full, 0ull);
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       load_kv_tile(p, is_k ? &p.tmap_k : &p.tmap_v, ring + st * kTile, &fullb[st], j, klen, qst, trow, kh, lane,
                    pol);
     }
-  } else if (warp == 5) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     // One thread polls both products and issues whichever is ready: q.K^T of
     // tile kq once K landed and its S buffer is free (at most two ahead),
@@ -322,64 +329,88 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ softmax warps 0-3
+    // ------------------------------------------------------------ softmax warps 0-7
+    // Warp w owns query rows 32 (w % 4) .. + 31 (TMEM lanes) and keys
+    // 64 (w / 4) .. + 63 of every tile (its half); the two warps of a row
+    // exchange their half-row maxima through shared memory once per tile.
     // O accumulates in TMEM across the tiles (P.V with accumulate); P of a
     // tile is 2^(s - m) for the row's running reference m, which moves only
     // when the tile's maximum exceeds it by more than 2^8 (then the row's O
-    // in TMEM and its sum l are rescaled once), so values of P stay <= 256.
-    const int qi = q0 + threadIdx.x;                   // query index within the request
+    // in TMEM, each half its 64 dims, and the sums l are rescaled once), so
+    // values of P stay <= 256.
+    const int half = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;                  // query row of the tile = TMEM lane
+    const int qi = q0 + row;                                  // query index within the request
     const bool row_ok = qi < qlen;
-    const int lim = row_ok ? klen - qlen + qi : -1;    // last key this query sees
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t t_o = tmem + lane_base + 2 * kKT;
-    float m = -INFINITY, l = 0.f;
+    const int lim = row_ok ? klen - qlen + qi : -1;          // last key this query sees
+    const int lim_all = klen - qlen + q0;                     // keys every query of the tile sees
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_o = tmem + lane_base + 2 * kKT + 64 * half;  // this half's 64 dims of O
+    float* red = reinterpret_cast<float*>(smem + kOffRed);   // [2 halves][128 rows]
+    float m = -INFINITY, l = 0.f;  // m: log2-domain reference of the row; l: this half's sum
+    // Every softmax warp runs all nkv iterations and passes both named
+    // barriers of each (a warp that failed a wait, or saw another role
+    // abort, only skips its work and its waits), so no barrier is ever left
+    // waiting for a warp that has gone.
     bool ok = true;
-    for (int j = 0; ok && j < nkv; ++j) {
-      if (__any_sync(0xffffffffu, misc[0] != 0)) {  // decisions stay warp-uniform (TMEM access is warp-wide)
-        ok = false;
-        break;
-      }
+    for (int j = 0; j < nkv; ++j) {
+      if (ok && __any_sync(0xffffffffu, misc[0] != 0)) ok = false;  // warp-uniform (TMEM access is warp-wide)
       const int sb = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, p.err))) {
-        ok = false;
-        break;
+      if (ok && !__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, p.err))) ok = false;
+      uint32_t sr[2][32];  // this half of the S row: two loads, one wait
+      float mx = -INFINITY;  // raw score maximum (scale > 0)
+      const int kbase = j * kKT + 64 * half;
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) tmem_ld32_nowait(tmem + lane_base + sb * kKT + 64 * half + 32 * c, sr[c]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[sb]);  // S buffer free for the tile after next
       }
-      tc_fence_after();
-      // the S row in registers: four loads, one wait
-      uint32_t sr[kKT / 32][32];
+      const bool full_tile = j * kKT + kKT - 1 <= lim_all;  // below the diagonal for every row: no mask
+      if (!ok) {
+      } else if (full_tile) {
 #pragma unroll
-      for (int c = 0; c < kKT / 32; ++c) tmem_ld32_nowait(tmem + lane_base + sb * kKT + 32 * c, sr[c]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);  // S buffer free for the tile after next
-      const int kbase = j * kKT;
-      float mx = -INFINITY;
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int c = 0; c < kKT / 32; ++c)
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+      } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float x = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) * p.sl2 : -INFINITY;
-          sr[c][e] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
+            sr[c][e] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+      }
+      // the row's maximum over both halves (two barriers: values written,
+      // then read, before the next tile overwrites them)
+      red[half * 128 + row] = mx;
+      named_barrier_sync(1, kSoftWarps * 32);
+      mx = fmaxf(mx, red[(1 - half) * 128 + row]);
+      named_barrier_sync(1, kSoftWarps * 32);
+      if (!ok) continue;
+      const float mxs = mx * p.sl2;  // log2 domain
       // P buffer sb is free once the P.V of tile j - 2 completed
       if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_free[sb], (uint32_t)((j >> 1) - 1) & 1u, p.err))) {
         ok = false;
-        break;
+        continue;
       }
-      const bool grow = m != -INFINITY && mx > m + 8.f;
+      const bool grow = m != -INFINITY && mxs > m + 8.f;
       if (__any_sync(0xffffffffu, grow)) {
         // O must hold every tile up to j - 1: wait for the P.V of tile j - 1
-        // (P.V products complete in order); TMEM access is warp-wide
+        // (P.V products complete in order)
         if (!__all_sync(0xffffffffu, mbar_wait(&p_free[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, p.err))) {
           ok = false;
-          break;
+          continue;
         }
         tc_fence_after();
-        const float alpha = grow ? exp2f(m - mx) : 1.f;
+        const float alpha = grow ? exp2f(m - mxs) : 1.f;
 #pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32_nowait(t_o + 32 * c, o);
           tmem_wait_ld();
@@ -390,22 +421,23 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
         tmem_wait_st();
         l *= alpha;
       }
-      if (grow || m == -INFINITY) m = mx;  // the first keys of the row set the reference
-      const float m_use = m == -INFINITY ? 0.f : m;
-      unsigned char* ps = smem + kOffP + sb * kTile;
+      if (grow || m == -INFINITY) m = mxs;  // the first keys of the row set the reference
+      const float neg_m = m == -INFINITY ? 0.f : -m;
+      unsigned char* ps = smem + kOffP + sb * kTile + half * kPanel;  // this half's keys: panel `half`
       float lsum = 0.f;
 #pragma unroll
-      for (int ch = 0; ch < kKT / 8; ++ch) {  // keys 8 ch .. 8 ch + 7 = 16-byte chunk ch of this row
+      for (int ch = 0; ch < 8; ++ch) {  // keys 8 ch .. 8 ch + 7 of this half = 16-byte chunk ch of its panel
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
-          const float p0 = exp2f(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e]) - m_use);  // masked: 2^-inf = 0
-          const float p1 = exp2f(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e + 1]) - m_use);
+          // 2^(s * scale * log2 e - m); masked keys hold -inf: 2^-inf = 0
+          const float p0 = exp2f(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e]), p.sl2, neg_m));
+          const float p1 = exp2f(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e + 1]), p.sl2, neg_m));
           const T h0 = Dt<T>::narrow(p0), h1 = Dt<T>::narrow(p1);
           lsum += Dt<T>::to_f32(h0) + Dt<T>::to_f32(h1);  // the rounded values P.V multiplies
           pk[e >> 1] = bits16(h0) | (bits16(h1) << 16);
         }
-        sts128(ps + (ch >> 3) * kPanel + swz(threadIdx.x, ch & 7), make_uint4(pk[0], pk[1], pk[2], pk[3]));
+        sts128(ps + swz(row, ch), make_uint4(pk[0], pk[1], pk[2], pk[3]));
       }
       l += lsum;
       tc_fence_before();
@@ -414,21 +446,25 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&p_full[sb]);
     }
     if (ok && nkv > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&p_free[(nkv - 1) & 1], (uint32_t)((nkv - 1) >> 1) & 1u, p.err));  // the last P.V
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_free[(nkv - 1) & 1], (uint32_t)((nkv - 1) >> 1) & 1u, p.err));
       tc_fence_after();
     }
+    // the row's sum over both halves (every softmax warp reaches this barrier)
+    red[half * 128 + row] = l;
+    named_barrier_sync(1, kSoftWarps * 32);
+    l += red[(1 - half) * 128 + row];
     if (!ok) {
       misc[0] = 1;
     } else {
-      uint32_t o[kD / 32][32];
+      uint32_t o[2][32];
 #pragma unroll
-      for (int c = 0; c < kD / 32; ++c) tmem_ld32_nowait(t_o + 32 * c, o[c]);
+      for (int c = 0; c < 2; ++c) tmem_ld32_nowait(t_o + 32 * c, o[c]);
       tmem_wait_ld();
       if (row_ok) {
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(qst + qi) * p.out_st + (int64_t)h * p.out_sh;
+        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(qst + qi) * p.out_st + (int64_t)h * p.out_sh + 64 * half;
 #pragma unroll
-        for (int c = 0; c < kD / 8; ++c) {
+        for (int c = 0; c < 8; ++c) {
           uint32_t w[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -446,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5)
+  if (warp == kWarpMma)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
