@@ -9,8 +9,10 @@ read of an unwritten slot or a stray table entry shows up.
 Every step runs FastDecodeImpl._forward_split (tier-aware KV write + split-KV
 decode through the C ABI) and is compared with fp32 attention over one unified
 cache holding the same data; the new K/V must land bit-exactly in the tier
-that owns each slot.  Prefill rows go to a torch stand-in for FlashAttention
-(prefill is outside this engine).  Tolerances: fp16 output 2e-3 absolute,
+that owns each slot.  Prefill rows (P and F classes) run on this engine's
+tcgen05 prefill kernel (fd_prefill_attn); one case switches it off
+(FASTDECODE_B200_PREFILL=0), which sends them to a torch stand-in for
+FlashAttention as in the reference.  Tolerances: fp16 output 2e-3 absolute,
 bf16 1.6e-2 (the decode tests' bounds), relative to outputs of magnitude <= 1.
 """
 
@@ -65,19 +67,21 @@ class GpuOpsTorchPrefill(backend._GpuOps):
     fa = staticmethod(torch_fa)
 
 
-@pytest.mark.parametrize("dtype,H,KVH,two_pass,device_plan", [
-    (torch.float16, 8, 8, False, False),
-    (torch.bfloat16, 16, 4, False, False),
-    (torch.float16, 8, 2, True, False),
-    (torch.float16, 8, 8, False, True),
-    (torch.bfloat16, 16, 4, False, True),
+@pytest.mark.parametrize("dtype,H,KVH,two_pass,device_plan,b200_prefill", [
+    (torch.float16, 8, 8, False, False, True),
+    (torch.bfloat16, 16, 4, False, False, True),
+    (torch.float16, 8, 2, True, False, True),
+    (torch.float16, 8, 8, False, True, True),
+    (torch.bfloat16, 16, 4, False, True, True),
+    (torch.bfloat16, 16, 4, False, False, False),
 ])
-def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass, device_plan):
+def test_continuous_batching_trace(monkeypatch, dtype, H, KVH, two_pass, device_plan, b200_prefill):
     """device_plan: decode-only steps are planned on the GPU (fd_plan_step)
     and run through FastDecodeImpl._forward_device, as the metadata builder
     does for them; steps with prefills take the host planner."""
     if two_pass:
         monkeypatch.setenv(config.ENV_TWO_PASS, "1")
+    monkeypatch.setenv(config.ENV_PREFILL, "1" if b200_prefill else "0")
     monkeypatch.setattr(backend, "OPS", GpuOpsTorchPrefill)
     from vllm_fastdecoder_b200 import gpu_ops
 

@@ -127,6 +127,35 @@ __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUten
   if (lane == 0) mbar_arrive(bar);
 }
 
+// 2^x by the SFU's ex2 instruction (relative error a few ulp of fp32;
+// 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two floats rounded to T and packed (lo, hi) in one conversion; r0, r1 the
+// rounded values as floats.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b, float& r0, float& r1);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b, float& r0, float& r1) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&v);
+  r0 = __uint_as_float(u << 16);
+  r1 = __uint_as_float(u & 0xffff0000u);
+  return u;
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b, float& r0, float& r1) {
+  const __half2 v = __floats2half2_rn(a, b);
+  const float2 f = __half22float2(v);
+  r0 = f.x;
+  r1 = f.y;
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_constant__ PrefillParams p) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -370,21 +399,27 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
         if (lane == 0) mbar_arrive(&s_empty[sb]);  // S buffer free for the tile after next
       }
       const bool full_tile = j * kKT + kKT - 1 <= lim_all;  // below the diagonal for every row: no mask
-      if (!ok) {
-      } else if (full_tile) {
+      if (ok) {
+        // eight independent partial maxima (short dependency chains)
+        float m8[8];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
+        if (full_tile) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
-      } else {
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+            for (int e = 0; e < 32; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(sr[c][e]));
+        } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
-            sr[c][e] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float x = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
+              sr[c][e] = __float_as_uint(x);
+              m8[e & 7] = fmaxf(m8[e & 7], x);
+            }
+        }
+        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       }
       // the row's maximum over both halves (two barriers: values written,
       // then read, before the next tile overwrites them)
@@ -424,22 +459,22 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       if (grow || m == -INFINITY) m = mxs;  // the first keys of the row set the reference
       const float neg_m = m == -INFINITY ? 0.f : -m;
       unsigned char* ps = smem + kOffP + sb * kTile + half * kPanel;  // this half's keys: panel `half`
-      float lsum = 0.f;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {  // keys 8 ch .. 8 ch + 7 of this half = 16-byte chunk ch of its panel
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
-          // 2^(s * scale * log2 e - m); masked keys hold -inf: 2^-inf = 0
-          const float p0 = exp2f(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e]), p.sl2, neg_m));
-          const float p1 = exp2f(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e + 1]), p.sl2, neg_m));
-          const T h0 = Dt<T>::narrow(p0), h1 = Dt<T>::narrow(p1);
-          lsum += Dt<T>::to_f32(h0) + Dt<T>::to_f32(h1);  // the rounded values P.V multiplies
-          pk[e >> 1] = bits16(h0) | (bits16(h1) << 16);
+          // 2^(s * scale * log2 e - m) by the hardware ex2 (2^-inf = 0 for masked keys)
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e]), p.sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e + 1]), p.sl2, neg_m));
+          float r0, r1;
+          pk[e >> 1] = pack2<T>(p0, p1, r0, r1);  // rounded to T; r0, r1: the values P.V multiplies
+          ls[e >> 1] += r0 + r1;
         }
         sts128(ps + swz(row, ch), make_uint4(pk[0], pk[1], pk[2], pk[3]));
       }
-      l += lsum;
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tc_fence_before();
       fence_proxy_async_smem();  // generic smem writes of P (and TMEM stores of O) before the MMA reads them
       __syncwarp();
