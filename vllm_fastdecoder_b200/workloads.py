@@ -335,5 +335,6 @@ def materialize(b: Batch, device: torch.device, seed: int | None = None) -> Resi
         host_tier = KVTier(hk, hv)
     q = torch.empty(b.n, b.H, D, dtype=dt, device=device)
     _fill_normal(q, gen)
-    torch.cuda.synchronize(device)
+    if device is not None and torch.device(device).type == "cuda":
+        torch.cuda.synchronize(device)
     return Resident(b, q, (hbm_tier, host_tier), phys, b.block_table.to(device), b.lens.to(device))
