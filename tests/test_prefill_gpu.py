@@ -48,11 +48,12 @@ def _check(out, ref, q_start, q_len, dtype, T):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("H,KVH", [(8, 2), (4, 4)])
+@pytest.mark.parametrize("H,KVH", [(8, 2), (4, 4), (16, 2)])
 def test_prefill_paged_matches_reference(dtype, H, KVH):
     """P class: queries over a cached context in the paged HBM tier (vLLM's
     NHD layout), tiles cut across and inside requests, a one-token request,
-    a request whose queries start mid-tile of the batch."""
+    a request whose queries start mid-tile of the batch; query groups 4, 1
+    and 8 (a tile holds 128 / G query tokens of all G heads of a kv head)."""
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(11 + H)
     D, BS = 128, 16

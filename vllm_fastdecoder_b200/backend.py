@@ -388,10 +388,12 @@ class FastDecodeImpl(FlashAttentionImpl):
 
     def _prefill_on_b200(self, query) -> bool:
         """Whether this layer's prefill rows run on fd_prefill_attn: enabled
-        (FASTDECODE_B200_PREFILL), fp16 / bf16, head size 128, no soft cap;
-        otherwise FlashAttention, as in the reference."""
+        (FASTDECODE_B200_PREFILL), fp16 / bf16, head size 128, a query group
+        dividing 128, no soft cap; otherwise FlashAttention, as in the
+        reference."""
+        G = self.num_heads // max(1, self.num_kv_heads)
         return (config.b200_prefill() and query.dtype in (torch.float16, torch.bfloat16) and self.head_size == 128
-                and not self.logits_soft_cap)
+                and not self.logits_soft_cap and G <= 16 and 128 % G == 0)
 
     def _split_two_pass(self, query, tiers, G, dp: DevicePlan, output):
         """The reference's structure (backend.py:293-356): an HBM partial over

@@ -940,7 +940,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // {D, 1, TT, 1}.  Returns false when the driver rejects it (the caller then
 // copies tile rows one by one).
 bool encode_tier_map_uncached(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
-                              int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128) {
+                              int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128, int BH) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (enc == nullptr || nblk <= 0 || nblk > (int64_t)0xffffffff) return false;
   CUtensorMapDataType dt = dtype == FD_DTYPE_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -949,7 +949,7 @@ bool encode_tier_map_uncached(CUtensorMap* m, const void* base, int dtype, int D
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)KVH, (cuuint64_t)BS, (cuuint64_t)nblk};
   const cuuint64_t strides[3] = {(cuuint64_t)head_sb, (cuuint64_t)tok_sb, (cuuint64_t)blk_sb};
   // swizzled: 128-byte box rows (64 16-bit dims), the layout the UMMA reads
-  const cuuint32_t box[4] = {swizzle128 ? 64u : (cuuint32_t)D, 1u, (cuuint32_t)TT, 1u};
+  const cuuint32_t box[4] = {swizzle128 ? 64u : (cuuint32_t)D, (cuuint32_t)BH, (cuuint32_t)TT, 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -963,11 +963,12 @@ bool encode_tier_map_uncached(CUtensorMap* m, const void* base, int dtype, int D
 struct TmapKey {
   const void* base;
   int64_t nblk, head_sb, tok_sb, blk_sb;
-  int dtype, D, KVH, BS, TT, swizzle;
+  int dtype, D, KVH, BS, TT, swizzle, BH;
 };
 
 bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH, int BS, int64_t nblk,
-                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128 = false) {
+                     int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int TT, bool swizzle128 = false,
+                     int BH = 1) {
   constexpr int kSlots = 32;
   struct Entry {
     TmapKey key;
@@ -990,6 +991,7 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
   key.BS = BS;
   key.TT = TT;
   key.swizzle = swizzle128 ? 1 : 0;
+  key.BH = BH;
   {
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < kSlots; ++i)
@@ -998,7 +1000,7 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
         return true;
       }
   }
-  if (!encode_tier_map_uncached(m, base, dtype, D, KVH, BS, nblk, head_sb, tok_sb, blk_sb, TT, swizzle128))
+  if (!encode_tier_map_uncached(m, base, dtype, D, KVH, BS, nblk, head_sb, tok_sb, blk_sb, TT, swizzle128, BH))
     return false;
   std::lock_guard<std::mutex> lock(mu);
   Entry& e = cache[next];
@@ -1012,11 +1014,13 @@ bool encode_tier_map(CUtensorMap* m, const void* base, int dtype, int D, int KVH
 }  // namespace
 
 namespace fdk {
-// Cached 4-D tiled tensor map {D, heads, BS, blocks} with box {64 or D, 1,
-// box_tokens, 1} (the encoder the decode kernels use), for the prefill kernel.
+// Cached 4-D tiled tensor map {D, heads, BS, blocks} with box {64 or D,
+// box_heads, box_tokens, 1} (the encoder the decode kernels use), for the
+// prefill kernel.
 bool encode_kv_map(CUtensorMap* m, const void* base, int dtype, int D, int heads, int BS, int64_t nblk,
-                   int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int box_tokens, bool swizzle128) {
-  return encode_tier_map(m, base, dtype, D, heads, BS, nblk, head_sb, tok_sb, blk_sb, box_tokens, swizzle128);
+                   int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int box_tokens, bool swizzle128, int box_heads) {
+  return encode_tier_map(m, base, dtype, D, heads, BS, nblk, head_sb, tok_sb, blk_sb, box_tokens, swizzle128,
+                         box_heads);
 }
 }  // namespace fdk
 

@@ -268,10 +268,11 @@ int launch_decode_mma(const DecodeParams& p, int dtype, int D, size_t extra_smem
                       bool* launched, bool pdl);
 
 // Tiled tensor map of a 4-D view {D, heads, BS, blocks} (byte strides of
-// heads, tokens and blocks), box {64 (swizzled) or D, 1, box_tokens, 1},
-// cached per view (fd_decode.cu); false when the driver rejects it.
+// heads, tokens and blocks), box {64 (swizzled) or D, box_heads, box_tokens,
+// 1}, cached per view (fd_decode.cu); false when the driver rejects it.
 bool encode_kv_map(CUtensorMap* m, const void* base, int dtype, int D, int heads, int BS, int64_t nblk,
-                   int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int box_tokens, bool swizzle128);
+                   int64_t head_sb, int64_t tok_sb, int64_t blk_sb, int box_tokens, bool swizzle128,
+                   int box_heads = 1);
 
 // Whether the tcgen05 kernel covers this shape (16-bit KV, head size 128,
 // query group 2, 4 or 8, block size a multiple of 16).

@@ -3,7 +3,9 @@
 // classes of the split path, which the reference hands to FlashAttention
 // (fastdecode/backend.py:317-340, flash_attn_varlen_func with causal=True).
 //
-// A CTA computes 128 query rows of one request for one query head:
+// A CTA computes 128 rows of one request for one kv head: 128 / G query
+// tokens times the G query heads that share the kv head (row = token * G +
+// head), so each K/V tile is loaded once for the whole group:
 //   S [128 q x 128 keys] = Q [128 x D] . K^T        (tcgen05, K-major A and B)
 //   O [128 q x D]       = P [128 x 128 keys] . V   (tcgen05, V as MN-major B)
 // over the key tiles the causal mask leaves (query i of a request with q_len
@@ -88,6 +90,7 @@ struct PrefillParams {
   const int32_t* k_len;
   const int32_t* bt_row;
   int n, H, G, BS;
+  int tq;     // query tokens per tile: 128 / G (the G heads of a kv head share the tile's 128 rows)
   float sl2;  // scale * log2(e)
   int dtype;
   int32_t* err;
@@ -182,8 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
-  const int kh = h / p.G;
+  const int kh = blockIdx.y;    // kv head; rows of the tile are (query token, head of its group) pairs
+  const int h0 = kh * p.G;      // first query head of the group
+  const int tq = p.tq;          // query tokens per tile (128 / G)
   const int b = blockIdx.x;
 
   // ---------------------------------------------------------------- setup
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     for (int base = 0; base < p.n && found < 0; base += 32) {
       const int i = base + lane;
       const int ql = i < p.n ? p.q_len[i] : 0;
-      const int c = ql > 0 ? (ql + kM - 1) / kM : 0;
+      const int c = ql > 0 ? (ql + tq - 1) / tq : 0;
       int v = c;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   __syncthreads();
   const int r = misc[1];
   if (r < 0) return;  // spare CTA of the grid's upper bound (before any TMEM is held)
-  const int q0 = (b - misc[2]) * kM;
+  const int q0 = (b - misc[2]) * tq;
   const int qlen = p.q_len[r];
   const int klen = p.k_len[r];
   const int qst = p.q_start[r];
@@ -243,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
     return;
   }
-  const int i_last = min(q0 + kM, qlen) - 1;         // last query of this tile
+  const int i_last = min(q0 + tq, qlen) - 1;         // last query of this tile
   const int nkv = (klen - qlen + i_last) / kKT + 1;  // key tiles the causal mask leaves
 
   // K and V rings start as zeros: boxes not loaded (keys past k_len) hold
@@ -269,8 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     const bool is_k = warp == kWarpK;
     if (is_k && lane == 0) {
       mbar_expect_tx(q_full, (uint32_t)kTile);
-      tma_load_4d(qs, &p.tmap_q, 0, h, qst + q0, 0, q_full, 0ull);
-      tma_load_4d(qs + kPanel, &p.tmap_q, 64, h, qst + q0, 0, q_full, 0ull);
+      // box {64 dims, G heads, 128 / G tokens}: row r = token (r / G), head h0 + r % G
+      tma_load_4d(qs, &p.tmap_q, 0, h0, qst + q0, 0, q_full, 0ull);
+      tma_load_4d(qs + kPanel, &p.tmap_q, 64, h0, qst + q0, 0, q_full, 0ull);
       mbar_arrive(q_full);
     }
     const uint64_t pol = l2_evict_first_policy();
@@ -368,8 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     // in TMEM, each half its 64 dims, and the sums l are rescaled once), so
     // values of P stay <= 256.
     const int half = warp >> 2;
-    const int row = (warp & 3) * 32 + lane;                  // query row of the tile = TMEM lane
-    const int qi = q0 + row;                                  // query index within the request
+    const int row = (warp & 3) * 32 + lane;                  // row of the tile = TMEM lane
+    const int qi = q0 + row / p.G;                            // its query index within the request
+    const int h = h0 + row % p.G;                             // and its query head
     const bool row_ok = qi < qlen;
     const int lim = row_ok ? klen - qlen + qi : -1;          // last key this query sees
     const int lim_all = klen - qlen + q0;                     // keys every query of the tile sees
@@ -558,9 +564,13 @@ extern "C" int fd_prefill_attn(const fd_prefill_args* a, void* stream) {
 
   PrefillParams p{};
   const int H = a->num_heads, KVH = a->num_kv_heads;
-  // q as {D, H, tokens, 1} with a 128-query box
+  const int G = H / KVH;
+  if (G > 16 || fdk::pf::kM % G != 0)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: query group %d must divide 128 (at most 16)", G);
+  const int tq = fdk::pf::kM / G;
+  // q as {D, H, tokens, 1} with a box of the G heads of a kv head x 128 / G queries
   bool ok = fdk::encode_kv_map(&p.tmap_q, a->q, a->dtype, (int)D, H, a->num_tokens, 1, a->q_stride_h * es,
-                               a->q_stride_t * es, a->q_stride_t * es * a->num_tokens, fdk::pf::kM, true);
+                               a->q_stride_t * es, a->q_stride_t * es * a->num_tokens, tq, true, G);
   if (paged) {
     ok = ok && fdk::encode_kv_map(&p.tmap_k, kv.k, a->dtype, (int)D, KVH, a->block_size, kv.num_blocks,
                                   kv.head_stride * es, kv.tok_stride * es, kv.blk_stride * es, fdk::pf::kSub, true);
@@ -588,22 +598,23 @@ extern "C" int fd_prefill_attn(const fd_prefill_args* a, void* stream) {
   p.bt_row = a->bt_row;
   p.n = a->n;
   p.H = H;
-  p.G = H / KVH;
+  p.G = G;
+  p.tq = tq;
   p.BS = paged ? a->block_size : 1;
   p.sl2 = a->scale * fdk::kLog2e;
   p.dtype = a->dtype;
   p.err = a->error;
 
-  // grid: an upper bound of the query tiles (sum of ceil(q_len / 128) <=
-  // ceil(total_q / 128) + n) by heads; spare CTAs return at once
-  const int64_t tiles = ((int64_t)a->total_q + fdk::pf::kM - 1) / fdk::pf::kM + a->n;
+  // grid: an upper bound of the query tiles (sum of ceil(q_len / tq) <=
+  // ceil(total_q / tq) + n) by kv heads; spare CTAs return at once
+  const int64_t tiles = ((int64_t)a->total_q + tq - 1) / tq + a->n;
   if (tiles > 0x7fffffff) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: too many query tiles");
   const void* kern = a->dtype == FD_DTYPE_BF16 ? reinterpret_cast<const void*>(fdk::pf::fd_prefill_kernel<__nv_bfloat16>)
                                                : reinterpret_cast<const void*>(fdk::pf::fd_prefill_kernel<__half>);
   static unsigned long long done_h = 0, done_b = 0;
   int st = fdh::ensure_smem(kern, fdk::pf::kSmem, a->dtype == FD_DTYPE_BF16 ? &done_b : &done_h);
   if (st != FD_OK) return st;
-  return fdh::launch_maybe_pdl(kern, dim3((unsigned)tiles, (unsigned)H), dim3(fdk::pf::kThreads), fdk::pf::kSmem,
+  return fdh::launch_maybe_pdl(kern, dim3((unsigned)tiles, (unsigned)KVH), dim3(fdk::pf::kThreads), fdk::pf::kSmem,
                                static_cast<cudaStream_t>(stream), false, p, "fd_prefill_kernel launch");
 }
 
