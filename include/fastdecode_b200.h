@@ -392,7 +392,7 @@ FD_API int fd_peer_open(const void *ipc_handle, void **ptr);
 FD_API int fd_peer_close(void *ptr);
 FD_API int fd_peer_free(void *ptr);
 /* One step: every rank calls it once per step, in the same order, with the
- * same n / heads / head size / num_ctas (0: 32, at most 64).  send: this rank's packed
+ * same n / heads / head size / num_ctas (0: 64, at most 64; CTAs of 128 threads).  send: this rank's packed
  * partial (16-byte aligned); out [n, H, D] in out_dtype; out_lse [H, n] or
  * NULL.  Each value a rank pushes carries the step number in the same
  * 8-byte word; the merge waits until every word it reads carries this step

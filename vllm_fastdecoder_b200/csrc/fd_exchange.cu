@@ -8,7 +8,7 @@
 //   [0]    step counters    u64 [kMaxCtas]: CTA b's completed steps (its own)
 //   [8192] receive slots    [2 parities][world][slot] tagged words: float i of
 //                            a slot is the 8-byte word {value bits, step}
-// One launch per step of at most 64 CTAs of 256 threads, which the SMs hold
+// One launch per step of at most 64 CTAs of 128 threads, which the SMs hold
 // at once (every wait is bounded in any case):
 //   1. every CTA stores its share of the rank's packed partial into slot
 //      [parity][rank] of every rank's buffer over NVLink, each float with the
@@ -51,7 +51,11 @@
 
 namespace fdk {
 
-constexpr int kXThreads = 256;  // threads per exchange CTA
+// threads per exchange CTA: small CTAs (128 threads x ~145 registers) fit on
+// an SM beside a tensor-core decode CTA, so the next step's decode, launched
+// as a programmatic dependent of this kernel, can be resident on every SM
+// while the exchange runs
+constexpr int kXThreads = 128;
 constexpr int kXMaxCtas = 64;   // CTAs per launch, at most (per-CTA step counters)
 
 struct ExchangeParams {
@@ -386,7 +390,7 @@ int exchange_params(const fd_peer_exchange* x, const float* send, int32_t n, int
     return fdh::fail(FD_ERR_ALIGN, "%s: send buffer not 16-byte aligned", what);
   for (int q = 0; q < x->world; ++q)
     if (x->base[q] == nullptr) return fdh::fail(FD_ERR_INVALID, "%s: rank %d buffer unmapped", what, q);
-  *ctas = num_ctas > 0 ? num_ctas : 32;
+  *ctas = num_ctas > 0 ? num_ctas : 64;
   if (*ctas > fdk::kXMaxCtas) return fdh::fail(FD_ERR_INVALID, "%s: at most %d CTAs (%d)", what, fdk::kXMaxCtas, *ctas);
   *p = fdk::ExchangeParams{};
   p->send = send;
@@ -411,8 +415,8 @@ int exchange_params(const fd_peer_exchange* x, const float* send, int32_t n, int
 
 // Every CTA waits for every other.  A cooperative launch would guarantee
 // co-residency but cost ~55 us per step on B200 (measured); at most 64 CTAs
-// of 256 threads and no shared memory are resident together on an otherwise
-// idle stream, and the bounded wait turns any exception into
+// of 128 threads and no shared memory are resident together (beside decode
+// CTAs too), and the bounded wait turns any exception into
 // FD_DEVERR_TIMEOUT rather than a hang.  Programmatic dependent launch: the
 // CTAs may start while the kernel ahead on the stream finishes and wait for
 // it in griddepcontrol.wait.

@@ -106,7 +106,7 @@ class PeerExchange:
     synchronisation): after a timeout it marks the exchange unusable, so
     later steps raise until every rank closes it and builds a new one."""
 
-    def __init__(self, n: int, H: int, D: int, world: int, device: torch.device, group=None, num_ctas: int = 32,
+    def __init__(self, n: int, H: int, D: int, world: int, device: torch.device, group=None, num_ctas: int = 64,
                  timeout_s: float = 2.0):
         import ctypes
 
