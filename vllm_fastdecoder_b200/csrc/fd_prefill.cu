@@ -7,28 +7,29 @@
 // tokens times the G query heads that share the kv head (row = token * G +
 // head), so each K/V tile is loaded once for the whole group:
 //   S [128 q x 128 keys] = Q [128 x D] . K^T        (tcgen05, K-major A and B)
-//   O [128 q x D]       = P [128 x 128 keys] . V   (tcgen05, V as MN-major B)
+//   O [128 q x D]       = P [128 x 128 keys] . V   (tcgen05, P from TMEM, V as MN-major B)
 // over the key tiles the causal mask leaves (query i of a request with q_len
 // queries and k_len keys sees keys 0 .. k_len - q_len + i: the bottom-right
 // alignment of FlashAttention's causal mask).  Six warps:
 //   warps 8, 10  TMA producers: warp 8 loads Q once (box {64, 1, 128, 1})
-//            and the K tiles of 128 keys into a 2-slot ring, warp 10 the V
-//            tiles into their own 2-slot ring (a K slot is free once its
+//            and the K tiles of 128 keys into a 3-slot ring, warp 10 the V
+//            tiles into their own 3-slot ring (a K slot is free once its
 //            q.K^T completed, a V slot once its P.V did), one 16-key box per
 //            lane and 64-dim half (128-byte swizzle, the layout the MMA
 //            reads); keys come from the paged HBM cache through the block
 //            table, or from the batch's own new K/V rows (fresh prefills)
 //   warp 9   MMA issuer (one thread): polls both products and issues q.K^T
 //            of a tile into one of two TMEM S buffers once its keys landed,
-//            P.V of a tile once its P (double-buffered in shared memory) and
-//            V are in place; tcgen05.commit to mbarriers
+//            P.V of a tile once its P (double-buffered in TMEM) and V are
+//            in place; tcgen05.commit to mbarriers
 //   warps 0-7  softmax, two warpgroups: warp w owns query rows 32 (w % 4) ..
 //            + 31 (TMEM lanes) and keys 64 (w / 4) .. + 63 of each tile; it
 //            loads its half of the S row into registers, masks it (tiles
 //            below the causal diagonal skip the mask), exchanges the half-
 //            row maximum with its partner warp through shared memory, and
-//            writes P = 2^(s - m) as 16-bit values into its panel of the
-//            swizzled A operand of P.V; O accumulates in TMEM over the
+//            writes P = 2^(s - m) as 16-bit values packed two per TMEM
+//            column, the A operand of P.V (no shared-memory round trip and
+//            no proxy fence); O accumulates in TMEM over the
 //            tiles, rescaled (each warpgroup its 64 dims) only when the
 //            row's maximum moves past its reference m by more than 2^8; at
 //            the end o = O / l.
@@ -56,19 +57,20 @@ constexpr int kKT = 128;                // keys per tile (MMA N of S, K of P.V)
 constexpr int kSub = 16;                // keys per TMA box
 constexpr int kSubs = kKT / kSub;       // boxes per 64-dim half of a tile
 constexpr int kPanel = 128 * 128;       // 128 rows x 128 B (64 dims)
-constexpr int kTile = 2 * kPanel;       // K or V of one tile / Q / P (32 KB)
+constexpr int kTile = 2 * kPanel;       // K or V of one tile / Q (32 KB)
 constexpr int kSoftWarps = 8;           // two warpgroups: keys 0-63 and 64-127 of each tile
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K producer, MMA issuer, V producer
 constexpr int kThreads = 11 * 32;
-constexpr int kTmemCols = 512;          // S0 [0,128) S1 [128,256) O [256,384)
+constexpr int kTmemCols = 512;          // S0 [0,128) S1 [128,256) O [256,384) P0, P1 [384,512)
 
-// shared memory: Q | K ring [2] | V ring [2] | P [2] | barriers | TMEM slot | misc
+// shared memory: Q | K ring [3] | V ring [3] | barriers | TMEM slot | misc | row reductions
 constexpr int kOffQ = 0;
+constexpr int kRing = 3;                // slots of the K ring and of the V ring
 constexpr int kOffK = kOffQ + kTile;
-constexpr int kOffV = kOffK + 2 * kTile;
-constexpr int kOffP = kOffV + 2 * kTile;
-constexpr int kOffBar = kOffP + 2 * kTile;
-constexpr int kNumBars = 1 + 4 * 2 + 2 * 2 + 2 * 2 + 1;  // q_full, k/v full/empty, s_full/empty, p_full/free, drain
+constexpr int kOffV = kOffK + kRing * kTile;
+constexpr int kOffBar = kOffV + kRing * kTile;
+constexpr int kNumBars = 1 + 4 * kRing + 2 * 2 + 2 * 2 + 1;  // q_full, k/v full/empty, s_full/empty, p_full/free, drain
+constexpr int kTmemP = 3 * kKT;         // P0 [384, 448), P1 [448, 512): 16-bit P packed two per column
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kOffMisc = (kOffTmem + 16 + 15) / 16 * 16;  // [0] abort, [1] request, [2] its first tile
 constexpr int kOffRed = kOffMisc + 64;                     // [2 halves][128 rows] floats: row maxima, then sums
@@ -169,17 +171,17 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   unsigned char* smem = smem_raw + ((((raw + 1023u) & ~1023u)) - raw);
   unsigned char* qs = smem + kOffQ;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;           // producer lane 0 + the TMA bytes of Q
-  uint64_t* k_full = bars + 1;       // [2] K tile landed
-  uint64_t* k_empty = bars + 3;      // [2] MMA commit after q.K^T
-  uint64_t* v_full = bars + 5;       // [2] V tile landed
-  uint64_t* v_empty = bars + 7;      // [2] MMA commit after P.V
-  uint64_t* s_full = bars + 9;       // [2] MMA commit: S ready
-  uint64_t* s_empty = bars + 11;     // [2] 4 softmax warps read S
-  uint64_t* p_full = bars + 13;      // [2] 4 softmax warps wrote P
-  uint64_t* p_free = bars + 15;      // [2] MMA commit after P.V: P buffer free, O up to date
-  uint64_t* drain = bars + 17;       // MMA commit before TMEM release
-  static_assert(kNumBars == 18, "barrier count");
+  uint64_t* q_full = bars;                    // producer lane 0 + the TMA bytes of Q
+  uint64_t* k_full = bars + 1;                // [kRing] K tile landed
+  uint64_t* k_empty = k_full + kRing;         // [kRing] MMA commit after q.K^T
+  uint64_t* v_full = k_empty + kRing;         // [kRing] V tile landed
+  uint64_t* v_empty = v_full + kRing;         // [kRing] MMA commit after P.V
+  uint64_t* s_full = v_empty + kRing;         // [2] MMA commit: S ready
+  uint64_t* s_empty = s_full + 2;             // [2] softmax warps read S
+  uint64_t* p_full = s_empty + 2;             // [2] softmax warps wrote P (TMEM)
+  uint64_t* p_free = p_full + 2;              // [2] MMA commit after P.V: P buffer free, O up to date
+  uint64_t* drain = p_free + 2;               // MMA commit before TMEM release
+  static_assert(1 + 4 * kRing + 8 + 1 == kNumBars, "barrier count");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   volatile int* misc = reinterpret_cast<volatile int*>(smem + kOffMisc);
 
@@ -222,11 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   if (threadIdx.x == 32) {
     misc[0] = 0;
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], kSoftWarps);  // one arrival per softmax warp
       mbar_init(&p_full[s], kSoftWarps);
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
 
   // K and V rings start as zeros: boxes not loaded (keys past k_len) hold
   // finite values, which P = 0 cancels
-  for (int o = threadIdx.x * 16; o < 4 * kTile; o += kThreads * 16)
+  for (int o = threadIdx.x * 16; o < 2 * kRing * kTile; o += kThreads * 16)
     sts128(smem + kOffK + o, make_uint4(0u, 0u, 0u, 0u));
   fence_proxy_async_smem();
   if (warp == kWarpMma) {
@@ -283,8 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     uint64_t* emptyb = is_k ? k_empty : v_empty;
     unsigned char* ring = smem + (is_k ? kOffK : kOffV);
     for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      if (j >= 2 && !mbar_wait(&emptyb[st], (uint32_t)((j >> 1) - 1) & 1u, p.err)) {
+      const int st = j % kRing;
+      if (j >= kRing && !mbar_wait(&emptyb[st], (uint32_t)((j / kRing) - 1) & 1u, p.err)) {
         misc[0] = 1;
         break;
       }
@@ -306,11 +310,11 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       while (ok && kp < nkv) {
         bool prog = false;
         if (kq < nkv && kq < kp + 2) {
-          const int sb = kq & 1;
-          if (mbar_test_wait(&k_full[sb], (uint32_t)(kq >> 1) & 1u) &&
+          const int sb = kq & 1, kslot = kq % kRing;
+          if (mbar_test_wait(&k_full[kslot], (uint32_t)(kq / kRing) & 1u) &&
               (kq < 2 || mbar_test_wait(&s_empty[sb], (uint32_t)((kq >> 1) - 1) & 1u))) {
             tc_fence_after();
-            const uint32_t sk = smem_u32(smem + kOffK + sb * kTile);
+            const uint32_t sk = smem_u32(smem + kOffK + kslot * kTile);
 #pragma unroll
             for (int ks = 0; ks < kD / 16; ++ks) {
               const uint32_t off = (ks >> 2) * kPanel + (ks & 3) * 32;
@@ -318,26 +322,23 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
                        ks > 0 ? 1u : 0u);
             }
             umma_commit(&s_full[sb]);
-            umma_commit(&k_empty[sb]);
+            umma_commit(&k_empty[kslot]);
             ++kq;
             prog = true;
           }
         }
         if (kp < kq) {
-          const int pb = kp & 1;
+          const int pb = kp & 1, vslot = kp % kRing;
           if (mbar_test_wait(&p_full[pb], (uint32_t)(kp >> 1) & 1u) &&
-              mbar_test_wait(&v_full[pb], (uint32_t)(kp >> 1) & 1u)) {
+              mbar_test_wait(&v_full[vslot], (uint32_t)(kp / kRing) & 1u)) {
             tc_fence_after();
-            const uint32_t sp = smem_u32(smem + kOffP + pb * kTile);
-            const uint32_t sv = smem_u32(smem + kOffV + pb * kTile);
+            const uint32_t sv = smem_u32(smem + kOffV + vslot * kTile);
 #pragma unroll
-            for (int ks = 0; ks < kKT / 16; ++ks) {
-              const uint32_t poff = (ks >> 2) * kPanel + (ks & 3) * 32;
-              umma_f16(tmem + 2 * kKT, sw128_desc(sp + poff, 16, 1024), sw128_desc(sv + ks * 2048, kPanel, 1024),
-                       kIdPV, (kp > 0 || ks > 0) ? 1u : 0u);  // O accumulates over the tiles
-            }
+            for (int ks = 0; ks < kKT / 16; ++ks)  // A = P from TMEM: 16 keys = 8 packed columns per step
+              umma_f16_ts(tmem + 2 * kKT, tmem + kTmemP + 64 * pb + 8 * ks, sw128_desc(sv + ks * 2048, kPanel, 1024),
+                          kIdPV, (kp > 0 || ks > 0) ? 1u : 0u);  // O accumulates over the tiles
             umma_commit(&p_free[pb]);
-            umma_commit(&v_empty[pb]);
+            umma_commit(&v_empty[vslot]);
             ++kp;
             prog = true;
           }
@@ -464,25 +465,23 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       }
       if (grow || m == -INFINITY) m = mxs;  // the first keys of the row set the reference
       const float neg_m = m == -INFINITY ? 0.f : -m;
-      unsigned char* ps = smem + kOffP + sb * kTile + half * kPanel;  // this half's keys: panel `half`
+      // this half's 64 keys as 32 packed columns of P[sb] in TMEM (column c:
+      // keys 2c, 2c + 1 in the low and high halves), the A operand of P.V
       float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
+      uint32_t pk[32];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {  // keys 8 ch .. 8 ch + 7 of this half = 16-byte chunk ch of its panel
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          // 2^(s * scale * log2 e - m) by the hardware ex2 (2^-inf = 0 for masked keys)
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e]), p.sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + e + 1]), p.sl2, neg_m));
-          float r0, r1;
-          pk[e >> 1] = pack2<T>(p0, p1, r0, r1);  // rounded to T; r0, r1: the values P.V multiplies
-          ls[e >> 1] += r0 + r1;
-        }
-        sts128(ps + swz(row, ch), make_uint4(pk[0], pk[1], pk[2], pk[3]));
+      for (int c = 0; c < 32; ++c) {
+        // 2^(s * scale * log2 e - m) by the hardware ex2 (2^-inf = 0 for masked keys)
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 4][(2 * c) & 31]), p.sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c >> 4][(2 * c + 1) & 31]), p.sl2, neg_m));
+        float r0, r1;
+        pk[c] = pack2<T>(p0, p1, r0, r1);  // rounded to T; r0, r1: the values P.V multiplies
+        ls[c & 3] += r0 + r1;
       }
+      tmem_st32(tmem + lane_base + kTmemP + 64 * sb + 32 * half, pk);
+      tmem_wait_st();
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tc_fence_before();
-      fence_proxy_async_smem();  // generic smem writes of P (and TMEM stores of O) before the MMA reads them
+      tc_fence_before();  // TMEM stores of P (and of a rescaled O) before the MMA reads them
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
     }
