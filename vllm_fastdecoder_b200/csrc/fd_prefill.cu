@@ -3,36 +3,35 @@
 // classes of the split path, which the reference hands to FlashAttention
 // (fastdecode/backend.py:317-340, flash_attn_varlen_func with causal=True).
 //
-// A CTA computes 128 rows of one request for one kv head: 128 / G query
-// tokens times the G query heads that share the kv head (row = token * G +
-// head), so each K/V tile is loaded once for the whole group:
+// A CTA computes two query tiles A and B of one request for one kv head
+// (two consecutive tiles, the longer B last; a tile is 128 rows: 128 / G
+// query tokens times the G query heads that share the kv head, row = token
+// * G + head), so each K/V tile is loaded once for 256 rows:
 //   S [128 q x 128 keys] = Q [128 x D] . K^T        (tcgen05, K-major A and B)
 //   O [128 q x D]       = P [128 x 128 keys] . V   (tcgen05, P from TMEM, V as MN-major B)
 // over the key tiles the causal mask leaves (query i of a request with q_len
 // queries and k_len keys sees keys 0 .. k_len - q_len + i: the bottom-right
-// alignment of FlashAttention's causal mask).  Six warps:
-//   warps 8, 10  TMA producers: warp 8 loads Q once (box {64, 1, 128, 1})
-//            and the K tiles of 128 keys into a 3-slot ring, warp 10 the V
-//            tiles into their own 3-slot ring (a K slot is free once its
-//            q.K^T completed, a V slot once its P.V did), one 16-key box per
+// alignment of FlashAttention's causal mask).  Eleven warps:
+//   warps 8, 10  TMA producers: warp 8 loads both query tiles once (box
+//            {64, G, 128 / G, 1}) and the K tiles of 128 keys into a 3-slot
+//            ring, warp 10 the V tiles into a 2-slot ring (a slot is free
+//            once the products of its tile completed), one 16-key box per
 //            lane and 64-dim half (128-byte swizzle, the layout the MMA
 //            reads); keys come from the paged HBM cache through the block
 //            table, or from the batch's own new K/V rows (fresh prefills)
-//   warp 9   MMA issuer (one thread): polls both products and issues q.K^T
-//            of a tile into one of two TMEM S buffers once its keys landed,
-//            P.V of a tile once its P (double-buffered in TMEM) and V are
-//            in place; tcgen05.commit to mbarriers
-//   warps 0-7  softmax, two warpgroups: warp w owns query rows 32 (w % 4) ..
-//            + 31 (TMEM lanes) and keys 64 (w / 4) .. + 63 of each tile; it
-//            loads its half of the S row into registers, masks it (tiles
-//            below the causal diagonal skip the mask), exchanges the half-
-//            row maximum with its partner warp through shared memory, and
-//            writes P = 2^(s - m) as 16-bit values packed two per TMEM
-//            column, the A operand of P.V (no shared-memory round trip and
-//            no proxy fence); O accumulates in TMEM over the
-//            tiles, rescaled (each warpgroup its 64 dims) only when the
-//            row's maximum moves past its reference m by more than 2^8; at
-//            the end o = O / l.
+//   warp 9   MMA issuer (one thread), in an order that lets one tile's
+//            softmax overlap the other tile's products:
+//            P.V(A, j), q.K^T(A, j + 1), P.V(B, j), q.K^T(B, j + 1);
+//            tcgen05.commit to mbarriers
+//   warps 0-7  softmax, warpgroup x for query tile x: one thread per row
+//            loads the row's 128 scores of a key tile from TMEM, masks them
+//            (tiles below the causal diagonal skip the mask) and writes
+//            P = 2^(s - m) as 16-bit values packed two per TMEM column over
+//            the first 64 columns of the same S buffer, the A operand of
+//            P.V; O accumulates in TMEM over the tiles, rescaled only when
+//            the row's maximum moves past its reference m by more than 2^8;
+//            at the end o = O / l.
+//   TMEM: S/P of A [0,128), S/P of B [128,256), O of A [256,384), O of B [384,512).
 // Numerics: scores fp32 from the exact 16-bit q and K, P rounded to the
 // input type for P.V (as FlashAttention does), accumulation fp32.  Every
 // mbarrier wait is bounded (FD_DEVERR_TIMEOUT); TMEM is released on every
@@ -52,29 +51,29 @@ namespace fdk {
 namespace pf {
 
 constexpr int kD = 128;                 // head size
-constexpr int kM = 128;                 // query rows per CTA (MMA M)
+constexpr int kM = 128;                 // rows per query tile (MMA M)
 constexpr int kKT = 128;                // keys per tile (MMA N of S, K of P.V)
 constexpr int kSub = 16;                // keys per TMA box
 constexpr int kSubs = kKT / kSub;       // boxes per 64-dim half of a tile
 constexpr int kPanel = 128 * 128;       // 128 rows x 128 B (64 dims)
-constexpr int kTile = 2 * kPanel;       // K or V of one tile / Q (32 KB)
-constexpr int kSoftWarps = 8;           // two warpgroups: keys 0-63 and 64-127 of each tile
+constexpr int kTile = 2 * kPanel;       // K or V of one tile / one query tile (32 KB)
+constexpr int kSoftWarps = 8;           // two warpgroups: query tile A (warps 0-3) and B (warps 4-7)
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K producer, MMA issuer, V producer
 constexpr int kThreads = 11 * 32;
-constexpr int kTmemCols = 512;          // S0 [0,128) S1 [128,256) O [256,384) P0, P1 [384,512)
+constexpr int kTmemCols = 512;          // S/P A [0,128) S/P B [128,256) O A [256,384) O B [384,512)
+constexpr int kRingK = 3;               // slots of the K ring
+constexpr int kRingV = 2;               // slots of the V ring (V of a tile is read after its softmax)
 
-// shared memory: Q | K ring [3] | V ring [3] | barriers | TMEM slot | misc | row reductions
+// shared memory: Q A | Q B | K ring | V ring | barriers | TMEM slot | misc
 constexpr int kOffQ = 0;
-constexpr int kRing = 3;                // slots of the K ring and of the V ring
-constexpr int kOffK = kOffQ + kTile;
-constexpr int kOffV = kOffK + kRing * kTile;
-constexpr int kOffBar = kOffV + kRing * kTile;
-constexpr int kNumBars = 1 + 4 * kRing + 2 * 2 + 2 * 2 + 1;  // q_full, k/v full/empty, s_full/empty, p_full/free, drain
-constexpr int kTmemP = 3 * kKT;         // P0 [384, 448), P1 [448, 512): 16-bit P packed two per column
+constexpr int kOffK = kOffQ + 2 * kTile;
+constexpr int kOffV = kOffK + kRingK * kTile;
+constexpr int kOffBar = kOffV + kRingV * kTile;
+// q_full, k full/empty, v full/empty, s_full[2], p_full[2], o_full[2], drain
+constexpr int kNumBars = 1 + 2 * kRingK + 2 * kRingV + 3 * 2 + 1;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
-constexpr int kOffMisc = (kOffTmem + 16 + 15) / 16 * 16;  // [0] abort, [1] request, [2] its first tile
-constexpr int kOffRed = kOffMisc + 64;                     // [2 halves][128 rows] floats: row maxima, then sums
-constexpr int kSmem = kOffRed + 2 * 128 * 4 + 1024;        // + 1024 to align the base
+constexpr int kOffMisc = (kOffTmem + 16 + 15) / 16 * 16;  // [0] abort, [1] request, [2] its first pair
+constexpr int kSmem = kOffMisc + 64 + 1024;                // + 1024 to align the base
 static_assert(kSmem <= 227 * 1024, "smem budget");
 
 struct PrefillParams {
@@ -101,9 +100,12 @@ struct PrefillParams {
 // One producer warp's share of a key tile: lane l < 8 loads keys
 // [128 j + 16 l, +16) of K or V (both 64-dim halves) into `dst`, completion
 // as bytes on `bar` (lane 0 arms it with the bytes of the lanes that load).
+// With zero_missing, boxes past k_len are written as zeros instead (the warp
+// together, before the arrival): P is 0 there, and 0 x V must stay 0.  K
+// needs no fill: the causal mask replaces every score past k_len.
 __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUtensorMap* map, unsigned char* dst,
                                              uint64_t* bar, int j, int klen, int qst, int trow, int kh, int lane,
-                                             uint64_t pol) {
+                                             uint64_t pol, bool zero_missing) {
   const int t = j * kKT + lane * kSub;
   bool valid = lane < kSubs && t < klen;
   int blk = 0, r0 = 0;
@@ -128,8 +130,43 @@ __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUten
     tma_load_4d(dst + lane * kSub * 128, map, 0, kh, r0, blk, bar, pol);
     tma_load_4d(dst + kPanel + lane * kSub * 128, map, 64, kh, r0, blk, bar, pol);
   }
+  unsigned missing = ~vmask & ((1u << kSubs) - 1u);
+  if (zero_missing && missing != 0u) {
+    while (missing != 0u) {  // each missing box: 2 x 2 KB, 128 bytes per lane
+      const int s = __ffs(missing) - 1;
+      missing &= missing - 1u;
+      unsigned char* box = dst + s * kSub * 128 + lane * 64;
+      sts128(box, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + 16, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + 32, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + 48, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + kPanel, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + kPanel + 16, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + kPanel + 32, make_uint4(0u, 0u, 0u, 0u));
+      sts128(box + kPanel + 48, make_uint4(0u, 0u, 0u, 0u));
+    }
+    fence_proxy_async_smem();  // the zeros before the tensor cores read the slot
+  }
   __syncwarp();
   if (lane == 0) mbar_arrive(bar);
+}
+
+// Wait for the phase of `bar` with the given parity, giving up when another
+// role raised the abort flag or after kWaitLimitNs (FD_DEVERR_TIMEOUT).
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_error(err, FD_DEVERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
 }
 
 // 2^x by the SFU's ex2 instruction (relative error a few ulp of fp32;
@@ -169,45 +206,43 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((((raw + 1023u) & ~1023u)) - raw);
-  unsigned char* qs = smem + kOffQ;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;                    // producer lane 0 + the TMA bytes of Q
-  uint64_t* k_full = bars + 1;                // [kRing] K tile landed
-  uint64_t* k_empty = k_full + kRing;         // [kRing] MMA commit after q.K^T
-  uint64_t* v_full = k_empty + kRing;         // [kRing] V tile landed
-  uint64_t* v_empty = v_full + kRing;         // [kRing] MMA commit after P.V
-  uint64_t* s_full = v_empty + kRing;         // [2] MMA commit: S ready
-  uint64_t* s_empty = s_full + 2;             // [2] softmax warps read S
-  uint64_t* p_full = s_empty + 2;             // [2] softmax warps wrote P (TMEM)
-  uint64_t* p_free = p_full + 2;              // [2] MMA commit after P.V: P buffer free, O up to date
-  uint64_t* drain = p_free + 2;               // MMA commit before TMEM release
-  static_assert(1 + 4 * kRing + 8 + 1 == kNumBars, "barrier count");
+  uint64_t* q_full = bars;               // producer lane 0 + the TMA bytes of the query tiles
+  uint64_t* k_full = bars + 1;           // [kRingK] K tile landed
+  uint64_t* k_empty = k_full + kRingK;   // [kRingK] MMA commit after the q.K^T products that read it
+  uint64_t* v_full = k_empty + kRingK;   // [kRingV] V tile landed
+  uint64_t* v_empty = v_full + kRingV;   // [kRingV] MMA commit after the P.V products that read it
+  uint64_t* s_full = v_empty + kRingV;   // [2] MMA commit: S of query tile A / B ready
+  uint64_t* p_full = s_full + 2;         // [2] the four softmax warps of the tile wrote P
+  uint64_t* o_full = p_full + 2;         // [2] MMA commit after the tile's last P.V
+  uint64_t* drain = o_full + 2;          // MMA commit before TMEM release
+  static_assert(1 + 2 * kRingK + 2 * kRingV + 6 + 1 == kNumBars, "barrier count");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   volatile int* misc = reinterpret_cast<volatile int*>(smem + kOffMisc);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kh = blockIdx.y;    // kv head; rows of the tile are (query token, head of its group) pairs
+  const int kh = blockIdx.y;    // kv head; rows of a tile are (query token, head of its group) pairs
   const int h0 = kh * p.G;      // first query head of the group
   const int tq = p.tq;          // query tokens per tile (128 / G)
   const int b = blockIdx.x;
 
   // ---------------------------------------------------------------- setup
-  // this CTA's request: the one whose query tiles (ceil(q_len / 128) each,
-  // in request order) contain tile b; a running scan over the requests
+  // this CTA's request: the one whose tile pairs (ceil(ceil(q_len / tq) / 2)
+  // each, in request order) contain pair b; a running scan over the requests
   if (warp == 0) {
     int carry = 0, found = -1, first = 0;
     for (int base = 0; base < p.n && found < 0; base += 32) {
       const int i = base + lane;
       const int ql = i < p.n ? p.q_len[i] : 0;
-      const int c = ql > 0 ? (ql + tq - 1) / tq : 0;
+      const int c = ql > 0 ? ((ql + tq - 1) / tq + 1) / 2 : 0;
       int v = c;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int u = __shfl_up_sync(0xffffffffu, v, off);
         if (lane >= off) v += u;
       }
-      const int lo = carry + v - c;  // first tile of request i
+      const int lo = carry + v - c;  // first pair of request i
       const unsigned hit = __ballot_sync(0xffffffffu, i < p.n && c > 0 && lo <= b && b < lo + c);
       if (hit != 0u) {
         const int w = __ffs(hit) - 1;
@@ -224,17 +259,18 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   if (threadIdx.x == 32) {
     misc[0] = 0;
     mbar_init(q_full, 1);
-    for (int s = 0; s < kRing; ++s) {
+    for (int s = 0; s < kRingK; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kRingV; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], kSoftWarps);  // one arrival per softmax warp
-      mbar_init(&p_full[s], kSoftWarps);
-      mbar_init(&p_free[s], 1);
+      mbar_init(&p_full[s], kSoftWarps / 2);  // one arrival per warp of the tile's warpgroup
+      mbar_init(&o_full[s], 1);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -242,7 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
   __syncthreads();
   const int r = misc[1];
   if (r < 0) return;  // spare CTA of the grid's upper bound (before any TMEM is held)
-  const int q0 = (b - misc[2]) * tq;
   const int qlen = p.q_len[r];
   const int klen = p.k_len[r];
   const int qst = p.q_start[r];
@@ -251,14 +286,16 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     if (threadIdx.x == 0) set_error(p.err, FD_DEVERR_LEN);
     return;
   }
-  const int i_last = min(q0 + tq, qlen) - 1;         // last query of this tile
-  const int nkv = (klen - qlen + i_last) / kKT + 1;  // key tiles the causal mask leaves
+  // pair kk of the request holds tiles tB and tA = tB - 1, the last two
+  // tiles first (the longest causal rows start first); tA = -1: the
+  // request's first tile alone (odd tile count)
+  const int kk = b - misc[2];
+  const int tB = (qlen + tq - 1) / tq - 1 - 2 * kk;
+  const int tA = tB - 1;
+  const int q0B = tB * tq, q0A = tA * tq;
+  const int nkvB = (klen - qlen + min(q0B + tq, qlen) - 1) / kKT + 1;  // key tiles the causal mask leaves
+  const int nkvA = tA >= 0 ? (klen - qlen + q0A + tq - 1) / kKT + 1 : 0;  // <= nkvB (tile A is never last)
 
-  // K and V rings start as zeros: boxes not loaded (keys past k_len) hold
-  // finite values, which P = 0 cancels
-  for (int o = threadIdx.x * 16; o < 2 * kRing * kTile; o += kThreads * 16)
-    sts128(smem + kOffK + o, make_uint4(0u, 0u, 0u, 0u));
-  fence_proxy_async_smem();
   if (warp == kWarpMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
@@ -272,90 +309,110 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
 
   if (warp == kWarpK || warp == kWarpV) {
     // ------------------------------------------------------------ producers
-    // warp 8: Q, then K tiles (a K slot is free once its q.K^T completed);
-    // warp 10: V tiles (a V slot is free once its P.V completed)
+    // warp 8: both query tiles, then the K tiles (a K slot is free once the
+    // q.K^T products of its tile completed); warp 10: the V tiles (a V slot
+    // is free once the P.V products of its tile completed)
     const bool is_k = warp == kWarpK;
     if (is_k && lane == 0) {
-      mbar_expect_tx(q_full, (uint32_t)kTile);
+      mbar_expect_tx(q_full, (uint32_t)((tA >= 0 ? 2 : 1) * kTile));
       // box {64 dims, G heads, 128 / G tokens}: row r = token (r / G), head h0 + r % G
-      tma_load_4d(qs, &p.tmap_q, 0, h0, qst + q0, 0, q_full, 0ull);
-      tma_load_4d(qs + kPanel, &p.tmap_q, 64, h0, qst + q0, 0, q_full, 0ull);
+      if (tA >= 0) {
+        tma_load_4d(smem + kOffQ, &p.tmap_q, 0, h0, qst + q0A, 0, q_full, 0ull);
+        tma_load_4d(smem + kOffQ + kPanel, &p.tmap_q, 64, h0, qst + q0A, 0, q_full, 0ull);
+      }
+      tma_load_4d(smem + kOffQ + kTile, &p.tmap_q, 0, h0, qst + q0B, 0, q_full, 0ull);
+      tma_load_4d(smem + kOffQ + kTile + kPanel, &p.tmap_q, 64, h0, qst + q0B, 0, q_full, 0ull);
       mbar_arrive(q_full);
     }
     const uint64_t pol = l2_evict_first_policy();
+    const int ring_n = is_k ? kRingK : kRingV;
     uint64_t* fullb = is_k ? k_full : v_full;
     uint64_t* emptyb = is_k ? k_empty : v_empty;
     unsigned char* ring = smem + (is_k ? kOffK : kOffV);
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j % kRing;
-      if (j >= kRing && !mbar_wait(&emptyb[st], (uint32_t)((j / kRing) - 1) & 1u, p.err)) {
+    int issued = 0;
+    for (int j = 0; j < nkvB; ++j) {
+      const int st = j % ring_n;
+      const bool free_slot = j < ring_n || wait_or_abort(&emptyb[st], (uint32_t)((j / ring_n) - 1) & 1u, misc, p.err);
+      if (!__all_sync(0xffffffffu, free_slot)) {
         misc[0] = 1;
         break;
       }
-      if (misc[0]) break;
+      if (__any_sync(0xffffffffu, misc[0] != 0)) break;
       load_kv_tile(p, is_k ? &p.tmap_k : &p.tmap_v, ring + st * kTile, &fullb[st], j, klen, qst, trow, kh, lane,
-                   pol);
+                   pol, !is_k);
+      issued = j + 1;
+    }
+    // no copy of this warp is in flight when the CTA ends: wait (bounded)
+    // for the last tile issued into each slot (at once on the normal path,
+    // where the MMA issuer waited for every tile)
+    for (int st = 0; st < ring_n && st < issued; ++st) {
+      const int jl = st + ring_n * ((issued - 1 - st) / ring_n);
+      mbar_wait(&fullb[st], (uint32_t)(jl / ring_n) & 1u, p.err);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    // One thread polls both products and issues whichever is ready: q.K^T of
-    // tile kq once K landed and its S buffer is free (at most two ahead),
-    // P.V of tile kp once P and V are in shared memory.
+    // One thread, in a fixed order that lets one tile's softmax run while the
+    // tensor cores work for the other tile:
+    //   q.K^T of tile 0 for A and B; then for each key tile j:
+    //   P.V(A, j), q.K^T(A, j + 1), P.V(B, j), q.K^T(B, j + 1).
+    // P of a query tile lives in the first 64 columns of its S buffer: the
+    // next q.K^T into that buffer is issued after the P.V that reads it
+    // (tcgen05.mma operations of one thread execute in order), and the
+    // commit of an S also tells its softmax that O holds every earlier tile.
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0u, p.err);
-      const uint32_t sq = smem_u32(qs);
-      int kq = 0, kp = 0;
-      uint32_t spins = 0;
-      uint64_t t_idle = 0;
-      while (ok && kp < nkv) {
-        bool prog = false;
-        if (kq < nkv && kq < kp + 2) {
-          const int sb = kq & 1, kslot = kq % kRing;
-          if (mbar_test_wait(&k_full[kslot], (uint32_t)(kq / kRing) & 1u) &&
-              (kq < 2 || mbar_test_wait(&s_empty[sb], (uint32_t)((kq >> 1) - 1) & 1u))) {
-            tc_fence_after();
-            const uint32_t sk = smem_u32(smem + kOffK + kslot * kTile);
+      const uint32_t sq0 = smem_u32(smem + kOffQ);
+      auto qk = [&](int x, int j) {  // S_x = Q_x . K(j)^T, K-major A and B
+        const uint32_t sq = sq0 + x * kTile;
+        const uint32_t sk = smem_u32(smem + kOffK + (j % kRingK) * kTile);
 #pragma unroll
-            for (int ks = 0; ks < kD / 16; ++ks) {
-              const uint32_t off = (ks >> 2) * kPanel + (ks & 3) * 32;
-              umma_f16(tmem + sb * kKT, sw128_desc(sq + off, 16, 1024), sw128_desc(sk + off, 16, 1024), kIdQK,
-                       ks > 0 ? 1u : 0u);
-            }
-            umma_commit(&s_full[sb]);
-            umma_commit(&k_empty[kslot]);
-            ++kq;
-            prog = true;
-          }
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * kPanel + (ks & 3) * 32;
+          umma_f16(tmem + x * kKT, sw128_desc(sq + off, 16, 1024), sw128_desc(sk + off, 16, 1024), kIdQK,
+                   ks > 0 ? 1u : 0u);
         }
-        if (kp < kq) {
-          const int pb = kp & 1, vslot = kp % kRing;
-          if (mbar_test_wait(&p_full[pb], (uint32_t)(kp >> 1) & 1u) &&
-              mbar_test_wait(&v_full[vslot], (uint32_t)(kp / kRing) & 1u)) {
-            tc_fence_after();
-            const uint32_t sv = smem_u32(smem + kOffV + vslot * kTile);
+        umma_commit(&s_full[x]);
+      };
+      auto pv = [&](int x, int j) {  // O_x += P_x . V(j), P from TMEM: 16 keys = 8 packed columns per step
+        const uint32_t sv = smem_u32(smem + kOffV + (j % kRingV) * kTile);
 #pragma unroll
-            for (int ks = 0; ks < kKT / 16; ++ks)  // A = P from TMEM: 16 keys = 8 packed columns per step
-              umma_f16_ts(tmem + 2 * kKT, tmem + kTmemP + 64 * pb + 8 * ks, sw128_desc(sv + ks * 2048, kPanel, 1024),
-                          kIdPV, (kp > 0 || ks > 0) ? 1u : 0u);  // O accumulates over the tiles
-            umma_commit(&p_free[pb]);
-            umma_commit(&v_empty[vslot]);
-            ++kp;
-            prog = true;
-          }
-        }
-        if (prog) {
-          spins = 0;
-          t_idle = 0;
-        } else if ((++spins & 255u) == 0u) {
-          if (misc[0]) ok = false;
-          const uint64_t now = globaltimer_ns();
-          if (t_idle == 0) {
-            t_idle = now;
-          } else if (now - t_idle > kWaitLimitNs) {
-            set_error(p.err, FD_DEVERR_TIMEOUT);
+        for (int ks = 0; ks < kKT / 16; ++ks)
+          umma_f16_ts(tmem + 2 * kKT + x * kD, tmem + x * kKT + 8 * ks, sw128_desc(sv + ks * 2048, kPanel, 1024),
+                      kIdPV, (j > 0 || ks > 0) ? 1u : 0u);
+      };
+      bool ok = wait_or_abort(q_full, 0u, misc, p.err) && wait_or_abort(&k_full[0], 0u, misc, p.err);
+      if (ok) {
+        tc_fence_after();
+        if (nkvA > 0) qk(0, 0);
+        qk(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < nkvB; ++j) {
+        for (int x = 0; x < 2; ++x) {
+          const int nk = x ? nkvB : nkvA;
+          if (j >= nk) continue;
+          // the first of the tile's users waits for V(j) (A, when it still runs)
+          if (!wait_or_abort(&p_full[x], (uint32_t)j & 1u, misc, p.err) ||
+              ((x == 0 || j >= nkvA) &&
+               !wait_or_abort(&v_full[j % kRingV], (uint32_t)(j / kRingV) & 1u, misc, p.err))) {
             ok = false;
+            break;
+          }
+          tc_fence_after();
+          pv(x, j);
+          if (j == nk - 1) umma_commit(&o_full[x]);
+          if (j + 1 < nk) {
+            const int t = j + 1;
+            if ((x == 0 || t >= nkvA) &&
+                !wait_or_abort(&k_full[t % kRingK], (uint32_t)(t / kRingK) & 1u, misc, p.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            qk(x, t);
+            if (x == 1) umma_commit(&k_empty[t % kRingK]);  // B reads every K tile last
           }
         }
+        if (ok) umma_commit(&v_empty[j % kRingV]);
       }
       if (!ok) misc[0] = 1;
       // all MMAs issued by this thread complete before TMEM is released
@@ -365,15 +422,16 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax warps 0-7
-    // Warp w owns query rows 32 (w % 4) .. + 31 (TMEM lanes) and keys
-    // 64 (w / 4) .. + 63 of every tile (its half); the two warps of a row
-    // exchange their half-row maxima through shared memory once per tile.
+    // Warpgroup x (warps 4x .. 4x + 3) owns query tile x (0: A, 1: B); warp
+    // w of it owns rows 32 (w % 4) .. + 31 (TMEM lanes), one row per thread
+    // with all 128 keys of each key tile, so no row statistics cross warps.
     // O accumulates in TMEM across the tiles (P.V with accumulate); P of a
     // tile is 2^(s - m) for the row's running reference m, which moves only
     // when the tile's maximum exceeds it by more than 2^8 (then the row's O
-    // in TMEM, each half its 64 dims, and the sums l are rescaled once), so
-    // values of P stay <= 256.
-    const int half = warp >> 2;
+    // in TMEM and the sum l are rescaled once), so values of P stay <= 256.
+    const int x = warp >> 2;
+    const int nkv = x ? nkvB : nkvA;
+    const int q0 = x ? q0B : q0A;
     const int row = (warp & 3) * 32 + lane;                  // row of the tile = TMEM lane
     const int qi = q0 + row / p.G;                            // its query index within the request
     const int h = h0 + row % p.G;                             // and its query head
@@ -381,138 +439,109 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     const int lim = row_ok ? klen - qlen + qi : -1;          // last key this query sees
     const int lim_all = klen - qlen + q0;                     // keys every query of the tile sees
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_o = tmem + lane_base + 2 * kKT + 64 * half;  // this half's 64 dims of O
-    float* red = reinterpret_cast<float*>(smem + kOffRed);   // [2 halves][128 rows]
-    float m = -INFINITY, l = 0.f;  // m: log2-domain reference of the row; l: this half's sum
-    // Every softmax warp runs all nkv iterations and passes both named
-    // barriers of each (a warp that failed a wait, or saw another role
-    // abort, only skips its work and its waits), so no barrier is ever left
-    // waiting for a warp that has gone.
+    const uint32_t t_s = tmem + lane_base + x * kKT;          // S of the tile, then P in columns 0 .. 63
+    const uint32_t t_o = tmem + lane_base + 2 * kKT + x * kD; // O of the tile
+    float m = -INFINITY, l = 0.f;  // m: log2-domain reference of the row; l: its sum
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (ok && __any_sync(0xffffffffu, misc[0] != 0)) ok = false;  // warp-uniform (TMEM access is warp-wide)
-      const int sb = j & 1;
-      if (ok && !__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, p.err))) ok = false;
-      uint32_t sr[2][32];  // this half of the S row: two loads, one wait
-      float mx = -INFINITY;  // raw score maximum (scale > 0)
-      const int kbase = j * kKT + 64 * half;
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) tmem_ld32_nowait(tmem + lane_base + sb * kKT + 64 * half + 32 * c, sr[c]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[sb]);  // S buffer free for the tile after next
-      }
-      const bool full_tile = j * kKT + kKT - 1 <= lim_all;  // below the diagonal for every row: no mask
-      if (ok) {
-        // eight independent partial maxima (short dependency chains)
-        float m8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
-        if (full_tile) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(sr[c][e]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float x = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
-              sr[c][e] = __float_as_uint(x);
-              m8[e & 7] = fmaxf(m8[e & 7], x);
-            }
-        }
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      }
-      // the row's maximum over both halves (two barriers: values written,
-      // then read, before the next tile overwrites them)
-      red[half * 128 + row] = mx;
-      named_barrier_sync(1, kSoftWarps * 32);
-      mx = fmaxf(mx, red[(1 - half) * 128 + row]);
-      named_barrier_sync(1, kSoftWarps * 32);
-      if (!ok) continue;
-      const float mxs = mx * p.sl2;  // log2 domain
-      // P buffer sb is free once the P.V of tile j - 2 completed
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_free[sb], (uint32_t)((j >> 1) - 1) & 1u, p.err))) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(&s_full[x], (uint32_t)j & 1u, misc, p.err))) {
         ok = false;
-        continue;
+        break;
       }
+      tc_fence_after();
+      uint32_t sr[4][32];  // the S row: four loads, one wait
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + 32 * c, sr[c]);
+      tmem_wait_ld();
+      // eight independent partial maxima (short dependency chains); the
+      // mask is skipped below the causal diagonal of every row
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
+      if (j * kKT + kKT - 1 <= lim_all) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(sr[c][e]));
+      } else {
+        const int kbase = j * kKT;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float v = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
+            sr[c][e] = __float_as_uint(v);
+            m8[e & 7] = fmaxf(m8[e & 7], v);
+          }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      const float mxs = mx * p.sl2;  // log2 domain (scale > 0)
       const bool grow = m != -INFINITY && mxs > m + 8.f;
       if (__any_sync(0xffffffffu, grow)) {
-        // O must hold every tile up to j - 1: wait for the P.V of tile j - 1
-        // (P.V products complete in order)
-        if (!__all_sync(0xffffffffu, mbar_wait(&p_free[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, p.err))) {
-          ok = false;
-          continue;
-        }
-        tc_fence_after();
+        // O holds tiles 0 .. j - 1: their P.V were issued before this S's commit
         const float alpha = grow ? exp2f(m - mxs) : 1.f;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld32_nowait(t_o + 32 * c, o);
+#pragma unroll 1
+        for (int c = 0; c < kD / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16_nowait(t_o + 16 * c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(t_o + 32 * c, o);
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st16(t_o + 16 * c, o);
         }
-        tmem_wait_st();
         l *= alpha;
       }
       if (grow || m == -INFINITY) m = mxs;  // the first keys of the row set the reference
       const float neg_m = m == -INFINITY ? 0.f : -m;
-      // this half's 64 keys as 32 packed columns of P[sb] in TMEM (column c:
-      // keys 2c, 2c + 1 in the low and high halves), the A operand of P.V
+      // P as 64 packed columns (column c: keys 2c, 2c + 1 in the low and high
+      // halves) over columns 0 .. 63 of the S buffer: the A operand of P.V
       float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
-      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        // 2^(s * scale * log2 e - m) by the hardware ex2 (2^-inf = 0 for masked keys)
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 4][(2 * c) & 31]), p.sl2, neg_m));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c >> 4][(2 * c + 1) & 31]), p.sl2, neg_m));
-        float r0, r1;
-        pk[c] = pack2<T>(p0, p1, r0, r1);  // rounded to T; r0, r1: the values P.V multiplies
-        ls[c & 3] += r0 + r1;
+      for (int q = 0; q < 4; ++q) {  // keys 32 q .. 32 q + 31: packed columns 16 q .. 16 q + 15
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          // 2^(s * scale * log2 e - m) by the hardware ex2 (2^-inf = 0 for masked keys)
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[q][2 * c]), p.sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[q][2 * c + 1]), p.sl2, neg_m));
+          float r0, r1;
+          pk[c] = pack2<T>(p0, p1, r0, r1);  // rounded to T; r0, r1: the values P.V multiplies
+          ls[c & 3] += r0 + r1;
+        }
+        tmem_st16(t_s + 16 * q, pk);
       }
-      tmem_st32(tmem + lane_base + kTmemP + 64 * sb + 32 * half, pk);
       tmem_wait_st();
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tc_fence_before();  // TMEM stores of P (and of a rescaled O) before the MMA reads them
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
+      if (lane == 0) mbar_arrive(&p_full[x]);
     }
     if (ok && nkv > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&p_free[(nkv - 1) & 1], (uint32_t)((nkv - 1) >> 1) & 1u, p.err));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&o_full[x], 0u, misc, p.err));
       tc_fence_after();
     }
-    // the row's sum over both halves (every softmax warp reaches this barrier)
-    red[half * 128 + row] = l;
-    named_barrier_sync(1, kSoftWarps * 32);
-    l += red[(1 - half) * 128 + row];
     if (!ok) {
       misc[0] = 1;
-    } else {
-      uint32_t o[2][32];
+    } else if (nkv > 0) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(qst + qi) * p.out_st + (int64_t)h * p.out_sh;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld32_nowait(t_o + 32 * c, o[c]);
-      tmem_wait_ld();
-      if (row_ok) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(qst + qi) * p.out_st + (int64_t)h * p.out_sh + 64 * half;
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32_nowait(t_o + 32 * c, o);
+        tmem_wait_ld();
+        if (row_ok) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t w[4];
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float a0 = __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * k]) * inv;
-            const float a1 = __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * k + 1]) * inv;
-            w[k] = bits16(Dt<T>::narrow(a0)) | (bits16(Dt<T>::narrow(a1)) << 16);
+            for (int k = 0; k < 4; ++k) {
+              float r0, r1;
+              w[k] = pack2<T>(__uint_as_float(o[8 * q + 2 * k]) * inv, __uint_as_float(o[8 * q + 2 * k + 1]) * inv,
+                              r0, r1);
+            }
+            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          *reinterpret_cast<uint4*>(orow + 8 * c) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }
@@ -604,9 +633,10 @@ extern "C" int fd_prefill_attn(const fd_prefill_args* a, void* stream) {
   p.dtype = a->dtype;
   p.err = a->error;
 
-  // grid: an upper bound of the query tiles (sum of ceil(q_len / tq) <=
-  // ceil(total_q / tq) + n) by kv heads; spare CTAs return at once
-  const int64_t tiles = ((int64_t)a->total_q + tq - 1) / tq + a->n;
+  // grid: an upper bound of the tile pairs (a request's ceil(ceil(q_len /
+  // tq) / 2) <= q_len / (2 tq) + 1, summed) by kv heads; spare CTAs return
+  // at once
+  const int64_t tiles = ((int64_t)a->total_q + 2 * tq - 1) / (2 * tq) + a->n;
   if (tiles > 0x7fffffff) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: too many query tiles");
   const void* kern = a->dtype == FD_DTYPE_BF16 ? reinterpret_cast<const void*>(fdk::pf::fd_prefill_kernel<__nv_bfloat16>)
                                                : reinterpret_cast<const void*>(fdk::pf::fd_prefill_kernel<__half>);
