@@ -200,6 +200,12 @@ __device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
   return d;
 }
 
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+  f2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
   f2_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));

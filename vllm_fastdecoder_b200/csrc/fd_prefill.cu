@@ -33,7 +33,8 @@
 //            at the end o = O / l.
 //   TMEM: S/P of A [0,128), S/P of B [128,256), O of A [256,384), O of B [384,512).
 // Numerics: scores fp32 from the exact 16-bit q and K, P rounded to the
-// input type for P.V (as FlashAttention does), accumulation fp32.  Every
+// input type for P.V and its row sum over the fp32 values (as FlashAttention
+// does), accumulation fp32.  Every
 // mbarrier wait is bounded (FD_DEVERR_TIMEOUT); TMEM is released on every
 // path.
 
@@ -177,24 +178,24 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// Two floats rounded to T and packed (lo, hi) in one conversion; r0, r1 the
-// rounded values as floats.
+// max(a, b, c) in one instruction (the three-input form of sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two floats rounded to T and packed (lo, hi) in one conversion.
 template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b, float& r0, float& r1);
+__device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
-__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b, float& r0, float& r1) {
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-  const uint32_t u = *reinterpret_cast<const uint32_t*>(&v);
-  r0 = __uint_as_float(u << 16);
-  r1 = __uint_as_float(u & 0xffff0000u);
-  return u;
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 template <>
-__device__ __forceinline__ uint32_t pack2<__half>(float a, float b, float& r0, float& r1) {
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   const __half2 v = __floats2half2_rn(a, b);
-  const float2 f = __half22float2(v);
-  r0 = f.x;
-  r1 = f.y;
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
@@ -453,28 +454,24 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + 32 * c, sr[c]);
       tmem_wait_ld();
-      // eight independent partial maxima (short dependency chains); the
-      // mask is skipped below the causal diagonal of every row
-      float m8[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
-      if (j * kKT + kKT - 1 <= lim_all) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(sr[c][e]));
-      } else {
-        const int kbase = j * kKT;
+      // the causal mask (skipped below the diagonal of every row), then the
+      // row maximum
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (j * kKT + kKT - 1 > lim_all) {
+        const int nv = lim - j * kKT + 1;  // keys of the tile this row sees (may be <= 0 or >= 128)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float v = (kbase + 32 * c + e <= lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
-            sr[c][e] = __float_as_uint(v);
-            m8[e & 7] = fmaxf(m8[e & 7], v);
-          }
+          for (int e = 0; e < 32; ++e)
+            if (32 * c + e >= nv) sr[c][e] = __float_as_uint(-INFINITY);
       }
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      // four independent chains of three-input maxima (two scores each)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const float mxs = mx * p.sl2;  // log2 domain (scale > 0)
       const bool grow = m != -INFINITY && mxs > m + 8.f;
       if (__any_sync(0xffffffffu, grow)) {
@@ -495,23 +492,32 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       const float neg_m = m == -INFINITY ? 0.f : -m;
       // P as 64 packed columns (column c: keys 2c, 2c + 1 in the low and high
       // halves) over columns 0 .. 63 of the S buffer: the A operand of P.V
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
+      // the row sum l adds the fp32 values of P, as FlashAttention's does;
+      // P.V multiplies them rounded to T
+      const f2_t sl2x2 = f2_pack(p.sl2, p.sl2), nm2 = f2_pack(neg_m, neg_m);
+      f2_t ls[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};  // packed partial sums
 #pragma unroll
       for (int q = 0; q < 4; ++q) {  // keys 32 q .. 32 q + 31: packed columns 16 q .. 16 q + 15
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           // 2^(s * scale * log2 e - m) by the hardware ex2 (2^-inf = 0 for masked keys)
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[q][2 * c]), p.sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[q][2 * c + 1]), p.sl2, neg_m));
-          float r0, r1;
-          pk[c] = pack2<T>(p0, p1, r0, r1);  // rounded to T; r0, r1: the values P.V multiplies
-          ls[c & 3] += r0 + r1;
+          float a0, a1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[q][2 * c]), __uint_as_float(sr[q][2 * c + 1])), sl2x2, nm2), a0,
+                    a1);
+          const float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+          pk[c] = pack2<T>(p0, p1);
+          ls[c & 1] = f2_add(ls[c & 1], f2_pack(p0, p1));
         }
         tmem_st16(t_s + 16 * q, pk);
       }
       tmem_wait_st();
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(ls[0], a0, a1);
+        f2_unpack(ls[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
       tc_fence_before();  // TMEM stores of P (and of a rescaled O) before the MMA reads them
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[x]);
@@ -536,9 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
             uint32_t w[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              float r0, r1;
-              w[k] = pack2<T>(__uint_as_float(o[8 * q + 2 * k]) * inv, __uint_as_float(o[8 * q + 2 * k + 1]) * inv,
-                              r0, r1);
+              w[k] = pack2<T>(__uint_as_float(o[8 * q + 2 * k]) * inv, __uint_as_float(o[8 * q + 2 * k + 1]) * inv);
             }
             *reinterpret_cast<uint4*>(orow + 32 * c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
           }
