@@ -511,7 +511,12 @@ FD_API size_t fd_prefill_args_bytes(void);
  * block < tier_split -> tier[0], else tier[1] at block - tier_split.
  * slot < 0 is skipped (reshape_and_cache_flash convention).  If any slot is
  * outside both tiers nothing is written and the error word gets
- * FD_DEVERR_SLOT.  Bit-exact copy.
+ * FD_DEVERR_SLOT.  Bit-exact copy.  Up to 2048 rows: one launch.  More: two
+ * launches (a check, then the copy as its programmatic dependent); the
+ * check's verdict lives in one of 1024 device flags, taken per call in turn,
+ * so two such calls share a flag only if they are 1024 calls apart (a CUDA
+ * graph holding the call reuses its flag on every replay: replay it on one
+ * stream at a time).
  * Replaces vLLM reshape_and_cache_flash (fastdecode/backend.py:269-273) plus
  * the D2H staging and store_kv (backend.py:279-285,344-346;
  * fastdecode/csrc/cpu_attn.cpp:413-431,492-517).

@@ -106,6 +106,81 @@ def test_store_kv_out_of_range_writes_nothing(ops):
     assert not kc.any() and not vc.any()
 
 
+def _large_case(g, m):
+    """A prefill-sized write (more than 2048 rows: the check kernel, then the
+    copy as its dependent launch), rows spread over both tiers."""
+    G, C, KVH, BS, D = 1200, 400, 2, 16, 64
+    _, tiers = _tiers(G, C, KVH, BS, D, torch.float16, g)
+    slots = torch.randperm((G + C) * BS, generator=g)[:m].to(torch.int64)
+    slots[::101] = -1
+    k = torch.randn(m, KVH, D, generator=g).to(torch.float16)
+    v = torch.randn(m, KVH, D, generator=g).to(torch.float16)
+    return G, tiers, slots, k, v
+
+
+def test_store_kv_two_launch_form_bit_exact(ops):
+    """m = 20000 rows: twenty check CTAs (1024 slots each) folded into one
+    flag, then the full-grid copy; repeated calls reuse the flag ring."""
+    from oracle import oracle as O
+
+    g = torch.Generator().manual_seed(21)
+    dev = torch.device("cuda")
+    ops.error_word(dev).zero_()
+    G, tiers, slots, k, v = _large_case(g, 20000)
+    want_k, want_v = _unified(tiers)
+    keep = slots >= 0
+    O.store_kv(k[keep].contiguous(), v[keep].contiguous(), slots[keep].contiguous(), want_k, want_v)
+    dk, dv, ds = k.to(dev), v.to(dev), slots.to(dev)
+    for _ in range(3):
+        ops.store_kv_tiered(dk, dv, ds, tiers, G)
+    torch.cuda.synchronize()
+    ops.check_device_errors(dev)
+    got_k, got_v = _unified(tiers)
+    assert torch.equal(got_k.view(torch.uint8), want_k.view(torch.uint8))
+    assert torch.equal(got_v.view(torch.uint8), want_v.view(torch.uint8))
+
+
+def test_store_kv_two_launch_form_out_of_range_writes_nothing(ops):
+    """One bad slot in the seventeenth check CTA's range: no row of the call is
+    written and the error word says so; a good call afterwards (the flags
+    reset by the last check CTA) writes everything, also from a CUDA graph."""
+    from oracle import oracle as O
+
+    g = torch.Generator().manual_seed(22)
+    dev = torch.device("cuda")
+    ops.error_word(dev).zero_()
+    G, tiers, slots, k, v = _large_case(g, 20000)
+    before_k, before_v = _unified(tiers)
+    bad = slots.clone()
+    bad[17000] = (G + 400) * 16  # one past the last slot of the host tier
+    dk, dv = k.to(dev), v.to(dev)
+    for _ in range(2):
+        ops.store_kv_tiered(dk, dv, bad.to(dev), tiers, G)
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError):
+            ops.check_device_errors(dev)
+        ops.error_word(dev).zero_()
+        after_k, after_v = _unified(tiers)
+        assert torch.equal(after_k.view(torch.uint8), before_k.view(torch.uint8))
+        assert torch.equal(after_v.view(torch.uint8), before_v.view(torch.uint8))
+    want_k, want_v = _unified(tiers)
+    keep = slots >= 0
+    O.store_kv(k[keep].contiguous(), v[keep].contiguous(), slots[keep].contiguous(), want_k, want_v)
+    ds = slots.to(dev)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+        ops.store_kv_tiered(dk, dv, ds, tiers, G)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    ops.check_device_errors(dev)
+    got_k, got_v = _unified(tiers)
+    assert torch.equal(got_k.view(torch.uint8), want_k.view(torch.uint8))
+    assert torch.equal(got_v.view(torch.uint8), want_v.view(torch.uint8))
+
+
 def _lse(H, n, g, empty_frac=0.15):
     lse = torch.randn(H, n, generator=g) * 3
     r = torch.rand(H, n, generator=g)

@@ -4,17 +4,27 @@
 // Addressing follows the reference store_kv (fastdecode/csrc/cpu_attn.cpp
 // :413-431): blk = slot / BS, off = slot % BS, destination
 // blk*blk_stride + head*head_stride + off*tok_stride.  Range checking follows
-// :506-510, except that it runs on the device: every CTA scans all slots
-// first and, if any is outside both tiers, nothing is written and the error
-// word gets FD_DEVERR_SLOT.  slot < 0 means "not this call's" and is skipped,
+// :506-510, except that it runs on the device: all slots are checked before
+// any row is written and, if any is outside both tiers, nothing is written
+// and the error word gets FD_DEVERR_SLOT.  slot < 0 means "not this call's" and is skipped,
 // like reshape_and_cache_flash.
 //
-// The all-or-nothing check makes every CTA read all m slots, so the grid is
-// kept to at most two CTAs of 512 threads per SM (a prefill-sized m = 16k
-// reads ~40 MB of slots from L2 in all, not the ~150 MB of one CTA per 256
-// chunks), the scan reads two slots per 16-byte load, and the copy keeps two
-// 16-byte loads of K and V in flight per thread so the few CTAs still stream
-// at HBM rate.
+// The all-or-nothing check takes one of two forms.  Up to kSmallM rows (a
+// decode step's writes) one kernel does it all: every CTA scans all m slots
+// (two per 16-byte load) before it copies, on a grid of at most two CTAs of
+// 512 threads per SM.  Above kSmallM (prefill-sized writes, where every CTA
+// scanning every slot would cost a fifth of the copy) a check kernel scans
+// the slots once (1024 per CTA, one load per thread; the last CTA to finish
+// folds the CTAs' results into one flag of this call; itself a programmatic
+// dependent of the kernel ahead, whose completion it awaits before reading
+// the slots) and the copy kernel, launched as its
+// programmatic dependent on a grid that covers all chunks, issues its first
+// loads, waits for the check (griddepcontrol.wait), and writes only if the
+// flag is clear.  A call's flag is a slot of a ring of kFlagRing, chosen on
+// the host per call; two calls in flight at once share one only if they are
+// kFlagRing calls apart.
+
+#include <atomic>
 
 #include "fd_common.cuh"
 #include "fd_internal.h"
@@ -33,34 +43,72 @@ struct StoreParams {
   int64_t nblk[2];
   int64_t split;
   int32_t* err;
+  int flag;  // this call's slot of the flag ring (two-kernel form)
 };
 
 constexpr int kStoreThreads = 512;
 constexpr int kStoreUnroll = 2;
+constexpr int kSmallM = 2048;        // rows up to which one kernel checks and copies
+constexpr int kCheckThreads = 512;
+constexpr int kCheckSlots = 2 * kCheckThreads;  // slots per check CTA: one 16-byte load per thread
+constexpr int kFlagRing = 1024;
+__device__ int g_store_bad[kFlagRing];          // per call: 1 = some slot out of range
+__device__ int g_store_acc[kFlagRing];          // OR of the check CTAs' results (reset by the last)
+__device__ unsigned g_store_done[kFlagRing];    // check CTAs finished (reset by the last)
 
-__global__ void __launch_bounds__(kStoreThreads, 2) fd_store_kv_kernel(const __grid_constant__ StoreParams p) {
-  auto out_of_range = [&](int64_t s) -> bool {
-    if (s < 0) return false;
-    int64_t b = s / p.BS;
-    int t = 0;
-    if (b >= p.split) {
-      t = 1;
-      b -= p.split;
-    }
-    return b >= p.nblk[t];
-  };
-  // slots are 8-byte aligned; pairs from a 16-byte boundary, the odd one out alone
-  const int lead = (reinterpret_cast<uintptr_t>(p.slots) & 15u) ? 1 : 0;
+__device__ __forceinline__ bool slot_out_of_range(const StoreParams& p, int64_t s) {
+  if (s < 0) return false;
+  int64_t b = s / p.BS;
+  int t = 0;
+  if (b >= p.split) {
+    t = 1;
+    b -= p.split;
+  }
+  return b >= p.nblk[t];
+}
+
+// Does any of slots [lo, hi) fall outside both tiers?  (The block's threads
+// together; slots are 8-byte aligned: pairs from a 16-byte boundary, the odd
+// ones at either end alone.)
+__device__ __forceinline__ bool scan_slots(const StoreParams& p, int lo, int hi) {
   bool mine = false;
-  if (lead && threadIdx.x == 0 && p.m > 0) mine = out_of_range(p.slots[0]);
-  const int pairs = (p.m - lead) / 2;
-  const longlong2* sp = reinterpret_cast<const longlong2*>(p.slots + lead);
+  if (lo >= hi) return false;
+  const int lead = (reinterpret_cast<uintptr_t>(p.slots + lo) & 15u) ? 1 : 0;
+  if (lead && threadIdx.x == 0) mine = slot_out_of_range(p, p.slots[lo]);
+  const int pairs = (hi - lo - lead) / 2;
+  const longlong2* sp = reinterpret_cast<const longlong2*>(p.slots + lo + lead);
   for (int j = threadIdx.x; j < pairs; j += blockDim.x) {
     const longlong2 v = sp[j];
-    mine |= out_of_range(v.x) | out_of_range(v.y);
+    mine |= slot_out_of_range(p, v.x) | slot_out_of_range(p, v.y);
   }
-  if (threadIdx.x == 0 && lead + 2 * pairs < p.m) mine |= out_of_range(p.slots[p.m - 1]);
-  if (__syncthreads_or(mine ? 1 : 0)) {
+  if (threadIdx.x == 0 && lo + lead + 2 * pairs < hi) mine |= slot_out_of_range(p, p.slots[hi - 1]);
+  return mine;
+}
+
+// The check of the two-kernel form.
+__global__ void __launch_bounds__(kCheckThreads) fd_store_check_kernel(const __grid_constant__ StoreParams p) {
+  griddep_wait();               // the kernel ahead (which may have written the slots) has completed
+  griddep_launch_dependents();  // the copy kernel's CTAs may start loading now
+  const int lo = blockIdx.x * kCheckSlots;
+  const bool bad = __syncthreads_or(scan_slots(p, lo, min(p.m, lo + kCheckSlots)) ? 1 : 0) != 0;
+  if (threadIdx.x == 0) {
+    if (bad) atomicOr(&g_store_acc[p.flag], 1);
+    __threadfence();
+    if (atomicAdd(&g_store_done[p.flag], 1u) == gridDim.x - 1) {  // the last check CTA of this call
+      __threadfence();
+      const int any = atomicExch(&g_store_acc[p.flag], 0);
+      g_store_done[p.flag] = 0u;
+      g_store_bad[p.flag] = any;
+      if (any) set_error(p.err, FD_DEVERR_SLOT);
+    }
+  }
+}
+
+// kChecked = false: the one-kernel form (every CTA scans all slots first);
+// true: the copy of the two-kernel form (the check kernel ahead of it).
+template <bool kChecked, int kUnroll>
+__global__ void __launch_bounds__(kStoreThreads) fd_store_kv_kernel(const __grid_constant__ StoreParams p) {
+  if (!kChecked && __syncthreads_or(scan_slots(p, 0, p.m) ? 1 : 0)) {
     if (blockIdx.x == 0 && threadIdx.x == 0) set_error(p.err, FD_DEVERR_SLOT);
     return;
   }
@@ -68,12 +116,18 @@ __global__ void __launch_bounds__(kStoreThreads, 2) fd_store_kv_kernel(const __g
   const uint32_t per_row = (uint32_t)p.KVH * (uint32_t)p.nch;
   const uint32_t total = (uint32_t)p.m * per_row;
   const uint32_t stride = gridDim.x * blockDim.x;
-  for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < total; base += stride * kStoreUnroll) {
-    uint4 kv[kStoreUnroll], vv[kStoreUnroll];
-    int64_t dst[kStoreUnroll];
-    int tier[kStoreUnroll];
+  bool first = true;
+  for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x;; base += stride * kUnroll) {
+    if (kChecked && first) {
+      // the first loads (below) are issued; then the check's verdict
+    } else if (base >= total) {
+      break;
+    }
+    uint4 kv[kUnroll], vv[kUnroll];
+    int64_t dst[kUnroll];
+    int tier[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kStoreUnroll; ++u) {
+    for (int u = 0; u < kUnroll; ++u) {
       const uint32_t idx = base + u * stride;
       dst[u] = -1;
       tier[u] = 0;
@@ -88,13 +142,19 @@ __global__ void __launch_bounds__(kStoreThreads, 2) fd_store_kv_kernel(const __g
       const int64_t off = s - b * p.BS;
       const int t = b >= p.split ? 1 : 0;
       if (t) b -= p.split;
+      if (b >= p.nblk[t]) continue;  // never written (the check has rejected the call); no address formed
       tier[u] = t;
       dst[u] = b * p.blk_sb[t] + (int64_t)h * p.head_sb[t] + off * p.tok_sb[t] + c * 16;
       kv[u] = *reinterpret_cast<const uint4*>(p.key + j * p.k_sn + h * p.k_sh + c * 16);
       vv[u] = *reinterpret_cast<const uint4*>(p.value + j * p.v_sn + h * p.v_sh + c * 16);
     }
+    if (kChecked && first) {
+      griddep_wait();  // the check kernel has completed and its flag is visible
+      if (*reinterpret_cast<volatile const int*>(&g_store_bad[p.flag]) != 0) return;
+    }
+    first = false;
 #pragma unroll
-    for (int u = 0; u < kStoreUnroll; ++u) {
+    for (int u = 0; u < kUnroll; ++u) {
       if (dst[u] < 0) continue;
       *reinterpret_cast<uint4*>(p.tk[tier[u]] + dst[u]) = kv[u];
       *reinterpret_cast<uint4*>(p.tv[tier[u]] + dst[u]) = vv[u];
@@ -155,11 +215,24 @@ extern "C" int fd_store_kv(const void* key, int64_t key_stride_n, int64_t key_st
     return fdh::fail(FD_ERR_UNSUPPORTED, "fd_store_kv: %lld 16-byte chunks in one call (at most 2^31 - 1)",
                      (long long)total);
   const int threads = fdk::kStoreThreads;
-  int dev = 0, sms = 0;
-  const int st = fdh::device_sms(&dev, &sms);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (m <= fdk::kSmallM) {
+    int dev = 0, sms = 0;
+    const int st = fdh::device_sms(&dev, &sms);
+    if (st != FD_OK) return st;
+    int64_t blocks = (total + (int64_t)threads * fdk::kStoreUnroll - 1) / ((int64_t)threads * fdk::kStoreUnroll);
+    if (blocks > 2 * (int64_t)sms) blocks = 2 * (int64_t)sms;  // every CTA scans all slots: few, wide CTAs
+    fdk::fd_store_kv_kernel<false, fdk::kStoreUnroll><<<(unsigned)blocks, threads, 0, s>>>(p);
+    return fdh::cuda_status(cudaGetLastError(), "fd_store_kv_kernel launch");
+  }
+  static std::atomic<unsigned> next_flag{0};
+  p.flag = (int)(next_flag.fetch_add(1u, std::memory_order_relaxed) % (unsigned)fdk::kFlagRing);
+  const unsigned checks = (unsigned)((m + fdk::kCheckSlots - 1) / fdk::kCheckSlots);
+  int st = fdh::launch_maybe_pdl(reinterpret_cast<const void*>(fdk::fd_store_check_kernel), dim3(checks),
+                                  dim3(fdk::kCheckThreads), 0, s, true, p, "fd_store_check_kernel launch");
   if (st != FD_OK) return st;
-  int64_t blocks = (total + (int64_t)threads * fdk::kStoreUnroll - 1) / ((int64_t)threads * fdk::kStoreUnroll);
-  if (blocks > 2 * (int64_t)sms) blocks = 2 * (int64_t)sms;  // every CTA scans all slots: few, wide CTAs
-  fdk::fd_store_kv_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return fdh::cuda_status(cudaGetLastError(), "fd_store_kv_kernel launch");
+  // every thread two 16-byte chunks of K and V, one per pass
+  const int64_t blocks = (total + (int64_t)threads * 2 - 1) / ((int64_t)threads * 2);
+  return fdh::launch_maybe_pdl(reinterpret_cast<const void*>(fdk::fd_store_kv_kernel<true, 1>), dim3((unsigned)blocks),
+                               dim3(threads), 0, s, true, p, "fd_store_kv_kernel launch");
 }
