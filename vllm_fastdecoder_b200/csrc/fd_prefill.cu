@@ -81,6 +81,7 @@ struct PrefillParams {
   CUtensorMap tmap_q;   // {D, H, T, 1}, box {64, 1, 128, 1}, swizzled
   CUtensorMap tmap_k;   // paged: {D, KVH, BS, blocks}; contiguous: {D, KVH, T, 1}; box {64, 1, 16, 1}
   CUtensorMap tmap_v;
+  CUtensorMap tmap_o;   // out as tmap_q: {D, H, T, 1}, box {64, G, 128 / G, 1}, swizzled
   void* out;
   int64_t out_st, out_sh;  // elements
   const int32_t* bt;       // null: keys are the batch's own rows (q_start + j)
@@ -168,6 +169,45 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
       }
     }
   }
+}
+
+// The same, polling without suspending (the MMA issuer: a waiting thread
+// resumes within a few cycles of the phase completing).
+__device__ __forceinline__ bool poll_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              int32_t* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_error(err, FD_DEVERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Tensor store of a box from shared memory (bulk async group of this thread).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+// Named barrier over `count` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool bar_sync_and(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %2, 0;\n\t"
+      "bar.red.and.pred p, %1, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"((uint32_t)v), "r"(count)
+      : "memory");
+  return r != 0;
 }
 
 // 2^x by the SFU's ex2 instruction (relative error a few ulp of fp32;
@@ -380,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
           umma_f16_ts(tmem + 2 * kKT + x * kD, tmem + x * kKT + 8 * ks, sw128_desc(sv + ks * 2048, kPanel, 1024),
                       kIdPV, (j > 0 || ks > 0) ? 1u : 0u);
       };
-      bool ok = wait_or_abort(q_full, 0u, misc, p.err) && wait_or_abort(&k_full[0], 0u, misc, p.err);
+      bool ok = poll_or_abort(q_full, 0u, misc, p.err) && poll_or_abort(&k_full[0], 0u, misc, p.err);
       if (ok) {
         tc_fence_after();
         if (nkvA > 0) qk(0, 0);
@@ -392,9 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
           const int nk = x ? nkvB : nkvA;
           if (j >= nk) continue;
           // the first of the tile's users waits for V(j) (A, when it still runs)
-          if (!wait_or_abort(&p_full[x], (uint32_t)j & 1u, misc, p.err) ||
+          if (!poll_or_abort(&p_full[x], (uint32_t)j & 1u, misc, p.err) ||
               ((x == 0 || j >= nkvA) &&
-               !wait_or_abort(&v_full[j % kRingV], (uint32_t)(j / kRingV) & 1u, misc, p.err))) {
+               !poll_or_abort(&v_full[j % kRingV], (uint32_t)(j / kRingV) & 1u, misc, p.err))) {
             ok = false;
             break;
           }
@@ -404,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
           if (j + 1 < nk) {
             const int t = j + 1;
             if ((x == 0 || t >= nkvA) &&
-                !wait_or_abort(&k_full[t % kRingK], (uint32_t)(t / kRingK) & 1u, misc, p.err)) {
+                !poll_or_abort(&k_full[t % kRingK], (uint32_t)(t / kRingK) & 1u, misc, p.err)) {
               ok = false;
               break;
             }
@@ -435,7 +475,6 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
     const int q0 = x ? q0B : q0A;
     const int row = (warp & 3) * 32 + lane;                  // row of the tile = TMEM lane
     const int qi = q0 + row / p.G;                            // its query index within the request
-    const int h = h0 + row % p.G;                             // and its query head
     const bool row_ok = qi < qlen;
     const int lim = row_ok ? klen - qlen + qi : -1;          // last key this query sees
     const int lim_all = klen - qlen + q0;                     // keys every query of the tile sees
@@ -526,26 +565,51 @@ __global__ void __launch_bounds__(kThreads, 1) fd_prefill_kernel(const __grid_co
       ok = __all_sync(0xffffffffu, wait_or_abort(&o_full[x], 0u, misc, p.err));
       tc_fence_after();
     }
-    if (!ok) {
-      misc[0] = 1;
-    } else if (nkv > 0) {
+    // o = O / l, staged in the tile's Q buffer (its last q.K^T completed
+    // before this tile's last S) in the layout of the Q box: two 64-dim
+    // panels of 128-byte rows, 128-byte swizzle; then one tensor store of
+    // the tile, or (the request's last tile, whose box would reach into the
+    // next request) plain stores of the rows that belong to the request.
+    // All four warps of the warpgroup reach the barrier on every path.
+    unsigned char* stage = smem + kOffQ + x * kTile;
+    const bool fine = ok && nkv > 0;
+    if (fine) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(qst + qi) * p.out_st + (int64_t)h * p.out_sh;
 #pragma unroll
       for (int c = 0; c < kD / 32; ++c) {
         uint32_t o[32];
         tmem_ld32_nowait(t_o + 32 * c, o);
         tmem_wait_ld();
-        if (row_ok) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t w[4];
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              w[k] = pack2<T>(__uint_as_float(o[8 * q + 2 * k]) * inv, __uint_as_float(o[8 * q + 2 * k + 1]) * inv);
-            }
-            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
+          for (int k = 0; k < 4; ++k)
+            w[k] = pack2<T>(__uint_as_float(o[8 * q + 2 * k]) * inv, __uint_as_float(o[8 * q + 2 * k + 1]) * inv);
+          sts128(stage + (c >> 1) * kPanel + swz(row, (c & 1) * 4 + q), make_uint4(w[0], w[1], w[2], w[3]));
+        }
+      }
+      fence_proxy_async_smem();  // the staged rows before the tensor store reads them
+    }
+    if (!ok) misc[0] = 1;
+    if (bar_sync_and(1 + x, kSoftWarps / 2 * 32, fine)) {
+      if (q0 + tq <= qlen) {
+        if ((warp & 3) == 0 && lane == 0) {
+          tma_store_4d(&p.tmap_o, stage, 0, h0, qst + q0, 0);
+          tma_store_4d(&p.tmap_o, stage + kPanel, 64, h0, qst + q0, 0);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // smem read before the CTA ends
+        }
+      } else {
+        const int ch = lane & 15;
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {  // this warp's rows, two per instruction
+          const int rr = (warp & 3) * 32 + 2 * i + (lane >> 4);
+          const int qr = q0 + rr / p.G;
+          const uint4 v = lds128(stage + (ch >> 3) * kPanel + swz(rr, ch & 7));
+          if (qr < qlen)
+            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + (int64_t)(qst + qr) * p.out_st +
+                                      (int64_t)(h0 + rr % p.G) * p.out_sh + 8 * ch) = v;
         }
       }
     }
@@ -616,7 +680,11 @@ extern "C" int fd_prefill_attn(const fd_prefill_args* a, void* stream) {
     ok = ok && fdk::encode_kv_map(&p.tmap_v, kv.v, a->dtype, (int)D, KVH, (int)T, 1, kv.head_stride * es,
                                   kv.tok_stride * es, kv.tok_stride * es * T, fdk::pf::kSub, true);
   }
-  if (!ok) return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: tensor map encoding rejected the q / K / V views");
+  // out as q: tile stores of full query tiles
+  ok = ok && fdk::encode_kv_map(&p.tmap_o, a->out, a->dtype, (int)D, H, a->num_tokens, 1, a->out_stride_h * es,
+                                a->out_stride_t * es, a->out_stride_t * es * a->num_tokens, tq, true, G);
+  if (!ok)
+    return fdh::fail(FD_ERR_UNSUPPORTED, "fd_prefill_attn: tensor map encoding rejected the q / K / V / out views");
   p.out = a->out;
   p.out_st = a->out_stride_t;
   p.out_sh = a->out_stride_h;
